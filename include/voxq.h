@@ -1,0 +1,225 @@
+/*
+ * voxq.h -- C ABI of libvoxq, the sm_100a (B200) quantized-matmul library that
+ * replaces the voxcpm2-c reference's GPU offload (src/tensor_cuda.cu).
+ *
+ * Two groups of entry points:
+ *
+ *  1. The reference's CUDA block of include/tensor.h (tensor.h:316-342), same
+ *     names, arguments, ownership rules and error codes, so the reference
+ *     engine (src/model.c, src/nn.c, ...) links against libvoxq unchanged.
+ *
+ *  2. Additive voxq_* entry points on plain device pointers: the block
+ *     quantizer of scripts/quantize.py (bit-exact), dequantizers, the packed
+ *     device weight layout, the fused matmul with epilogues, and a grouped
+ *     launch for many independent GEMVs.  The reference has no quantized GPU
+ *     path at all; these are the calls its engine would make for one.
+ *
+ * All sizes are element counts unless named *_bytes.  Functions return
+ * VOXCPM_SUCCESS (0) or a negative VoxCPMError.  `stream` is a cudaStream_t
+ * passed as void* (NULL = the legacy default stream).
+ */
+#ifndef VOXQ_H
+#define VOXQ_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Exported from libvoxq.so (the library builds with hidden visibility). */
+#if defined(__GNUC__)
+#define VOXQ_API __attribute__((visibility("default")))
+#else
+#define VOXQ_API
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Reference ABI types.  Layout- and value-compatible with the reference's   */
+/* include/voxcpm.h:45-58 (VoxCPMError) and include/tensor.h:45-56 (Tensor). */
+/* When the reference headers are already included they are used instead.   */
+/* ------------------------------------------------------------------------ */
+#ifndef TENSOR_H
+#ifndef VOXCPM_H
+typedef enum {
+    VOXCPM_SUCCESS = 0,
+    VOXCPM_ERR_FILE_NOT_FOUND = -1,
+    VOXCPM_ERR_INVALID_MODEL = -2,
+    VOXCPM_ERR_INVALID_TEXT = -3,
+    VOXCPM_ERR_INVALID_AUDIO = -4,
+    VOXCPM_ERR_SHAPE_MISMATCH = -5,
+    VOXCPM_ERR_OOM = -6,
+    VOXCPM_ERR_GPU = -7,
+    VOXCPM_ERR_INTERNAL = -8,
+    VOXCPM_ERR_UNSUPPORTED = -9,
+    VOXCPM_ERR_TIMEOUT = -10,
+    VOXCPM_ERR_CUDA_NOT_FOUND = -11,
+} VoxCPMError;
+#endif
+
+typedef struct {
+    float* data;          /* fp32 data (host or device) */
+    int* shape;           /* [ndim], heap-owned */
+    int ndim;
+    int64_t strides[5];   /* in elements */
+    size_t size;          /* element count */
+    bool is_cuda;
+    bool is_owned;
+    uint16_t* data_fp16;  /* fp16 payload when is_fp16 */
+    bool is_fp16;
+    char name[64];
+} Tensor;
+#endif
+
+/* ======================================================================== */
+/* 1. Drop-in replacements for the reference's tensor.h CUDA block           */
+/* ======================================================================== */
+
+/* src/tensor_cuda.cu:47-82.  Selects the device (voxq_set_device, default 0),
+ * creates the library stream and reads VOXCPM_QUANT (f32 | q8 | q4; default
+ * f32), the format that tensor_to_cuda gives 2-D weights.  Returns
+ * VOXCPM_ERR_CUDA_NOT_FOUND when no device is usable. */
+VOXQ_API VoxCPMError tensor_cuda_init(void);
+
+/* src/tensor_cuda.cu:84-90. */
+VOXQ_API void tensor_cuda_shutdown(void);
+
+/* src/tensor_cuda.cu:96-126.  Moves t to the device and frees the host buffer
+ * (also for non-owned tensors, as the reference does).  Under VOXCPM_QUANT=q8
+ * or q4 a 2-D tensor with shape[1] % 32 == 0 is quantized on the device,
+ * bit-exactly as scripts/quantize.py:42-75 would, and kept only in the packed
+ * device layout; t->data then points at that opaque buffer. */
+VOXQ_API VoxCPMError tensor_to_cuda(Tensor* t);
+
+/* src/tensor_cuda.cu:128-159.  A quantized tensor comes back dequantized. */
+VOXQ_API VoxCPMError tensor_to_cpu(Tensor* t);
+
+/* src/tensor_cuda.cu:161-174. */
+VOXQ_API VoxCPMError tensor_cuda_free(Tensor* t);
+
+/* src/tensor_cuda.cu:192-333: out[M,N] = a[M,K] . b[N,K]^T, fp32 rows.
+ * a and out may live on the host or the device; b is a device weight (fp32,
+ * fp16 or quantized) or a host fp32/fp16 tensor (uploaded for this call).
+ * A host `out` is valid on return; a device `out` is complete in the order of
+ * the library stream (every later voxq call and tensor_to_cpu sees it).
+ * Shape errors -> VOXCPM_ERR_SHAPE_MISMATCH; not initialised ->
+ * VOXCPM_ERR_CUDA_NOT_FOUND (the caller then uses its CPU path). */
+VOXQ_API VoxCPMError tensor_matmul_nt_cuda(const Tensor* a, const Tensor* b, Tensor* out);
+
+/* src/tensor_cuda.cu:352-355 (defined there, not declared in tensor.h). */
+VOXQ_API VoxCPMError tensor_cuda_upload_weight(Tensor** t_ptr);
+
+/* ======================================================================== */
+/* 2. Additive voxq_* entry points                                          */
+/* ======================================================================== */
+
+/* Block formats: the codes of scripts/quantize.py:28 (QUANT_TYPES). */
+enum { VOXQ_F32 = 0, VOXQ_F16 = 1, VOXQ_Q4 = 2, VOXQ_Q8 = 3 };
+#define VOXQ_BLOCK 32
+
+/* Library version string. */
+VOXQ_API const char* voxq_version(void);
+
+/* Selects the CUDA device for the calling thread's later calls (multi-GPU
+ * runners use one host thread or process per GPU).  No counterpart in the
+ * reference, which hard-codes device 0 (src/tensor_cuda.cu:50). */
+VOXQ_API VoxCPMError voxq_set_device(int device);
+
+/* Bytes of the quantize.py block stream for n elements: ceil(n/32) blocks of
+ * 20 (Q4) or 40 (Q8) bytes (scripts/quantize.py:88-104 without its 20-byte
+ * tensor header). */
+VOXQ_API size_t voxq_quant_bytes(size_t n, int qtype);
+
+/* Quantizes n fp32 values (flattened, last block zero-padded,
+ * scripts/quantize.py:239-260) into the quantize.py block stream, bit-exact
+ * with quantize_q4_block / quantize_q8_block (scripts/quantize.py:42-75).
+ * voxq_quantize runs on the device (d_src, d_dst device pointers). */
+VOXQ_API VoxCPMError voxq_quantize(const float* d_src, size_t n, int qtype, uint8_t* d_dst, void* stream);
+
+/* Inverse of the above, bit-exact with dequantize_q4_block /
+ * dequantize_q8_block (scripts/quantize.py:56-82).  q8_signed = 1 reads Q8
+ * codes as int8 like scripts/quantize.py:79; q8_signed = 0 reads them as the
+ * unsigned codes the quantizer wrote (the default everywhere else). */
+VOXQ_API VoxCPMError voxq_dequantize(const uint8_t* d_src, size_t n, int qtype, int q8_signed, float* d_dst,
+                            void* stream);
+
+/* ---- Packed device weight layout ----------------------------------------
+ * A weight W[N,K] with K % 32 == 0 is stored as two arrays:
+ *   codes   Q8: uint8 [N][K]     (code of W[n][k] at n*K + k)
+ *           Q4: uint8 [N][K/2]   (byte i of a row = code[2i] << 4 | code[2i+1])
+ *   scales  Q8: float2 [N][K/32] (scale, min)   Q4: half2 [N][K/32] (scale, min)
+ * i.e. each quantize.py block split into its code bytes and its trailer.
+ * Same bytes per weight as the block stream (1.25 / 0.625). */
+typedef struct {
+    const uint8_t* codes;  /* device */
+    const void* scales;    /* device */
+    int32_t N, K;
+    int32_t qtype;         /* VOXQ_Q4 or VOXQ_Q8 */
+    int32_t q8_signed;     /* Q8 codes read as int8 (scripts/quantize.py:79) */
+} voxq_qweight;
+
+VOXQ_API size_t voxq_codes_bytes(int N, int K, int qtype);
+VOXQ_API size_t voxq_scales_bytes(int N, int K, int qtype);
+
+/* Quantizes a device fp32 weight W[N,K] straight into the packed layout and,
+ * when d_blocks is non-NULL, also into the quantize.py block stream. */
+VOXQ_API VoxCPMError voxq_quantize_weight(const float* d_w, int N, int K, int qtype, uint8_t* d_codes,
+                                 void* d_scales, uint8_t* d_blocks, void* stream);
+
+/* Block stream (e.g. read from a quantize.py file) -> packed layout, and back. */
+VOXQ_API VoxCPMError voxq_pack_blocks(const uint8_t* d_blocks, int N, int K, int qtype, uint8_t* d_codes,
+                             void* d_scales, void* stream);
+VOXQ_API VoxCPMError voxq_unpack_blocks(const uint8_t* d_codes, const void* d_scales, int N, int K, int qtype,
+                               uint8_t* d_blocks, void* stream);
+
+/* ---- Matmul -------------------------------------------------------------
+ * out[M,N] = epilogue(A[M,K] . W[N,K]^T), A and out fp32 row-major on the
+ * device (row strides lda / ldo in elements).  Epilogue, applied in order:
+ *   up != NULL  : out = silu(A.W^T) * (A.Up^T)     (src/nn.c:148-169)
+ *   bias != NULL: out += bias[n]                   (src/loc_dit.c:52-66)
+ *   residual    : out += residual[m*ldr + n]       (src/nn.c:655, 685)
+ * residual may alias out.  M <= 8 runs the HBM-streaming GEMV kernel; larger
+ * M runs the tcgen05 tensor-core GEMM (fp16 operands, fp32 accumulation in
+ * tensor memory), which needs a workspace from the library's device arena. */
+typedef struct {
+    const float* bias;         /* [N] or NULL */
+    const float* residual;     /* [M][ldr] or NULL */
+    int64_t ldr;
+    const voxq_qweight* up;    /* SwiGLU up-projection, or NULL */
+} voxq_epilogue;
+
+VOXQ_API VoxCPMError voxq_matmul_nt_q(const float* d_a, int M, int64_t lda, const voxq_qweight* w, float* d_out,
+                             int64_t ldo, const voxq_epilogue* epi, void* stream);
+
+/* Dense fp32 / fp16 weights (the reference's unquantized path,
+ * src/tensor_cuda.cu:192-333), full fp32 arithmetic. */
+VOXQ_API VoxCPMError voxq_matmul_nt_dense(const float* d_a, int M, int64_t lda, const void* d_w, int w_is_fp16,
+                                 int N, int K, float* d_out, int64_t ldo, void* stream);
+
+/* ---- Grouped GEMV ------------------------------------------------------
+ * Runs `count` independent quantized GEMVs (M <= 8 each) in ONE launch that
+ * streams all their weights back to back: the QKV or gate/up group of a
+ * decoder layer, or a whole stack of layers whose inputs are ready.  Each
+ * item is an independent voxq_matmul_nt_q call.  count <= VOXQ_MAX_BATCH. */
+#define VOXQ_MAX_BATCH 192
+typedef struct {
+    voxq_qweight w;
+    const float* a;            /* [M][lda] */
+    float* out;                /* [M][ldo] */
+    const float* bias;         /* or NULL */
+    const float* residual;     /* or NULL */
+    const uint8_t* up_codes;   /* SwiGLU up weight (same N, K, qtype), or NULL */
+    const void* up_scales;
+    int32_t M;
+    int32_t lda, ldo, ldr;
+} voxq_gemv_item;
+
+VOXQ_API VoxCPMError voxq_gemv_batch(const voxq_gemv_item* items, int count, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VOXQ_H */

@@ -1,0 +1,40 @@
+// voxq_internal.h -- declarations shared between the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "voxq.h"
+
+namespace voxq {
+
+// Device facts cached per device.
+int device_sm_count();
+int current_device();
+
+// Programmatic dependent launch on the voxq kernels (VOXQ_PDL=0 disables).
+bool pdl_enabled();
+
+// Grouped / single GEMV (voxq_gemv.cu).
+VoxCPMError validate_item(const voxq_gemv_item& x);
+VoxCPMError gemv_launch(const voxq_gemv_item* items, int count, cudaStream_t st);
+VoxCPMError gemv_k0(const voxq_gemv_item& x, cudaStream_t st);
+
+// Tensor-core GEMM for M > 8 (voxq_gemm.cu).  `ws` is a device workspace of
+// at least gemm_workspace_bytes(M, K) bytes, 256-byte aligned.
+size_t gemm_workspace_bytes(int M, int K);
+VoxCPMError gemm_launch(const float* a, int M, int64_t lda, const voxq_qweight* w, float* out, int64_t ldo,
+                        const voxq_epilogue* epi, void* ws, cudaStream_t st);
+
+// Dense fp32 / fp16 weights (voxq_dense.cu).
+VoxCPMError dense_launch(const float* a, int M, int64_t lda, const void* w, int w_is_fp16, int N, int K,
+                         float* out, int64_t ldo, cudaStream_t st);
+
+// fp16 -> fp32, exact (voxq_dense.cu).
+VoxCPMError widen_fp16(const uint16_t* src, float* dst, size_t n, cudaStream_t st);
+
+// Per-device workspace arena (voxq_runtime.cu): grows on demand, never
+// shrinks, ordered on the stream that uses it.
+void* workspace(size_t bytes);
+
+}  // namespace voxq
