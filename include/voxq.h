@@ -127,6 +127,13 @@ VOXQ_API const char* voxq_version(void);
  * reference, which hard-codes device 0 (src/tensor_cuda.cu:50). */
 VOXQ_API VoxCPMError voxq_set_device(int device);
 
+/* Device-side status of the current device's kernels: 0, or the code of the
+ * first bounded wait that gave up (1 full-stage, 2 empty-stage, 3 MMA
+ * completion, 4 tensor-memory allocation).  A kernel that gives up returns
+ * early instead of hanging; its outputs are then undefined.  clear != 0 resets
+ * the word.  Returns -1 if the word cannot be read. */
+VOXQ_API int voxq_device_error(int clear);
+
 /* Bytes of the quantize.py block stream for n elements: ceil(n/32) blocks of
  * 20 (Q4) or 40 (Q8) bytes (scripts/quantize.py:88-104 without its 20-byte
  * tensor header). */

@@ -84,6 +84,80 @@ __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Shared-memory barriers and bulk copies (sm_90+ PTX, used on sm_100a).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Device-side error word (one int per device, passed to the kernels): a
+// bounded wait that gives up records its site there; voxq_device_error reads
+// and clears it.  Kernels never trap or hang.
+enum : int { VOXQ_DEVERR_NONE = 0, VOXQ_DEVERR_WAIT_FULL = 1, VOXQ_DEVERR_WAIT_EMPTY = 2,
+             VOXQ_DEVERR_WAIT_MMA = 3, VOXQ_DEVERR_WAIT_TMEM = 4 };
+
+// Spins on a barrier phase at most `limit` polls (about a second with the
+// back-off); returns false and records `site` when the phase never completes.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int site, int* err,
+                                                  uint32_t limit = (1u << 24)) {
+    if (mbar_try_wait(bar, parity)) return true;
+    for (uint32_t i = 0; i < limit; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (i > 64) __nanosleep(64);
+    }
+    atomicCAS(err, 0, site);
+    return false;
+}
+
+// Global -> shared bulk copy completing on an mbarrier (16-byte aligned
+// addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst_smem)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+// Same with an L2 evict-first hint for data that is read exactly once.
+__device__ __forceinline__ void bulk_g2s_stream(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar,
+                                                uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_u32(dst_smem)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // binary64 -> binary16, round to nearest even, from the double directly.
 // Integer restatement of IEEE 754 rounding (same rule as the CPU checker).
 __host__ __device__ inline uint16_t double_to_half_rn(double d) {
@@ -124,7 +198,13 @@ __host__ __device__ inline uint16_t double_to_half_rn(double d) {
     return sign | (uint16_t)hm;
 }
 
+// binary16 -> binary32 keeping NaN payloads the way the reference's
+// fp16_to_fp32 (include/tensor.h:350-371) and x86 F16C do: mantissa << 13.
+// (The GPU conversion returns its canonical NaN instead.)  Finite values go
+// through the exact hardware conversion.
 __device__ __forceinline__ float half_bits_to_float(uint16_t h) {
+    if ((h & 0x7c00u) == 0x7c00u)
+        return __uint_as_float(((uint32_t)(h & 0x8000u) << 16) | 0x7f800000u | ((uint32_t)(h & 0x3ffu) << 13));
     return __half2float(__ushort_as_half(h));
 }
 

@@ -33,6 +33,9 @@ VoxCPMError dense_launch(const float* a, int M, int64_t lda, const void* w, int 
 // fp16 -> fp32, exact (voxq_dense.cu).
 VoxCPMError widen_fp16(const uint16_t* src, float* dst, size_t n, cudaStream_t st);
 
+// Per-device device-side error word (allocated on first use, zeroed).
+int* device_error_word();
+
 // Per-device workspace arena (voxq_runtime.cu): grows on demand, never
 // shrinks, ordered on the stream that uses it.
 void* workspace(size_t bytes);

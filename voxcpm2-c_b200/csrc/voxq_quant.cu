@@ -156,6 +156,25 @@ __global__ void quantize_kernel(const float* __restrict__ src, int64_t n, int qt
     }
 }
 
+// NaN encoding of the reference's x86 arithmetic, so NaN results match bit for
+// bit: an operation with a NaN operand returns that operand (quieted); an
+// invalid operation on non-NaN operands (0 * inf, inf - inf) returns the x86
+// default NaN 0xFFC00000.  (The GPU's own default NaN is 0x7FFFFFFF.)
+__device__ __forceinline__ float x86_mul(float a, float b) {
+    float r = __fmul_rn(a, b);
+    if (!isnan(r)) return r;
+    if (isnan(a)) return __uint_as_float(__float_as_uint(a) | 0x00400000u);
+    if (isnan(b)) return __uint_as_float(__float_as_uint(b) | 0x00400000u);
+    return __uint_as_float(0xFFC00000u);
+}
+__device__ __forceinline__ float x86_add(float a, float b) {
+    float r = __fadd_rn(a, b);
+    if (!isnan(r)) return r;
+    if (isnan(a)) return __uint_as_float(__float_as_uint(a) | 0x00400000u);
+    if (isnan(b)) return __uint_as_float(__float_as_uint(b) | 0x00400000u);
+    return __uint_as_float(0xFFC00000u);
+}
+
 // One thread per element.  Q4: f32(code) * f32(half scale), then + f32(half
 // min), each rounded (scripts/quantize.py:67).  Q8: same with f32 trailer.
 __global__ void dequantize_kernel(const uint8_t* __restrict__ src, int64_t n, int qtype, int q8_signed,
@@ -177,7 +196,7 @@ __global__ void dequantize_kernel(const uint8_t* __restrict__ src, int64_t n, in
             s = __uint_as_float(p[32] | (p[33] << 8) | (p[34] << 16) | ((uint32_t)p[35] << 24));
             m = __uint_as_float(p[36] | (p[37] << 8) | (p[38] << 16) | ((uint32_t)p[39] << 24));
         }
-        dst[i] = __fadd_rn(__fmul_rn(code, s), m);
+        dst[i] = x86_add(x86_mul(code, s), m);
     }
 }
 

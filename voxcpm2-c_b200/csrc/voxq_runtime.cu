@@ -33,6 +33,7 @@ struct QRec {
 };
 
 struct DevState {
+    int* err = nullptr;  // device-side error word of the bounded waits
     bool init = false;
     int quant = VOXQ_F32;  // format tensor_to_cuda gives 2-D weights
     int sms = 0;
@@ -97,6 +98,22 @@ static void* slot_get(DevState& s, int k, size_t bytes) {
     return s.slot[k];
 }
 
+int* device_error_word() {
+    int d = 0;
+    cudaGetDevice(&d);
+    if (d < 0 || d >= kMaxDev) return nullptr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevState& s = g_dev[d];
+    if (!s.err) {
+        if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) {
+            s.err = nullptr;
+            return nullptr;
+        }
+        cudaMemset(s.err, 0, sizeof(int));
+    }
+    return s.err;
+}
+
 void* workspace(size_t bytes) {
     int d = 0;
     cudaGetDevice(&d);
@@ -144,6 +161,15 @@ using namespace voxq;
 // ===========================================================================
 
 extern "C" const char* voxq_version(void) { return "voxq-b200 0.1 (sm_100a)"; }
+
+extern "C" int voxq_device_error(int clear) {
+    int* e = device_error_word();
+    if (!e) return -1;
+    int v = 0;
+    if (cudaMemcpy(&v, e, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (clear && v) cudaMemset(e, 0, sizeof(int));
+    return v;
+}
 
 extern "C" VoxCPMError voxq_set_device(int device) {
     if (device < 0 || device >= kMaxDev) return VOXCPM_ERR_CUDA_NOT_FOUND;
