@@ -157,8 +157,10 @@ VOXQ_API VoxCPMError voxq_dequantize(const uint8_t* d_src, size_t n, int qtype, 
  *   codes   Q8: uint8 [N][K]     (code of W[n][k] at n*K + k)
  *           Q4: uint8 [N][K/2]   (byte i of a row = code[2i] << 4 | code[2i+1])
  *   scales  Q8: float2 [N][K/32] (scale, min)   Q4: half2 [N][K/32] (scale, min)
+ *           followed by 16 bytes of padding (the kernels read 16-byte windows)
  * i.e. each quantize.py block split into its code bytes and its trailer.
- * Same bytes per weight as the block stream (1.25 / 0.625). */
+ * Same bytes per weight as the block stream (1.25 / 0.625).  Both arrays must
+ * be 16-byte aligned; allocate them with voxq_codes_bytes / voxq_scales_bytes. */
 typedef struct {
     const uint8_t* codes;  /* device */
     const void* scales;    /* device */

@@ -50,11 +50,13 @@ def test_sizes_and_layout_math():
     L = voxq.lib()
     assert L.voxq_codes_bytes(4096, 1024, voxq.Q8) == 4096 * 1024
     assert L.voxq_codes_bytes(4096, 1024, voxq.Q4) == 4096 * 512
-    assert L.voxq_scales_bytes(4096, 1024, voxq.Q8) == 4096 * 32 * 8
-    assert L.voxq_scales_bytes(4096, 1024, voxq.Q4) == 4096 * 32 * 4
+    # trailers plus 16 bytes of tail padding
+    assert L.voxq_scales_bytes(4096, 1024, voxq.Q8) == 4096 * 32 * 8 + 16
+    assert L.voxq_scales_bytes(4096, 1024, voxq.Q4) == 4096 * 32 * 4 + 16
     # same bytes per weight as the block stream (1.25 / 0.625)
     for qt in (voxq.Q4, voxq.Q8):
-        assert L.voxq_codes_bytes(64, 1024, qt) + L.voxq_scales_bytes(64, 1024, qt) == L.voxq_quant_bytes(64 * 1024, qt)
+        assert (L.voxq_codes_bytes(64, 1024, qt) + L.voxq_scales_bytes(64, 1024, qt) - 16
+                == L.voxq_quant_bytes(64 * 1024, qt))
 
 
 def test_tensor_struct_layout_matches_reference():

@@ -57,6 +57,23 @@ def test_gemv_matches_tensor_c(qt, M, N, K):
     assert_matmul_close(y, y_ref, sc, TOL_GEMV, f"M{M} N{N} K{K} q{qt}")
 
 
+@pytest.mark.parametrize("qt", [voxq.Q8, voxq.Q4], ids=["q8", "q4"])
+@pytest.mark.parametrize("M", [1, 2, 5])
+def test_gemv_outlier_activations(qt, M):
+    """Activations with rare huge entries (heavy tails, one dominant channel):
+    the case where the activation limbs need their third int8 term."""
+    N, K = 256, 1024
+    qw, wdeq = make_weight(N, K, qt, seed=31)
+    rs = np.random.RandomState(32)
+    a = rs.randn(M, K).astype(np.float32)
+    a[rs.rand(M, K) < 0.01] *= 300.0          # sparse outliers
+    a[:, 17] = 5e4                              # one channel dominating every row
+    a[:, 500:532] *= 1e-6                       # a near-silent block
+    y = voxq.matmul_nt_q(torch.from_numpy(a).cuda(), qw).cpu().numpy()
+    y_ref, sc = ref(a, wdeq)
+    assert_matmul_close(y, y_ref, sc, TOL_GEMV, f"outliers M{M} q{qt}")
+
+
 @pytest.mark.parametrize("M", [1, 3, 8])
 def test_gemv_q8_signed_mode(M):
     N, K = 200, 1024

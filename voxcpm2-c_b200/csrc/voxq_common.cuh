@@ -37,6 +37,12 @@ __host__ __device__ inline int64_t codes_row_bytes(int K, int qtype) {
 }
 __host__ __device__ inline int scale_bytes(int qtype) { return qtype == VOXQ_Q4 ? 4 : 8; }
 __host__ __device__ inline int block_bytes(int qtype) { return qtype == VOXQ_Q4 ? 20 : 40; }
+// Trailer (scale, min) array of a packed weight, and the tail padding that the
+// scales buffer carries so 16-byte bulk-copy windows never leave it.
+__host__ __device__ inline size_t trailer_bytes(int N, int K, int qtype) {
+    return (size_t)N * (size_t)(K / VOXQ_QBLK) * (size_t)scale_bytes(qtype);
+}
+#define VOXQ_TRAILER_PAD 16
 
 // ---------------------------------------------------------------------------
 // Device helpers
@@ -128,9 +134,14 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     if (mbar_try_wait(bar, parity)) return true;
     for (uint32_t i = 0; i < limit; i++) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (i > 64) __nanosleep(64);
+        if (i > 64) {
+            // once any wait has given up, later waits return at once so a
+            // failing kernel ends quickly instead of timing out per wait
+            if (i == 65 && site != VOXQ_DEVERR_NONE && *reinterpret_cast<volatile int*>(err) != 0) return false;
+            __nanosleep(64);
+        }
     }
-    atomicCAS(err, 0, site);
+    if (site != VOXQ_DEVERR_NONE) atomicCAS(err, 0, site);
     return false;
 }
 

@@ -1,28 +1,34 @@
 // voxq_gemv.cu -- quantized GEMV (M <= 8 activation rows) for sm_100a.
 //
-// out[m, n] = sum_k A[m, k] * W[n, k] with W in the packed Q4/Q8 layout
-// (voxq.h).  This is the batch-1 decode regime of the reference's
-// tensor_matmul_nt (src/tensor.c:617-678): every weight byte is read once and
-// the kernel is HBM-bound, so it is built around keeping bytes in flight:
+// out[m, n] = sum_k A[m, k] * W[n, k], W in the packed Q4/Q8 layout (voxq.h).
+// This is the batch-1 decode regime of the reference's tensor_matmul_nt
+// (src/tensor.c:617-678): every weight byte is read once, so the kernel is
+// HBM-bound and is built to stream with as few instructions per weight as
+// possible.
 //
-//   * Work = "tasks" of RG consecutive weight rows of one item; warps walk one
-//     global task list (all items of a grouped launch back to back).
-//   * Each row is cut into 16-byte chunks (32 Q4 codes = one block, or 16 Q8
-//     codes = half a block); lane l owns chunks l, l+32, ...  A "slab" is the
-//     32 chunks the warp's lanes own in one pass over the RG rows.
-//   * Every lane streams exactly the chunks (and their block trailers) it will
-//     consume into its own slots of a D-deep shared-memory ring with
-//     cp.async; the ring runs D slabs ahead of the math, across task and
-//     item boundaries.  A lane only ever reads what it copied itself: no
-//     barriers.  Launches use programmatic dependent launch, so a following
-//     voxq kernel is scheduled while this one drains.
-//   * Codes become exact floats without conversion instructions: code bits are
-//     OR-ed into the mantissa of 2^23 (byte permute / LOP3) and 2^23 is taken
-//     off with packed f32x2 adds; Q4 nibbles stay at their bit position and
-//     the matching activation is pre-scaled by 2^-p instead.
-//   * Per chunk: y += scale * sum(q*x) + min * sum(x)  (the dequantized weight
-//     q*scale+min is never formed; fp32 throughout, packed fma.rn.f32x2).
-//   * One transposed butterfly reduces all RG*M row sums of a task at once.
+// Exact integer formulation.  Each 16-byte chunk of a weight row holds 32 Q4
+// codes (one quantization block) or 16 Q8 codes (half a block).  The matching
+// activation chunk x is split once, by a prepass kernel, into three int8
+// limbs with per-chunk scales d1, d2 = d1/254, d3 = d2/254:
+//     x ~= d1*l1 + d2*l2 + d3*l3,  |l_i| <= 127,  error <= d3/2 (~2^-21 |x|max)
+// so the chunk's code dot product is three exact integer dot products, each a
+// dp4a per 4 codes on the raw code bytes (Q4 nibbles are split with one LOP3
+// per 4 codes; the prepass stores the limbs in the matching even/odd order).
+// Per chunk and row:
+//     y += scale * (d1*S1 + d2*S2 + d3*S3) + min * sum(x)
+// -- the dequantized weight q*scale+min is never formed.
+//
+// Streaming.  A tile is T consecutive rows of one item (16 KB of codes, one
+// contiguous range, plus their contiguous trailers).  One producer warp per
+// CTA streams tiles into a 4-deep shared-memory ring with two cp.async.bulk
+// copies each; 8 consumer warps each take groups of RG rows x one 512-byte
+// K-slab (32 lanes x 16 B), so activation limbs loaded once serve RG rows.
+// Rows longer than one slab are split across warps and their partial sums
+// combined in shared memory behind one named barrier per tile.  CTAs own
+// contiguous tile ranges, so consecutive tiles share an item and its limbs
+// stay in L1.  The producer starts streaming before the kernel waits on its
+// predecessor, which is always the limb prepass of the same call (that
+// prepass never writes weights and waits on its own predecessor first).
 #include <mutex>
 
 #include "voxq_common.cuh"
@@ -30,140 +36,209 @@
 
 namespace voxq {
 
+// Tuning knobs (overridable at build time): consumer warps per CTA (+1
+// producer warp) and ring depth.  A stage holds kConsumers groups of 4 rows x
+// one 512-byte slab, i.e. kConsumers * 2 KB of codes.
+#ifndef VOXQ_GEMV_CONSUMERS
+#define VOXQ_GEMV_CONSUMERS 8
+#endif
+#ifndef VOXQ_GEMV_STAGES
+#define VOXQ_GEMV_STAGES 4
+#endif
+constexpr int kConsumers = VOXQ_GEMV_CONSUMERS;
+constexpr int kStages = VOXQ_GEMV_STAGES;
+constexpr int kTile = kConsumers * 4 * 512;  // code bytes per stage (all weights of the tile)
+
+// Per-chunk limb record, in 16-byte granules laid out [m][granule][chunk] so a
+// warp reading granule g of 32 consecutive chunks issues one coalesced 512-B load.
+//   Q4 (32 codes): granules 0..5 = limb L (0..2) x {odd codes, even codes}
+//                  words j = 0..3 hold the limbs of elements 8j+1,3,5,7 (odd)
+//                  or 8j+0,2,4,6 (even); granule 6 = (d1, d2, d3, sum x)
+//   Q8 (16 codes): granules 0..2 = limb L, bytes in element order;
+//                  granule 3 = (d1, d2, d3, sum x)
+__host__ __device__ constexpr int limb_granules(int qtype) { return qtype == VOXQ_Q4 ? 7 : 4; }
+
+struct LimbJob {
+    const float* a;
+    uint4* dst;
+    int32_t M, lda, chunks;  // chunks per activation row
+    int32_t chunk_begin;     // prefix over jobs of M * chunks
+};
+
+constexpr int kMaxJobs = VOXQ_MAX_BATCH;
+struct LimbParams {
+    int32_t count, total, qtype, pad;
+    LimbJob job[kMaxJobs];
+};
+
+__device__ __forceinline__ int8_t rint_clamp127(float v) {
+    float r = rintf(v);
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    return (int8_t)(int)r;
+}
+
+// One thread per 8 consecutive activation values: Q4 chunks (32 values) are
+// 4 threads, Q8 chunks (16 values) 2 threads; chunk max / sum by shuffles.
+template <int QT>
+__global__ void __launch_bounds__(256) limb_kernel(const __grid_constant__ LimbParams p) {
+    pdl_wait();  // the activations may come from the previous kernel
+    pdl_launch_dependents();
+    constexpr int TPC = QT == VOXQ_Q4 ? 4 : 2;  // threads per chunk
+    constexpr int G = limb_granules(QT);
+    const int lane = threadIdx.x & 31;
+    int j = 0;
+    // every chunk's threads sit in one warp (TPC divides 32), and the loop
+    // stride is a multiple of 32, so shuffles stay within live groups
+    const int total = p.total * TPC;
+    const int span = (total + 31) & ~31;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < span; t += gridDim.x * blockDim.x) {
+        const bool live = t < total;
+        const int cidx = live ? t / TPC : 0;  // global chunk index
+        const int part = t % TPC;
+        if (j + 1 < p.count && cidx >= p.job[j + 1].chunk_begin) {
+            int lo = j + 1, hi = p.count - 1;  // last job with chunk_begin <= cidx
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (p.job[mid].chunk_begin <= cidx) lo = mid; else hi = mid - 1;
+            }
+            j = lo;
+        }
+        const LimbJob& jb = p.job[j];
+        const int local = cidx - jb.chunk_begin;
+        const int m = local / jb.chunks, c = local % jb.chunks;
+        float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (live) {
+            const float* x = jb.a + (int64_t)m * jb.lda + (int64_t)c * (8 * TPC) + part * 8;
+            const float4 f0 = *reinterpret_cast<const float4*>(x);
+            const float4 f1 = *reinterpret_cast<const float4*>(x + 4);
+            v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+            v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+        }
+        float amax = 0.0f, sum = 0.0f, asum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            amax = fmaxf(amax, fabsf(v[i]));
+            sum += v[i];
+            asum += fabsf(v[i]);
+        }
+#pragma unroll
+        for (int o = 1; o < TPC; o <<= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            asum += __shfl_xor_sync(0xffffffffu, asum, o);
+        }
+        if (!live) continue;
+        // d1: power of two with amax / d1 <= 127 (exact scaling); d2, d3 refine.
+        float d1 = 1.0f;
+        if (amax > 0.0f && isfinite(amax)) {
+            int e;
+            frexpf(amax * (1.0f / 127.0f), &e);
+            d1 = ldexpf(1.0f, e);
+            if (amax > 127.0f * d1) d1 *= 2.0f;
+        }
+        const float inv1 = 1.0f / d1;  // exact: power of two
+        const float d2 = d1 * (1.0f / 254.0f), d3 = d2 * (1.0f / 254.0f);
+        // Two limbs leave an error of at most ~3e-5 * amax per value; a chunk
+        // whose magnitude is spread (amax <= 5 * mean |x|) keeps that far below
+        // the matmul tolerance, so its third limb is dropped (d3 = 0).
+        const bool need3 = amax * (8 * TPC) > 5.0f * asum;
+        int8_t l[3][8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float r = v[i];
+            const float a = fminf(fmaxf(rintf(r * inv1), -127.0f), 127.0f);
+            r = fmaf(-a, d1, r);
+            const float b = fminf(fmaxf(rintf(r * (254.0f * inv1)), -127.0f), 127.0f);
+            r = fmaf(-b, d2, r);
+            const float cc = need3 ? fminf(fmaxf(rintf(r * (64516.0f * inv1)), -127.0f), 127.0f) : 0.0f;
+            l[0][i] = (int8_t)(int)a;
+            l[1][i] = (int8_t)(int)b;
+            l[2][i] = (int8_t)(int)cc;
+        }
+        auto pack4 = [](int8_t a, int8_t b, int8_t c2, int8_t d) -> uint32_t {
+            return (uint32_t)(uint8_t)a | ((uint32_t)(uint8_t)b << 8) | ((uint32_t)(uint8_t)c2 << 16) |
+                   ((uint32_t)(uint8_t)d << 24);
+        };
+        uint8_t* base = reinterpret_cast<uint8_t*>(jb.dst + (int64_t)m * G * jb.chunks + c);
+        const int64_t gstride = (int64_t)jb.chunks * 16;  // bytes between granules
+#pragma unroll
+        for (int L = 0; L < 3; L++) {
+            if (QT == VOXQ_Q4) {
+                // this thread's 8 values are code word `part` of the chunk
+                *reinterpret_cast<uint32_t*>(base + (2 * L) * gstride + 4 * part) =
+                    pack4(l[L][1], l[L][3], l[L][5], l[L][7]);
+                *reinterpret_cast<uint32_t*>(base + (2 * L + 1) * gstride + 4 * part) =
+                    pack4(l[L][0], l[L][2], l[L][4], l[L][6]);
+            } else {
+                *reinterpret_cast<uint2*>(base + L * gstride + 8 * part) =
+                    make_uint2(pack4(l[L][0], l[L][1], l[L][2], l[L][3]), pack4(l[L][4], l[L][5], l[L][6], l[L][7]));
+            }
+        }
+        if (part == 0)
+            *reinterpret_cast<uint4*>(base + (G - 1) * gstride) =
+                make_uint4(__float_as_uint(d1), __float_as_uint(d2), __float_as_uint(need3 ? d3 : 0.0f),
+                           __float_as_uint(sum));
+    }
+}
+
 struct GemvItemDev {
     const uint8_t* codes;
     const uint8_t* scales;
     const uint8_t* up_codes;
     const uint8_t* up_scales;
-    const float* a;
+    const uint4* limbs;  // [M][granule][chunks]
     float* out;
     const float* bias;
     const float* residual;
-    int32_t N, K, M, lda, ldo, ldr;
+    int32_t N, K, M, ldo, ldr;
+    int32_t rowb;        // code bytes per row
+    int32_t srow;        // trailer bytes per row
     int32_t chunks;      // 16-byte code chunks per row
     int32_t slabs;       // ceil(chunks / 32)
-    int32_t task_begin;  // first global task index of this item
+    int32_t T;           // rows per tile
+    int32_t tile_begin;  // first global tile of this item
     int32_t pad;
 };
 
 template <int MAXI>
 struct GemvParams {
     int32_t count;
-    int32_t total_tasks;
+    int32_t total_tiles;
     int* err;
     GemvItemDev it[MAXI];
 };
 
-constexpr int kWarps = 8;  // warps per CTA
-
-// Q4: per position e of the 8 codes in one 32-bit word, the bit offset p(e)
-// at which conv_q4 leaves the nibble -> the activation is scaled by 2^-p(e).
-__device__ __forceinline__ void q4_prescale(float (&x)[8]) {
-    x[0] *= 0.0625f;             // 2^-4
-    x[2] *= 0.000244140625f;     // 2^-12
-    x[3] *= 0.00390625f;         // 2^-8
-    x[4] *= 0.00390625f;         // 2^-8
-    x[5] *= 1.52587890625e-05f;  // 2^-16
-    x[6] *= 1.52587890625e-05f;  // 2^-16
-    x[7] *= 0.000244140625f;     // 2^-12
+__device__ __forceinline__ uint32_t dp4a_us(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
-
-// Q4 word (bytes q0q1 q2q3 q4q5 q6q7, high nibble = even element) -> the eight
-// exact floats q_e * 2^p(e) as four f32x2 pairs (e0,e1) .. (e6,e7).
-__device__ __forceinline__ void conv_q4(uint32_t w, uint64_t (&v)[4]) {
-    const uint32_t w2 = w >> 12;
-    const uint32_t E = 0x4B000000u;
-    const uint64_t bias = 0xCB000000CB000000ull;  // (-2^23, -2^23)
-    float f0 = __uint_as_float((w & 0x000F0u) | E);   // q0 << 4
-    float f1 = __uint_as_float((w & 0x0000Fu) | E);   // q1
-    float f2 = __uint_as_float((w & 0x0F000u) | E);   // q2 << 12
-    float f3 = __uint_as_float((w & 0x00F00u) | E);   // q3 << 8
-    float f4 = __uint_as_float((w2 & 0x00F00u) | E);  // q4 << 8
-    float f5 = __uint_as_float((w & 0xF0000u) | E);   // q5 << 16
-    float f6 = __uint_as_float((w2 & 0xF0000u) | E);  // q6 << 16
-    float f7 = __uint_as_float((w2 & 0x0F000u) | E);  // q7 << 12
-    v[0] = add2(pk(f0, f1), bias);
-    v[1] = add2(pk(f2, f3), bias);
-    v[2] = add2(pk(f4, f5), bias);
-    v[3] = add2(pk(f6, f7), bias);
-}
-
-// Q8 word (4 codes) -> four exact floats as two pairs.  Signed mode reads the
-// byte as int8 like scripts/quantize.py:79: (b ^ 0x80) - 128.
-template <bool SIGNED>
-__device__ __forceinline__ void conv_q8(uint32_t w, uint64_t (&v)[2]) {
-    if (SIGNED) w ^= 0x80808080u;
-    const uint64_t bias = SIGNED ? 0xCB000080CB000080ull : 0xCB000000CB000000ull;  // -(2^23 [+128])
-    float f0 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440));
-    float f1 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441));
-    float f2 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7442));
-    float f3 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7443));
-    v[0] = add2(pk(f0, f1), bias);
-    v[1] = add2(pk(f2, f3), bias);
+__device__ __forceinline__ uint32_t dp4a_ss(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
-// cp.async of 16 / 8 / 4 bytes into this lane's own slot.
-__device__ __forceinline__ void cp16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp8(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp4(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// Position in a warp's stream of (task, slab) stages.
-struct Cursor {
-    int task;  // global task index (-1: past the end)
-    int slab;
-    int item;
-};
-
-template <int MAXI>
-__device__ __forceinline__ void cursor_fix_item(const GemvParams<MAXI>& p, Cursor& c) {
-    while (c.item + 1 < p.count && c.task >= p.it[c.item + 1].task_begin) c.item++;
-}
-
-template <int MAXI>
-__device__ __forceinline__ void cursor_next(const GemvParams<MAXI>& p, Cursor& c, int stride) {
-    if (++c.slab >= p.it[c.item].slabs) {
-        c.slab = 0;
-        c.task += stride;
-        if (c.task >= p.total_tasks) {
-            c.task = -1;
-            return;
-        }
-        cursor_fix_item(p, c);
-    }
-}
+__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory"); }
 
 // Reduces V values per lane across the warp.  Afterwards value v (0 <= v < V)
 // is complete in lanes v * (32 / V) .. v * (32 / V) + 32 / V - 1.
 template <int V>
 __device__ __forceinline__ float transpose_reduce(float (&v)[V], int lane) {
-    int n = V;
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
+    for (int s = 0; s < 5; s++) {
+        const int off = 16 >> s;
+        const int n = V >> s;  // values still held per lane before this step
         if (n > 1) {
             const bool upper = (lane & off) != 0;
-            const int h = n / 2;
 #pragma unroll
-            for (int i = 0; i < V / 2; i++) {
-                if (i < h) {
-                    float send = upper ? v[i] : v[i + h];
-                    float keep = upper ? v[i + h] : v[i];
-                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-                }
+            for (int i = 0; i < n / 2; i++) {
+                const float send = upper ? v[i] : v[i + n / 2];
+                const float keep = upper ? v[i + n / 2] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
             }
-            n = h;
         } else {
             v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
         }
@@ -171,232 +246,286 @@ __device__ __forceinline__ float transpose_reduce(float (&v)[V], int lane) {
     return v[0];
 }
 
-template <int QT, int MT, int RG, int D, bool SWI, bool SIGNED, int MAXI>
-__global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant__ GemvParams<MAXI> p) {
-    constexpr int NW = SWI ? 2 : 1;                       // weights per row (gate, up)
-    constexpr int SB = (QT == VOXQ_Q4) ? 4 : 8;           // trailer bytes per chunk slot
-    constexpr int CPC = (QT == VOXQ_Q4) ? 32 : 16;        // codes per 16-byte chunk
-    constexpr int STAGE_CODES = NW * RG * 32 * 16;        // bytes per warp stage
-    constexpr int STAGE_SC = NW * RG * 32 * 8;
-    constexpr int WARP_BYTES = D * (STAGE_CODES + STAGE_SC);
+template <int MAXI>
+__device__ __forceinline__ void fix_item(const GemvParams<MAXI>& p, int tile, int& item) {
+    while (item + 1 < p.count && tile >= p.it[item + 1].tile_begin) item++;
+}
+
+// Epilogue of one finished output element.
+__device__ __forceinline__ void write_out(const GemvItemDev& it, int n, int m, float v) {
+    if (it.bias) v += it.bias[n];
+    if (it.residual) v += it.residual[(int64_t)m * it.ldr + n];
+    it.out[(int64_t)m * it.ldo + n] = v;
+}
+
+
+// Accumulates one chunk's contribution for RG rows x NW weights of activation
+// row m, with NLIMB int8 limbs of the activation (compile-time, so the unused
+// third limb costs no instructions).
+template <int QT, int NW, int RG, int MT, int NLIMB, bool SIGNED>
+__device__ __forceinline__ void chunk_dot(const uint32_t (&ca)[NW][RG][(QT == VOXQ_Q4) ? 8 : 4],
+                                          const float (&sc)[NW][RG], const float (&mn)[NW][RG], const uint4* lp,
+                                          int chunks, float d1, float d2, float d3, float xs, bool live, int m,
+                                          float (&acc)[NW][RG][MT]) {
+    constexpr int NL = (QT == VOXQ_Q4) ? 8 : 4;
+    uint32_t lw[NLIMB][NL];
+#pragma unroll
+    for (int L = 0; L < NLIMB; L++) {
+        if (QT == VOXQ_Q4) {
+            const uint4 o = __ldg(lp + (int64_t)(2 * L) * chunks);
+            const uint4 e = __ldg(lp + (int64_t)(2 * L + 1) * chunks);
+            lw[L][0] = o.x; lw[L][1] = o.y; lw[L][2] = o.z; lw[L][3] = o.w;
+            lw[L][4 % NL] = e.x; lw[L][5 % NL] = e.y; lw[L][6 % NL] = e.z; lw[L][7 % NL] = e.w;
+        } else {
+            const uint4 o = __ldg(lp + (int64_t)L * chunks);
+            lw[L][0] = o.x; lw[L][1] = o.y; lw[L][2] = o.z; lw[L][3] = o.w;
+        }
+    }
+#pragma unroll
+    for (int w = 0; w < NW; w++)
+#pragma unroll
+        for (int r = 0; r < RG; r++) {
+            float dot = 0.0f;
+#pragma unroll
+            for (int L = NLIMB - 1; L >= 0; L--) {
+                uint32_t so = 0u, se = 0u;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    if (QT == VOXQ_Q4) {
+                        so = dp4a_us(ca[w][r][q], lw[L][q], so);
+                        se = dp4a_us(ca[w][r][4 + q % 4], lw[L][4 + q % 4], se);
+                    } else {
+                        so = SIGNED ? dp4a_ss(ca[w][r][q], lw[L][q], so) : dp4a_us(ca[w][r][q], lw[L][q], so);
+                    }
+                }
+                // Q4: 16 * (odd + even) = 16 * odd + (16 * even)
+                const int S = (QT == VOXQ_Q4) ? (int)(se + (so << 4)) : (int)so;
+                const float d = L == 0 ? d1 : L == 1 ? d2 : d3;
+                dot = fmaf(d, (float)S, dot);
+            }
+            const float a2 = fmaf(sc[w][r], dot, fmaf(mn[w][r], xs, acc[w][r][m]));
+            acc[w][r][m] = live ? a2 : acc[w][r][m];
+        }
+}
+
+template <int QT, int MT, int RG, bool SWI, bool SIGNED, int MAXI>
+__global__ void __launch_bounds__((kConsumers + 1) * 32) gemv_kernel(const __grid_constant__ GemvParams<MAXI> p) {
+    constexpr int NW = SWI ? 2 : 1;  // weights per row (gate, up)
+    constexpr int G = limb_granules(QT);
     constexpr int V = RG * MT;
+    constexpr int NL = (QT == VOXQ_Q4) ? 8 : 4;   // limb words per chunk and limb
+    constexpr int SB = (QT == VOXQ_Q4) ? 4 : 8;   // trailer bytes per block
+    constexpr int CW = kTile / NW;                 // code bytes per weight per stage
+    constexpr int TW = CW / 4 + 32;                // trailer window bytes per weight
+    constexpr int STAGE = kTile + NW * TW;
+    constexpr int PART_G = 32;                     // groups per tile when rows span > 1 slab (host-checked)
 
-    extern __shared__ __align__(16) uint8_t smem[];
-    const int lane = threadIdx.x & 31;
-    const int wib = threadIdx.x >> 5;
-    uint8_t* wbase = smem + wib * WARP_BYTES;
-    uint8_t* codes_s = wbase;
-    uint8_t* sc_s = wbase + D * STAGE_CODES;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t full[kStages], empty[kStages];
+    __shared__ float part[kStages][PART_G][NW][V];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumers);
+        }
+    }
+    mbar_fence_init();
+    __syncthreads();
 
-    const int stride = gridDim.x * kWarps;
-    const int first = blockIdx.x * kWarps + wib;
-    if (first >= p.total_tasks) {
+    const int tb = (int)((int64_t)p.total_tiles * blockIdx.x / gridDim.x);
+    const int te = (int)((int64_t)p.total_tiles * (blockIdx.x + 1) / gridDim.x);
+
+    if (warp == kConsumers) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            int item = 0;
+            for (int t = tb, j = 0; t < te; ++t, ++j) {
+                fix_item(p, t, item);
+                const GemvItemDev& it = p.it[item];
+                const int s = j % kStages;
+                if (j >= kStages) mbar_wait_bounded(&empty[s], ((j / kStages) & 1) ^ 1, VOXQ_DEVERR_WAIT_EMPTY, p.err);
+                const int row0 = (t - it.tile_begin) * it.T;
+                const int rows = min(it.T, it.N - row0);
+                const uint32_t cb = (uint32_t)(rows * it.rowb);
+                const int64_t so = (int64_t)row0 * it.srow;
+                const int64_t sa = so & ~(int64_t)15;
+                const uint32_t tbytes = (uint32_t)(((so - sa) + (int64_t)rows * it.srow + 15) & ~(int64_t)15);
+                mbar_arrive_expect_tx(&full[s], NW * (cb + tbytes));
+                uint8_t* st = smem + s * STAGE;
+#pragma unroll
+                for (int w = 0; w < NW; w++) {
+                    const uint8_t* c = w ? it.up_codes : it.codes;
+                    const uint8_t* sc = w ? it.up_scales : it.scales;
+                    bulk_g2s(st + w * CW, c + (int64_t)row0 * it.rowb, cb, &full[s]);
+                    bulk_g2s(st + kTile + w * TW, sc + sa, tbytes, &full[s]);
+                }
+            }
+            // Normally the consumers have waited for every copy.  If a wait gave
+            // up, give the copies still in flight a bounded moment to land before
+            // the CTA's shared memory is released.
+            if (*reinterpret_cast<volatile int*>(p.err) != 0) {
+                const int n = te - tb;
+                for (int j = (n > kStages ? n - kStages : 0); j < n; j++)
+                    mbar_wait_bounded(&full[j % kStages], (j / kStages) & 1, VOXQ_DEVERR_WAIT_FULL, p.err, 1u << 14);
+            }
+        }
         pdl_launch_dependents();
         return;
     }
 
-    // ---- producer side of this lane's ring ----
-    Cursor pc = {first, 0, 0};
-    cursor_fix_item(p, pc);
-    auto issue = [&](int stage) {
-        if (pc.task >= 0) {
-            const GemvItemDev& it = p.it[pc.item];
-            const int chunk = pc.slab * 32 + lane;
-            if (chunk < it.chunks) {
-                const int n0 = (pc.task - it.task_begin) * RG;
-                const int64_t rowb = (int64_t)it.chunks * 16;
-                const int nblk = it.K / VOXQ_QBLK;
-                const int blk = (QT == VOXQ_Q4) ? chunk : (chunk >> 1);
-#pragma unroll
-                for (int w = 0; w < NW; w++) {
-                    const uint8_t* cb = w ? it.up_codes : it.codes;
-                    const uint8_t* sb = w ? it.up_scales : it.scales;
-#pragma unroll
-                    for (int r = 0; r < RG; r++) {
-                        const int row = min(n0 + r, it.N - 1);
-                        uint8_t* cd = codes_s + stage * STAGE_CODES + ((w * RG + r) * 32 + lane) * 16;
-                        uint8_t* sd = sc_s + stage * STAGE_SC + ((w * RG + r) * 32 + lane) * 8;
-                        cp16(cd, cb + row * rowb + (int64_t)chunk * 16);
-                        const uint8_t* ss = sb + ((int64_t)row * nblk + blk) * SB;
-                        if (SB == 4)
-                            cp4(sd, ss);
-                        else
-                            cp8(sd, ss);
-                    }
-                }
-            }
-            cursor_next(p, pc, stride);
-        }
-        cp_commit();  // empty groups keep the wait_group arithmetic uniform
-    };
-
-    // Everything this kernel reads (weights included: a quantize or pack kernel
-    // may have just written them) can come from the previous kernel in the
-    // stream, so wait for it before the first copy; the next kernel may launch.
-    pdl_wait();
+    // ---------------- consumers ----------------
+    pdl_wait();  // limbs come from the prepass launched just before this kernel
     pdl_launch_dependents();
-#pragma unroll
-    for (int s = 0; s < D; s++) issue(s);
+    int item = 0;
+    for (int t = tb, j = 0; t < te; ++t, ++j) {
+        fix_item(p, t, item);
+        const GemvItemDev& it = p.it[item];
+        const int s = j % kStages;
+        // a wait that gives up records the error and the tile is processed
+        // anyway (garbage), so every warp still meets the same barriers
+        mbar_wait_bounded(&full[s], (j / kStages) & 1, VOXQ_DEVERR_WAIT_FULL, p.err);
+        const uint8_t* st = smem + s * STAGE;
+        const int row0 = (t - it.tile_begin) * it.T;
+        const int rows = min(it.T, it.N - row0);
+        const int delta = (int)(((int64_t)row0 * it.srow) & 15);
+        const int SL = it.slabs;
+        const int ngroups = ((rows + RG - 1) / RG) * SL;
 
-    Cursor cc = {first, 0, 0};
-    cursor_fix_item(p, cc);
-    float acc[NW][RG][MT];
-    int stage = 0;
-    while (cc.task >= 0) {
-        const GemvItemDev& it = p.it[cc.item];
-        if (cc.slab == 0) {
+        // group g = (row group rgi, slab sl), g = warp, warp + kConsumers, ...
+        int sl = warp % SL, rgi = warp / SL;
+        for (int g = warp; g < ngroups; g += kConsumers) {
+            const int chunk0 = sl * 32 + lane;
+            const bool live = chunk0 < it.chunks;  // a row's last slab may be partial
+            const int chunk = live ? chunk0 : it.chunks - 1;
+            float acc[NW][RG][MT];
 #pragma unroll
             for (int w = 0; w < NW; w++)
 #pragma unroll
                 for (int r = 0; r < RG; r++)
 #pragma unroll
                     for (int m = 0; m < MT; m++) acc[w][r][m] = 0.0f;
-        }
-        cp_wait<D - 1>();
-        const int chunk = cc.slab * 32 + lane;
-        if (chunk < it.chunks) {
-            // activation chunk: CPC values per row, in 8-element quarters
-            uint64_t dot[NW][RG][MT];
-#pragma unroll
-            for (int w = 0; w < NW; w++)
-#pragma unroll
-                for (int r = 0; r < RG; r++)
-#pragma unroll
-                    for (int m = 0; m < MT; m++) dot[w][r][m] = 0ull;
-            float xsum[MT];
-#pragma unroll
-            for (int m = 0; m < MT; m++) xsum[m] = 0.0f;
-            uint4 cw[NW][RG];
-#pragma unroll
-            for (int w = 0; w < NW; w++)
-#pragma unroll
-                for (int r = 0; r < RG; r++)
-                    cw[w][r] = *reinterpret_cast<const uint4*>(codes_s + stage * STAGE_CODES +
-                                                               ((w * RG + r) * 32 + lane) * 16);
-#pragma unroll
-            for (int q = 0; q < CPC / 8; q++) {
-                uint64_t xp[MT][4];
-#pragma unroll
-                for (int m = 0; m < MT; m++) {
-                    const int mm = m < it.M ? m : it.M - 1;
-                    const float* ap = it.a + (int64_t)mm * it.lda + (int64_t)chunk * CPC + q * 8;
-                    float4 a0 = ldg_f4(ap), a1 = ldg_f4(ap + 4);
-                    float x[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                    xsum[m] += ((x[0] + x[1]) + (x[2] + x[3])) + ((x[4] + x[5]) + (x[6] + x[7]));
-                    if (QT == VOXQ_Q4) q4_prescale(x);
-#pragma unroll
-                    for (int j = 0; j < 4; j++) xp[m][j] = pk(x[2 * j], x[2 * j + 1]);
-                }
-#pragma unroll
-                for (int w = 0; w < NW; w++)
-#pragma unroll
-                    for (int r = 0; r < RG; r++) {
-                        uint64_t v[4];
-                        const uint4 c = cw[w][r];
-                        if (QT == VOXQ_Q4) {
-                            const uint32_t word = q == 0 ? c.x : q == 1 ? c.y : q == 2 ? c.z : c.w;
-                            conv_q4(word, v);
-                        } else {
-                            uint64_t lo[2], hi[2];
-                            conv_q8<SIGNED>(q == 0 ? c.x : c.z, lo);
-                            conv_q8<SIGNED>(q == 0 ? c.y : c.w, hi);
-                            v[0] = lo[0]; v[1] = lo[1]; v[2] = hi[0]; v[3] = hi[1];
-                        }
-#pragma unroll
-                        for (int m = 0; m < MT; m++)
-#pragma unroll
-                            for (int j = 0; j < 4; j++) dot[w][r][m] = fma2(v[j], xp[m][j], dot[w][r][m]);
-                    }
-            }
+            // codes -> dp4a operands.  Q4 bytes hold (even << 4 | odd): the odd
+            // codes are `w & 0x0F..`, the even ones stay in place as 16 * code.
+            uint32_t ca[NW][RG][NL];
+            float sc[NW][RG], mn[NW][RG];
+            const int blk = (QT == VOXQ_Q4) ? chunk : (chunk >> 1);
 #pragma unroll
             for (int w = 0; w < NW; w++)
 #pragma unroll
                 for (int r = 0; r < RG; r++) {
-                    float s, mn;
-                    const uint8_t* sp = sc_s + stage * STAGE_SC + ((w * RG + r) * 32 + lane) * 8;
-                    if (QT == VOXQ_Q4) {
-                        const uint32_t t = *reinterpret_cast<const uint32_t*>(sp);
-                        s = __half2float(__ushort_as_half((unsigned short)(t & 0xffff)));
-                        mn = __half2float(__ushort_as_half((unsigned short)(t >> 16)));
-                    } else {
-                        const float2 t = *reinterpret_cast<const float2*>(sp);
-                        s = t.x;
-                        mn = t.y;
-                    }
+                    const int lr = min(rgi * RG + r, rows - 1);
+                    const uint4 c = *reinterpret_cast<const uint4*>(st + w * CW + lr * it.rowb + chunk * 16);
+                    const uint32_t wd[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-                    for (int m = 0; m < MT; m++) {
-                        float d0, d1;
-                        upk(dot[w][r][m], d0, d1);
-                        acc[w][r][m] = fmaf(s, d0 + d1, fmaf(mn, xsum[m], acc[w][r][m]));
+                    for (int q = 0; q < 4; q++) {
+                        if (QT == VOXQ_Q4) {
+                            ca[w][r][q] = wd[q] & 0x0F0F0F0Fu;
+                            ca[w][r][4 + q % 4] = wd[q] & 0xF0F0F0F0u;
+                        } else {
+                            ca[w][r][q] = wd[q];
+                        }
+                    }
+                    const uint8_t* tp = st + kTile + w * TW + delta + lr * it.srow + blk * SB;
+                    if (QT == VOXQ_Q4) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(tp));
+                        sc[w][r] = f.x;
+                        mn[w][r] = f.y;
+                    } else {
+                        const float2 tv = *reinterpret_cast<const float2*>(tp);
+                        sc[w][r] = tv.x;
+                        mn[w][r] = tv.y;
                     }
                 }
-        }
-        // refill the slot just consumed with the stage D ahead
-        issue(stage);
-        stage = stage + 1 == D ? 0 : stage + 1;
-
-        const bool task_done = cc.slab + 1 >= it.slabs;
-        if (task_done) {
-            const int n0 = (cc.task - it.task_begin) * RG;
-            float vg[V];
 #pragma unroll
-            for (int r = 0; r < RG; r++)
+            for (int m = 0; m < MT; m++) {
+                const int mm = m < it.M ? m : it.M - 1;
+                const uint4* lp = it.limbs + (int64_t)mm * G * it.chunks + chunk;
+                const uint4 dd = __ldg(lp + (int64_t)(G - 1) * it.chunks);
+                const float k = (QT == VOXQ_Q4) ? 0.0625f : 1.0f;  // Q4 sums are 16x
+                const float d1 = __uint_as_float(dd.x) * k, d2 = __uint_as_float(dd.y) * k;
+                const float d3 = __uint_as_float(dd.z) * k, xs = __uint_as_float(dd.w);
+                // the third limb only where some lane's chunk needs it
+                const bool use3 = __any_sync(0xffffffffu, live && dd.z != 0u);
+                if (use3)
+                    chunk_dot<QT, NW, RG, MT, 3, SIGNED>(ca, sc, mn, lp, it.chunks, d1, d2, d3, xs, live, m, acc);
+                else
+                    chunk_dot<QT, NW, RG, MT, 2, SIGNED>(ca, sc, mn, lp, it.chunks, d1, d2, d3, xs, live, m, acc);
+            }
+            // reduce the group's RG x MT sums across the lanes
+            float red[NW];
 #pragma unroll
-                for (int m = 0; m < MT; m++) vg[r * MT + m] = acc[0][r][m];
-            float val = transpose_reduce<V>(vg, lane);
-            if (SWI) {
-                float vu[V];
+            for (int w = 0; w < NW; w++) {
+                float v[V];
 #pragma unroll
                 for (int r = 0; r < RG; r++)
 #pragma unroll
-                    for (int m = 0; m < MT; m++) vu[r * MT + m] = acc[NW - 1][r][m];
-                val = silu(val) * transpose_reduce<V>(vu, lane);
+                    for (int m = 0; m < MT; m++) v[r * MT + m] = acc[w][r][m];
+                red[w] = transpose_reduce<V>(v, lane);
             }
-            constexpr int LPV = 32 / V;  // lanes holding each value
+            constexpr int LPV = 32 / V;
             if ((lane & (LPV - 1)) == 0) {
                 const int v = lane / LPV;
-                const int r = v / MT, m = v % MT;
-                const int n = n0 + r;
-                if (n < it.N && m < it.M) {
-                    if (it.bias) val += it.bias[n];
-                    if (it.residual) val += it.residual[(int64_t)m * it.ldr + n];
-                    it.out[(int64_t)m * it.ldo + n] = val;
+                if (SL == 1) {
+                    const int n = row0 + rgi * RG + v / MT, m = v % MT;
+                    if (rgi * RG + v / MT < rows && m < it.M)
+                        write_out(it, n, m, SWI ? silu(red[0]) * red[NW - 1] : red[0]);
+                } else {
+#pragma unroll
+                    for (int w = 0; w < NW; w++) part[s][g][w][v] = red[w];
                 }
             }
+            sl += kConsumers;
+            while (sl >= SL) {
+                sl -= SL;
+                rgi++;
+            }
         }
-        cursor_next(p, cc, stride);
+        if (SL > 1) {
+            // rows span several slabs: combine the slab partial sums
+            consumer_bar();
+            const int nrg = (rows + RG - 1) / RG;
+            for (int e = warp * 32 + lane; e < nrg * V; e += kConsumers * 32) {
+                const int rgi = e / V, v = e % V;
+                float sum[NW];
+#pragma unroll
+                for (int w = 0; w < NW; w++) {
+                    sum[w] = 0.0f;
+                    for (int sl = 0; sl < SL; sl++) sum[w] += part[s][rgi * SL + sl][w][v];
+                }
+                const int r = rgi * RG + v / MT, m = v % MT;
+                if (r < rows && m < it.M) write_out(it, row0 + r, m, SWI ? silu(sum[0]) * sum[NW - 1] : sum[0]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
     }
-    cp_wait<0>();
 }
 
-// Kernel shape per activation-row count: rows per task and ring depth.
+// Rows per consumer group for each activation-row count.
 template <int MT, bool SWI>
 struct Shape {
-    static constexpr int RG0 = MT == 1 ? 4 : MT == 2 ? 4 : MT == 4 ? 2 : 2;
-    static constexpr int RG = SWI ? (RG0 > 2 ? RG0 / 2 : RG0) : RG0;
-    static constexpr int D = 4;
+    static constexpr int RG = (MT * (SWI ? 2 : 1) <= 2) ? 4 : 2;
 };
+static int rows_per_group(int mt, bool swi) { return (mt * (swi ? 2 : 1) <= 2) ? 4 : 2; }
 
 template <int QT, int MT, bool SWI, bool SIGNED, int MAXI>
 static VoxCPMError launch_t(const GemvParams<MAXI>& p, cudaStream_t st) {
     constexpr int RG = Shape<MT, SWI>::RG;
-    constexpr int D = Shape<MT, SWI>::D;
     constexpr int NW = SWI ? 2 : 1;
-    constexpr int smem = kWarps * D * NW * RG * 32 * (16 + 8);
-    auto kern = gemv_kernel<QT, MT, RG, D, SWI, SIGNED, MAXI>;
+    constexpr int smem = kStages * (kTile + NW * (kTile / NW / 4 + 32));
+    auto kern = gemv_kernel<QT, MT, RG, SWI, SIGNED, MAXI>;
     static int occ = 0;
     static std::once_flag once;
     std::call_once(once, [&] {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kWarps * 32, smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, (kConsumers + 1) * 32, smem);
     });
-    const int sms = device_sm_count();
-    const int want = (p.total_tasks + kWarps - 1) / kWarps;
-    const int cap = sms * (occ > 0 ? occ : 1);
-    const int blocks = want < cap ? (want < 1 ? 1 : want) : cap;
+    const int cap = device_sm_count() * (occ > 0 ? occ : 1);
+    const int blocks = p.total_tiles < cap ? p.total_tiles : cap;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(blocks);
-    cfg.blockDim = dim3(kWarps * 32);
+    cfg.gridDim = dim3(blocks < 1 ? 1 : blocks);
+    cfg.blockDim = dim3((kConsumers + 1) * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -410,8 +539,8 @@ static VoxCPMError launch_t(const GemvParams<MAXI>& p, cudaStream_t st) {
 
 template <int MAXI>
 static VoxCPMError dispatch(const GemvParams<MAXI>& p, int qtype, int mt, bool swi, bool sgn, cudaStream_t st) {
-#define VOXQ_GEMV_CASE(QT, MT)                                                                         \
-    if (qtype == QT && mt == MT) {                                                                     \
+#define VOXQ_GEMV_CASE(QT, MT)                                                                          \
+    if (qtype == QT && mt == MT) {                                                                      \
         if (swi) return sgn ? launch_t<QT, MT, true, true, MAXI>(p, st) : launch_t<QT, MT, true, false, MAXI>(p, st); \
         return sgn ? launch_t<QT, MT, false, true, MAXI>(p, st) : launch_t<QT, MT, false, false, MAXI>(p, st);      \
     }
@@ -429,15 +558,6 @@ static VoxCPMError dispatch(const GemvParams<MAXI>& p, int qtype, int mt, bool s
 
 static int round_mt(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 
-static int rows_per_task(int mt, bool swi) {
-    switch (mt) {
-        case 1: return swi ? Shape<1, true>::RG : Shape<1, false>::RG;
-        case 2: return swi ? Shape<2, true>::RG : Shape<2, false>::RG;
-        case 4: return swi ? Shape<4, true>::RG : Shape<4, false>::RG;
-        default: return swi ? Shape<8, true>::RG : Shape<8, false>::RG;
-    }
-}
-
 VoxCPMError validate_item(const voxq_gemv_item& x) {
     const voxq_qweight& w = x.w;
     if (w.qtype != VOXQ_Q4 && w.qtype != VOXQ_Q8) return VOXCPM_ERR_UNSUPPORTED;
@@ -445,48 +565,43 @@ VoxCPMError validate_item(const voxq_gemv_item& x) {
     if (w.N == 0 || x.M == 0) return VOXCPM_SUCCESS;
     if (!x.a || !x.out || (w.K > 0 && (!w.codes || !w.scales))) return VOXCPM_ERR_INTERNAL;
     if (x.lda < w.K || x.ldo < w.N || (x.residual && x.ldr < w.N)) return VOXCPM_ERR_SHAPE_MISMATCH;
-    // 16-byte activation loads, 16-byte code copies, 4/8-byte trailer copies
+    // a row of codes must fit one stage (K <= 16384 for Q8, 32768 for Q4; half that with SwiGLU)
+    if (codes_row_bytes(w.K, w.qtype) * (x.up_codes ? 2 : 1) > kTile) return VOXCPM_ERR_UNSUPPORTED;
+    // 16-byte activation loads, 16-byte aligned code and trailer arrays
     if ((reinterpret_cast<uintptr_t>(x.a) & 15) || (x.lda & 3)) return VOXCPM_ERR_UNSUPPORTED;
-    const uintptr_t sa = w.qtype == VOXQ_Q4 ? 3 : 7;
-    if ((reinterpret_cast<uintptr_t>(w.codes) & 15) || (reinterpret_cast<uintptr_t>(w.scales) & sa))
+    if ((reinterpret_cast<uintptr_t>(w.codes) & 15) || (reinterpret_cast<uintptr_t>(w.scales) & 15))
         return VOXCPM_ERR_UNSUPPORTED;
     if (x.up_codes && ((reinterpret_cast<uintptr_t>(x.up_codes) & 15) ||
-                       (reinterpret_cast<uintptr_t>(x.up_scales) & sa) || !x.up_scales))
+                       (reinterpret_cast<uintptr_t>(x.up_scales) & 15) || !x.up_scales))
         return VOXCPM_ERR_UNSUPPORTED;
     return VOXCPM_SUCCESS;
 }
 
-static void fill_dev(GemvItemDev& d, const voxq_gemv_item& x, int task_begin) {
-    d.codes = x.w.codes;
-    d.scales = reinterpret_cast<const uint8_t*>(x.w.scales);
-    d.up_codes = x.up_codes;
-    d.up_scales = reinterpret_cast<const uint8_t*>(x.up_scales);
-    d.a = x.a;
-    d.out = x.out;
-    d.bias = x.bias;
-    d.residual = x.residual;
-    d.N = x.w.N;
-    d.K = x.w.K;
-    d.M = x.M;
-    d.lda = x.lda;
-    d.ldo = x.ldo;
-    d.ldr = x.ldr;
-    d.chunks = (int32_t)(codes_row_bytes(x.w.K, x.w.qtype) / 16);
-    d.slabs = (d.chunks + 31) / 32;
-    d.task_begin = task_begin;
-    d.pad = 0;
+// Bytes of the limb workspace for one activation (M rows, K columns).
+static size_t limb_bytes(int M, int K, int qtype) {
+    const int chunks = (int)(codes_row_bytes(K, qtype) / 16);
+    return (size_t)M * limb_granules(qtype) * chunks * 16;
 }
 
-// Launches the items that share (qtype, swiglu, signed) as one grid.
+// Launches the items that share (qtype, swiglu, signed): one limb prepass for
+// their distinct activations, then one GEMV grid.
 template <int MAXI>
-static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStream_t st) {
+static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStream_t st, void* ws, size_t ws_bytes) {
     static thread_local GemvParams<MAXI> p;
+    static thread_local LimbParams lp;
     const voxq_gemv_item& f = *sel[0];
+    const int qt = f.w.qtype;
     int mt = 1;
     for (int i = 0; i < n; i++) mt = max(mt, round_mt(sel[i]->M));
     const bool swi = f.up_codes != nullptr;
-    const int rg = rows_per_task(mt, swi);
-    int tasks = 0, c = 0;
+    const int nw = swi ? 2 : 1;
+
+    // distinct activations -> limb jobs
+    struct Act { const float* a; int M, lda, K; uint4* dst; };
+    Act acts[VOXQ_MAX_BATCH];
+    int nact = 0;
+    size_t off = 0;
+    int c = 0, tiles = 0;
     for (int i = 0; i < n; i++) {
         const voxq_gemv_item& x = *sel[i];
         if (x.w.N == 0 || x.M == 0) continue;
@@ -495,18 +610,101 @@ static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStr
             if (e) return e;
             continue;
         }
-        fill_dev(p.it[c], x, tasks);
-        tasks += (x.w.N + rg - 1) / rg;
+        int ai = -1;
+        for (int k = 0; k < nact; k++)
+            if (acts[k].a == x.a && acts[k].M == x.M && acts[k].lda == x.lda && acts[k].K == x.w.K) ai = k;
+        if (ai < 0) {
+            const size_t b = limb_bytes(x.M, x.w.K, qt);
+            if (off + b > ws_bytes) return VOXCPM_ERR_OOM;
+            acts[nact] = {x.a, x.M, x.lda, x.w.K, reinterpret_cast<uint4*>(static_cast<uint8_t*>(ws) + off)};
+            off += (b + 255) & ~(size_t)255;
+            ai = nact++;
+        }
+        GemvItemDev& d = p.it[c];
+        d.codes = x.w.codes;
+        d.scales = reinterpret_cast<const uint8_t*>(x.w.scales);
+        d.up_codes = x.up_codes;
+        d.up_scales = reinterpret_cast<const uint8_t*>(x.up_scales);
+        d.limbs = acts[ai].dst;
+        d.out = x.out;
+        d.bias = x.bias;
+        d.residual = x.residual;
+        d.N = x.w.N;
+        d.K = x.w.K;
+        d.M = x.M;
+        d.ldo = x.ldo;
+        d.ldr = x.ldr;
+        d.rowb = (int32_t)codes_row_bytes(x.w.K, qt);
+        d.srow = (x.w.K / VOXQ_QBLK) * scale_bytes(qt);
+        d.chunks = d.rowb / 16;
+        d.slabs = (d.chunks + 31) / 32;
+        // rows per tile: fill the stage; rows spanning several slabs keep the
+        // tile a whole number of 512-byte slabs so groups tile it exactly
+        int T = kTile / nw / d.rowb;
+        if (T > x.w.N) T = x.w.N;
+        if (T < 1) T = 1;
+        if (d.slabs > 1) {
+            // partial-sum slots per tile: ceil(T / RG) * slabs <= 32
+            const int rg = rows_per_group(mt, swi);
+            if (T >= rg) T = T / rg * rg;
+            while (T > 1 && ((T + rg - 1) / rg) * d.slabs > 32) T--;
+        }
+        d.T = T;
+        d.tile_begin = tiles;
+        tiles += (x.w.N + d.T - 1) / d.T;
         c++;
     }
     if (c == 0) return VOXCPM_SUCCESS;
     p.count = c;
-    p.total_tasks = tasks;
+    p.total_tiles = tiles;
     p.err = device_error_word();
-    return dispatch<MAXI>(p, f.w.qtype, mt, swi, f.w.q8_signed != 0, st);
+
+    // limb prepass (several launches only if there are more than kMaxJobs activations)
+    for (int a0 = 0; a0 < nact; a0 += kMaxJobs) {
+        const int na = min(kMaxJobs, nact - a0);
+        int total = 0;
+        for (int k = 0; k < na; k++) {
+            const Act& a = acts[a0 + k];
+            LimbJob& j = lp.job[k];
+            j.a = a.a;
+            j.dst = a.dst;
+            j.M = a.M;
+            j.lda = a.lda;
+            j.chunks = (int32_t)(codes_row_bytes(a.K, qt) / 16);
+            j.chunk_begin = total;
+            total += a.M * j.chunks;
+        }
+        lp.count = na;
+        lp.total = total;
+        lp.qtype = qt;
+        cudaLaunchConfig_t cfg = {};
+        const int tpc = qt == VOXQ_Q4 ? 4 : 2;
+        const int blocks = (total * tpc + 255) / 256;
+        cfg.gridDim = dim3(blocks < 1 ? 1 : (blocks > 8 * device_sm_count() ? 8 * device_sm_count() : blocks));
+        cfg.blockDim = dim3(256);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (qt == VOXQ_Q4)
+            VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, limb_kernel<VOXQ_Q4>, lp));
+        else
+            VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, limb_kernel<VOXQ_Q8>, lp));
+    }
+    return dispatch<MAXI>(p, qt, mt, swi, f.w.q8_signed != 0, st);
 }
 
-VoxCPMError gemv_launch(const voxq_gemv_item* items, int count, cudaStream_t st) {
+size_t gemv_workspace_bytes(const voxq_gemv_item* items, int count) {
+    size_t total = 0;
+    for (int i = 0; i < count; i++)
+        if (items[i].w.K > 0 && items[i].M > 0)
+            total += (limb_bytes(items[i].M, items[i].w.K, items[i].w.qtype) + 255) & ~(size_t)255;
+    return total;
+}
+
+VoxCPMError gemv_launch_ws(const voxq_gemv_item* items, int count, cudaStream_t st, void* ws, size_t ws_bytes) {
     if (count < 0 || count > VOXQ_MAX_BATCH) return VOXCPM_ERR_UNSUPPORTED;
     for (int i = 0; i < count; i++) {
         VoxCPMError e = validate_item(items[i]);
@@ -515,6 +713,7 @@ VoxCPMError gemv_launch(const voxq_gemv_item* items, int count, cudaStream_t st)
     // group by kernel variant, preserving order inside a group
     const voxq_gemv_item* sel[VOXQ_MAX_BATCH];
     bool done[VOXQ_MAX_BATCH] = {};
+    size_t used = 0;
     for (int i = 0; i < count; i++) {
         if (done[i]) continue;
         int n = 0;
@@ -527,10 +726,26 @@ VoxCPMError gemv_launch(const voxq_gemv_item* items, int count, cudaStream_t st)
                 done[j] = true;
             }
         }
-        VoxCPMError e = (n == 1) ? launch_items<1>(sel, n, st) : launch_items<VOXQ_MAX_BATCH>(sel, n, st);
+        // each variant group gets its own part of the workspace
+        size_t need = 0;
+        for (int k = 0; k < n; k++)
+            if (sel[k]->w.K > 0 && sel[k]->M > 0)
+                need += (limb_bytes(sel[k]->M, sel[k]->w.K, sel[k]->w.qtype) + 255) & ~(size_t)255;
+        uint8_t* part = static_cast<uint8_t*>(ws) + used;
+        VoxCPMError e = (n == 1) ? launch_items<1>(sel, n, st, part, ws_bytes - used)
+                                 : launch_items<VOXQ_MAX_BATCH>(sel, n, st, part, ws_bytes - used);
         if (e) return e;
+        used += need;
     }
     return VOXCPM_SUCCESS;
+}
+
+VoxCPMError gemv_launch(const voxq_gemv_item* items, int count, cudaStream_t st) {
+    if (count < 0 || count > VOXQ_MAX_BATCH) return VOXCPM_ERR_UNSUPPORTED;
+    const size_t need = gemv_workspace_bytes(items, count);
+    void* ws = gemv_workspace(need);
+    if (!ws && need) return VOXCPM_ERR_OOM;
+    return gemv_launch_ws(items, count, st, ws, need);
 }
 
 // K == 0: the product is an empty sum (silu(0) * 0 == 0 for SwiGLU).

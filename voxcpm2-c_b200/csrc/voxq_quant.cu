@@ -244,7 +244,7 @@ extern "C" size_t voxq_codes_bytes(int N, int K, int qtype) {
 
 extern "C" size_t voxq_scales_bytes(int N, int K, int qtype) {
     if (qtype != VOXQ_Q4 && qtype != VOXQ_Q8) return 0;
-    return (size_t)N * (size_t)(K / VOXQ_QBLK) * (size_t)scale_bytes(qtype);
+    return trailer_bytes(N, K, qtype) + VOXQ_TRAILER_PAD;
 }
 
 static VoxCPMError check_qtype(int qtype) {
@@ -293,6 +293,8 @@ extern "C" VoxCPMError voxq_quantize_weight(const float* d_w, int N, int K, int 
     quantize_kernel<<<grid_for(nb, 128), 128, 0, (cudaStream_t)stream>>>(
         d_w, n, qtype, d_blocks, d_codes, reinterpret_cast<uint8_t*>(d_scales));
     VOXQ_CUDA_TRY(cudaGetLastError());
+    VOXQ_CUDA_TRY(cudaMemsetAsync(static_cast<uint8_t*>(d_scales) + trailer_bytes(N, K, qtype), 0, VOXQ_TRAILER_PAD,
+                                  (cudaStream_t)stream));
     return VOXCPM_SUCCESS;
 }
 
@@ -306,6 +308,8 @@ extern "C" VoxCPMError voxq_pack_blocks(const uint8_t* d_blocks, int N, int K, i
     pack_kernel<<<grid_for(nb, 256), 256, 0, (cudaStream_t)stream>>>(d_blocks, nb, qtype, d_codes,
                                                                       reinterpret_cast<uint8_t*>(d_scales), 0);
     VOXQ_CUDA_TRY(cudaGetLastError());
+    VOXQ_CUDA_TRY(cudaMemsetAsync(static_cast<uint8_t*>(d_scales) + trailer_bytes(N, K, qtype), 0, VOXQ_TRAILER_PAD,
+                                  (cudaStream_t)stream));
     return VOXCPM_SUCCESS;
 }
 

@@ -22,7 +22,7 @@
 namespace voxq {
 
 static constexpr int kMaxDev = 16;
-static constexpr int kSlots = 4;  // 0: activation, 1: output, 2: temp weight, 3: GEMM workspace
+static constexpr int kSlots = 5;  // 0: activation, 1: output, 2: temp weight, 3: GEMM workspace, 4: GEMV limbs
 
 struct QRec {
     void* base;      // one allocation: codes, then scales
@@ -119,6 +119,13 @@ void* workspace(size_t bytes) {
     cudaGetDevice(&d);
     std::lock_guard<std::mutex> lk(g_mu);
     return slot_get(g_dev[d], 3, bytes);
+}
+
+void* gemv_workspace(size_t bytes) {
+    int d = 0;
+    cudaGetDevice(&d);
+    std::lock_guard<std::mutex> lk(g_mu);
+    return slot_get(g_dev[d], 4, bytes);
 }
 
 static bool pinned_get(void** p, size_t* have, size_t bytes) {
