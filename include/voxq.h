@@ -157,7 +157,10 @@ VOXQ_API VoxCPMError voxq_dequantize(const uint8_t* d_src, size_t n, int qtype, 
  *   codes   Q8: uint8 [N][K]     (code of W[n][k] at n*K + k)
  *           Q4: uint8 [N][K/2]   (byte i of a row = code[2i] << 4 | code[2i+1])
  *   scales  Q8: float2 [N][K/32] (scale, min)   Q4: half2 [N][K/32] (scale, min)
- *           followed by 16 bytes of padding (the kernels read 16-byte windows)
+ *           then, at the next 16-byte boundary, float rowmul[N] = 2^e with
+ *           max_k |W[n][k]| * 2^e in [2^13, 2^14) (exact row scaling for the
+ *           fp16 tensor-core path; written by voxq_quantize_weight and
+ *           voxq_pack_blocks), then 16 bytes of padding
  * i.e. each quantize.py block split into its code bytes and its trailer.
  * Same bytes per weight as the block stream (1.25 / 0.625).  Both arrays must
  * be 16-byte aligned; allocate them with voxq_codes_bytes / voxq_scales_bytes. */

@@ -50,12 +50,13 @@ def test_sizes_and_layout_math():
     L = voxq.lib()
     assert L.voxq_codes_bytes(4096, 1024, voxq.Q8) == 4096 * 1024
     assert L.voxq_codes_bytes(4096, 1024, voxq.Q4) == 4096 * 512
-    # trailers plus 16 bytes of tail padding
-    assert L.voxq_scales_bytes(4096, 1024, voxq.Q8) == 4096 * 32 * 8 + 16
-    assert L.voxq_scales_bytes(4096, 1024, voxq.Q4) == 4096 * 32 * 4 + 16
-    # same bytes per weight as the block stream (1.25 / 0.625)
+    # trailers, a float row multiplier per row at a 16-byte boundary, 16 bytes of padding
+    assert L.voxq_scales_bytes(4096, 1024, voxq.Q8) == 4096 * 32 * 8 + 4 * 4096 + 16
+    assert L.voxq_scales_bytes(4096, 1024, voxq.Q4) == 4096 * 32 * 4 + 4 * 4096 + 16
+    assert L.voxq_scales_bytes(3, 32, voxq.Q4) == 16 + 12 + 16
+    # same block bytes per weight as the block stream (1.25 / 0.625)
     for qt in (voxq.Q4, voxq.Q8):
-        assert (L.voxq_codes_bytes(64, 1024, qt) + L.voxq_scales_bytes(64, 1024, qt) - 16
+        assert (L.voxq_codes_bytes(64, 1024, qt) + L.voxq_scales_bytes(64, 1024, qt) - 4 * 64 - 16
                 == L.voxq_quant_bytes(64 * 1024, qt))
 
 

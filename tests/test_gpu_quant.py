@@ -70,6 +70,16 @@ def test_packed_layout_roundtrip(qt, N, K):
     qw2 = voxq.QWeight.from_blocks(blocks, N, K, qt)
     assert torch.equal(qw.codes, qw2.codes) and torch.equal(qw.scales, qw2.scales)
     assert torch.equal(qw.to_blocks(), blocks)
+    # row multipliers: powers of two putting each row's largest |w| in [2^13, 2^14)
+    nb = K // 32
+    tb = N * nb * (4 if qt == voxq.Q4 else 8)
+    off = (tb + 15) // 16 * 16
+    rowmul = qw.scales[off:off + 4 * N].view(torch.float32).cpu().numpy()
+    wd = O.dequantize(blocks.cpu().numpy(), N * K, qt).reshape(N, K)
+    wmax = np.abs(wd).max(axis=1) * rowmul
+    mant, _ = np.frexp(rowmul)
+    assert np.all(mant == 0.5)
+    assert np.all((wmax < 2.0 ** 14) & ((wmax >= 2.0 ** 12) | (wmax == 0)))
 
 
 def test_quantize_rejects_bad_arguments():

@@ -37,12 +37,23 @@ __host__ __device__ inline int64_t codes_row_bytes(int K, int qtype) {
 }
 __host__ __device__ inline int scale_bytes(int qtype) { return qtype == VOXQ_Q4 ? 4 : 8; }
 __host__ __device__ inline int block_bytes(int qtype) { return qtype == VOXQ_Q4 ? 20 : 40; }
-// Trailer (scale, min) array of a packed weight, and the tail padding that the
-// scales buffer carries so 16-byte bulk-copy windows never leave it.
+// The scales buffer of a packed weight holds, in order:
+//   trailers  [N][K/32] (scale, min)
+//   rowmul    [N] float at the next 16-byte boundary: 2^e with
+//             max_k |w[n][k]| * 2^e in [2^13, 2^14), the exact power-of-two
+//             row scale the tensor-core path uses to stay in fp16 range
+//   16 bytes of padding, so 16-byte copy windows over the trailers never
+//   leave the buffer.
 __host__ __device__ inline size_t trailer_bytes(int N, int K, int qtype) {
     return (size_t)N * (size_t)(K / VOXQ_QBLK) * (size_t)scale_bytes(qtype);
 }
+__host__ __device__ inline size_t rowmul_offset(int N, int K, int qtype) {
+    return (trailer_bytes(N, K, qtype) + 15) & ~(size_t)15;
+}
 #define VOXQ_TRAILER_PAD 16
+__host__ __device__ inline size_t scales_buffer_bytes(int N, int K, int qtype) {
+    return rowmul_offset(N, K, qtype) + 4 * (size_t)N + VOXQ_TRAILER_PAD;
+}
 
 // ---------------------------------------------------------------------------
 // Device helpers

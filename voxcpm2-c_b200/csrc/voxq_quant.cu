@@ -221,6 +221,43 @@ __global__ void pack_kernel(const uint8_t* __restrict__ blocks, int64_t nb, int 
     }
 }
 
+// Per-row power-of-two multiplier of a packed weight (one warp per row): the
+// largest |q*scale+min| a block can produce is at q = 0 or q = max code (or
+// -128 when Q8 codes are read signed), so the row maximum comes from the
+// trailers alone.  rowmul = 2^e with rowmax * 2^e in [2^13, 2^14).
+__global__ void rowmul_kernel(const uint8_t* __restrict__ scales, int N, int K, int qtype, float* __restrict__ rowmul) {
+    const int lane = threadIdx.x & 31;
+    const int nblk = K / VOXQ_QBLK;
+    for (int n = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; n < N; n += (gridDim.x * blockDim.x) >> 5) {
+        float mx = 0.0f;
+        for (int b = lane; b < nblk; b += 32) {
+            float s, m;
+            if (qtype == VOXQ_Q4) {
+                const uint32_t t = reinterpret_cast<const uint32_t*>(scales)[(int64_t)n * nblk + b];
+                s = half_bits_to_float((uint16_t)(t & 0xffff));
+                m = half_bits_to_float((uint16_t)(t >> 16));
+            } else {
+                const float2 t = reinterpret_cast<const float2*>(scales)[(int64_t)n * nblk + b];
+                s = t.x;
+                m = t.y;
+            }
+            const float hi = qtype == VOXQ_Q4 ? 15.0f : 255.0f;
+            const float v = fmaxf(fmaxf(fabsf(m), fabsf(fmaf(hi, s, m))), qtype == VOXQ_Q8 ? fabsf(fmaf(-128.0f, s, m)) : 0.0f);
+            if (isfinite(v)) mx = fmaxf(mx, v);
+        }
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) {
+            float r = 1.0f;
+            if (mx > 0.0f) {
+                int e;
+                frexpf(mx, &e);  // mx in [2^(e-1), 2^e)
+                r = ldexpf(1.0f, min(max(14 - e, -120), 120));
+            }
+            rowmul[n] = r;
+        }
+    }
+}
+
 static int grid_for(int64_t work, int threads) {
     int64_t g = (work + threads - 1) / threads;
     if (g < 1) g = 1;
@@ -244,7 +281,7 @@ extern "C" size_t voxq_codes_bytes(int N, int K, int qtype) {
 
 extern "C" size_t voxq_scales_bytes(int N, int K, int qtype) {
     if (qtype != VOXQ_Q4 && qtype != VOXQ_Q8) return 0;
-    return trailer_bytes(N, K, qtype) + VOXQ_TRAILER_PAD;
+    return scales_buffer_bytes(N, K, qtype);
 }
 
 static VoxCPMError check_qtype(int qtype) {
@@ -277,8 +314,21 @@ static VoxCPMError check_packed(int N, int K, int qtype, const void* codes, cons
     if (check_qtype(qtype)) return VOXCPM_ERR_UNSUPPORTED;
     if (N < 0 || K < 0 || K % VOXQ_QBLK) return VOXCPM_ERR_SHAPE_MISMATCH;
     if ((N > 0 && K > 0) && (!codes || !scales)) return VOXCPM_ERR_INTERNAL;
-    if ((reinterpret_cast<uintptr_t>(codes) & 15) || (reinterpret_cast<uintptr_t>(scales) & 7))
+    if ((reinterpret_cast<uintptr_t>(codes) & 15) || (reinterpret_cast<uintptr_t>(scales) & 15))
         return VOXCPM_ERR_INTERNAL;
+    return VOXCPM_SUCCESS;
+}
+
+// Zeroes the gap and padding after the trailers and computes the row multipliers.
+static VoxCPMError finish_packed(void* d_scales, int N, int K, int qtype, cudaStream_t st) {
+    uint8_t* sc = static_cast<uint8_t*>(d_scales);
+    const size_t tb = trailer_bytes(N, K, qtype);
+    VOXQ_CUDA_TRY(cudaMemsetAsync(sc + tb, 0, scales_buffer_bytes(N, K, qtype) - tb, st));
+    if (N > 0 && K > 0) {
+        rowmul_kernel<<<grid_for((int64_t)N * 32, 256), 256, 0, st>>>(
+            sc, N, K, qtype, reinterpret_cast<float*>(sc + rowmul_offset(N, K, qtype)));
+        VOXQ_CUDA_TRY(cudaGetLastError());
+    }
     return VOXCPM_SUCCESS;
 }
 
@@ -293,9 +343,7 @@ extern "C" VoxCPMError voxq_quantize_weight(const float* d_w, int N, int K, int 
     quantize_kernel<<<grid_for(nb, 128), 128, 0, (cudaStream_t)stream>>>(
         d_w, n, qtype, d_blocks, d_codes, reinterpret_cast<uint8_t*>(d_scales));
     VOXQ_CUDA_TRY(cudaGetLastError());
-    VOXQ_CUDA_TRY(cudaMemsetAsync(static_cast<uint8_t*>(d_scales) + trailer_bytes(N, K, qtype), 0, VOXQ_TRAILER_PAD,
-                                  (cudaStream_t)stream));
-    return VOXCPM_SUCCESS;
+    return finish_packed(d_scales, N, K, qtype, (cudaStream_t)stream);
 }
 
 extern "C" VoxCPMError voxq_pack_blocks(const uint8_t* d_blocks, int N, int K, int qtype, uint8_t* d_codes,
@@ -308,9 +356,7 @@ extern "C" VoxCPMError voxq_pack_blocks(const uint8_t* d_blocks, int N, int K, i
     pack_kernel<<<grid_for(nb, 256), 256, 0, (cudaStream_t)stream>>>(d_blocks, nb, qtype, d_codes,
                                                                       reinterpret_cast<uint8_t*>(d_scales), 0);
     VOXQ_CUDA_TRY(cudaGetLastError());
-    VOXQ_CUDA_TRY(cudaMemsetAsync(static_cast<uint8_t*>(d_scales) + trailer_bytes(N, K, qtype), 0, VOXQ_TRAILER_PAD,
-                                  (cudaStream_t)stream));
-    return VOXCPM_SUCCESS;
+    return finish_packed(d_scales, N, K, qtype, (cudaStream_t)stream);
 }
 
 extern "C" VoxCPMError voxq_unpack_blocks(const uint8_t* d_codes, const void* d_scales, int N, int K, int qtype,
