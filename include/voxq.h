@@ -205,6 +205,23 @@ typedef struct {
 VOXQ_API VoxCPMError voxq_matmul_nt_q(const float* d_a, int M, int64_t lda, const voxq_qweight* w, float* d_out,
                              int64_t ldo, const voxq_epilogue* epi, void* stream);
 
+/* voxq_matmul_nt_q for M <= 8 activation rows that allocates no device memory.
+ * No counterpart in the reference.  For callers that cannot let the library
+ * allocate: engines that reserve their whole device-memory budget up front, or
+ * hosts that forbid device allocation after set-up because cudaMalloc /
+ * cudaFree can synchronise the device and stall a real-time audio stream.
+ * Its scratch is a fixed array of VOXQ_NOALLOC_SCRATCH_BYTES inside the
+ * library's own device image (every GPU that loads the library holds it until
+ * exit), which covers every shape the GEMV accepts (K <= 16384 for Q8, 32768
+ * for Q4).  Larger scratch needs -> VOXCPM_ERR_OOM; M > 8 ->
+ * VOXCPM_ERR_UNSUPPORTED.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) and clears its error word, so make
+ * that first call before any stream capture.  All calls share the one array:
+ * calls that overlap on the GPU (other streams, other host threads) race. */
+#define VOXQ_NOALLOC_SCRATCH_BYTES (512 * 1024)
+VOXQ_API VoxCPMError voxq_matmul_nt_q_noalloc(const float* d_a, int M, int64_t lda, const voxq_qweight* w,
+                                              float* d_out, int64_t ldo, const voxq_epilogue* epi, void* stream);
+
 /* Dense fp32 / fp16 weights (the reference's unquantized path,
  * src/tensor_cuda.cu:192-333), full fp32 arithmetic. */
 VOXQ_API VoxCPMError voxq_matmul_nt_dense(const float* d_a, int M, int64_t lda, const void* d_w, int w_is_fp16,

@@ -586,7 +586,8 @@ static size_t limb_bytes(int M, int K, int qtype) {
 // Launches the items that share (qtype, swiglu, signed): one limb prepass for
 // their distinct activations, then one GEMV grid.
 template <int MAXI>
-static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStream_t st, void* ws, size_t ws_bytes) {
+static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStream_t st, void* ws, size_t ws_bytes,
+                                int* err) {
     static thread_local GemvParams<MAXI> p;
     static thread_local LimbParams lp;
     const voxq_gemv_item& f = *sel[0];
@@ -657,7 +658,7 @@ static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStr
     if (c == 0) return VOXCPM_SUCCESS;
     p.count = c;
     p.total_tiles = tiles;
-    p.err = device_error_word();
+    p.err = err ? err : device_error_word();
 
     // limb prepass (several launches only if there are more than kMaxJobs activations)
     for (int a0 = 0; a0 < nact; a0 += kMaxJobs) {
@@ -704,7 +705,8 @@ size_t gemv_workspace_bytes(const voxq_gemv_item* items, int count) {
     return total;
 }
 
-VoxCPMError gemv_launch_ws(const voxq_gemv_item* items, int count, cudaStream_t st, void* ws, size_t ws_bytes) {
+VoxCPMError gemv_launch_ws(const voxq_gemv_item* items, int count, cudaStream_t st, void* ws, size_t ws_bytes,
+                           int* err) {
     if (count < 0 || count > VOXQ_MAX_BATCH) return VOXCPM_ERR_UNSUPPORTED;
     for (int i = 0; i < count; i++) {
         VoxCPMError e = validate_item(items[i]);
@@ -732,8 +734,8 @@ VoxCPMError gemv_launch_ws(const voxq_gemv_item* items, int count, cudaStream_t 
             if (sel[k]->w.K > 0 && sel[k]->M > 0)
                 need += (limb_bytes(sel[k]->M, sel[k]->w.K, sel[k]->w.qtype) + 255) & ~(size_t)255;
         uint8_t* part = static_cast<uint8_t*>(ws) + used;
-        VoxCPMError e = (n == 1) ? launch_items<1>(sel, n, st, part, ws_bytes - used)
-                                 : launch_items<VOXQ_MAX_BATCH>(sel, n, st, part, ws_bytes - used);
+        VoxCPMError e = (n == 1) ? launch_items<1>(sel, n, st, part, ws_bytes - used, err)
+                                 : launch_items<VOXQ_MAX_BATCH>(sel, n, st, part, ws_bytes - used, err);
         if (e) return e;
         used += need;
     }

@@ -18,9 +18,12 @@ bool pdl_enabled();
 // Grouped / single GEMV (voxq_gemv.cu).
 VoxCPMError validate_item(const voxq_gemv_item& x);
 VoxCPMError gemv_launch(const voxq_gemv_item* items, int count, cudaStream_t st);
-// Same with a caller-provided limb workspace of gemv_workspace_bytes() bytes.
+// Same with a caller-provided limb workspace of gemv_workspace_bytes() bytes
+// and, optionally, a caller-provided device error word (default: the
+// library's per-device word).
 size_t gemv_workspace_bytes(const voxq_gemv_item* items, int count);
-VoxCPMError gemv_launch_ws(const voxq_gemv_item* items, int count, cudaStream_t st, void* ws, size_t ws_bytes);
+VoxCPMError gemv_launch_ws(const voxq_gemv_item* items, int count, cudaStream_t st, void* ws, size_t ws_bytes,
+                           int* err = nullptr);
 VoxCPMError gemv_k0(const voxq_gemv_item& x, cudaStream_t st);
 
 // Tensor-core GEMM for M > 8 (voxq_gemm.cu).  `ws` is a device workspace of

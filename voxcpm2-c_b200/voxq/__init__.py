@@ -97,6 +97,7 @@ SIGNATURES = {
     "voxq_pack_blocks": ([_vp, _i, _i, _i, _vp, _vp, _vp], _i),
     "voxq_unpack_blocks": ([_vp, _vp, _i, _i, _i, _vp, _vp], _i),
     "voxq_matmul_nt_q": ([_vp, _i, _i64, C.POINTER(QWeightDesc), _vp, _i64, C.POINTER(Epilogue), _vp], _i),
+    "voxq_matmul_nt_q_noalloc": ([_vp, _i, _i64, C.POINTER(QWeightDesc), _vp, _i64, C.POINTER(Epilogue), _vp], _i),
     "voxq_matmul_nt_dense": ([_vp, _i, _i64, _vp, _i, _i, _i, _vp, _i64, _vp], _i),
     "voxq_gemv_batch": ([C.POINTER(GemvItem), _i, _vp], _i),
 }
