@@ -404,6 +404,52 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_c3(args, torch):
+    """BASELINE config 3 sweep (one JSON line per shape): K = 1024, N in {1024, 4096},
+    M in {16, 64, 256, 2048}, Q8 and Q4, one voxq_matmul_nt_q call per step.  Weight copies
+    are rotated so the weights of consecutive steps never share L2 (> 126 MB in total)."""
+    import voxq
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hbm, bf16, bf16s, peak_kind = peaks()
+    st = torch.cuda.Stream(dev)
+    K = 1024
+    g = torch.Generator(device=dev).manual_seed(3)
+    for qt in (voxq.Q8, voxq.Q4):
+        for N in (1024, 4096):
+            wbytes = int(N * K * (1.25 if qt == voxq.Q8 else 0.625))
+            copies = max(2, int(300e6 // wbytes) + 1)
+            ws = [voxq.QWeight.from_float(torch.randn(N, K, device=dev, generator=g) * 0.02, qt)
+                  for _ in range(copies)]
+            for M in (16, 64, 256, 2048):
+                a = torch.randn(M, K, device=dev, generator=g)
+                out = torch.empty(M, N, device=dev)
+                with torch.cuda.stream(st):
+                    for i in range(args.warmup):
+                        voxq.matmul_nt_q(a, ws[i % copies], out=out, stream=st)
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    reps = max(args.steps, copies)
+                    e0.record(st)
+                    for i in range(reps):
+                        voxq.matmul_nt_q(a, ws[i % copies], out=out, stream=st)
+                    e1.record(st)
+                torch.cuda.synchronize(dev)
+                ms = e0.elapsed_time(e1) / reps
+                flops = 2.0 * M * N * K
+                byts = wbytes + 4 * M * K + 4 * M * N
+                tf = flops / (ms * 1e-3) / 1e12
+                gbs = byts / (ms * 1e-3) / 1e9
+                ai = flops / byts
+                bound = "tensor" if ai > bf16 * 1e12 / (hbm * 1e9) else "hbm"
+                frac = tf / bf16 if bound == "tensor" else gbs / hbm
+                print(json.dumps({"config": "c3", "qtype": "q8" if qt == voxq.Q8 else "q4", "M": M, "N": N, "K": K,
+                                  "us": round(ms * 1e3, 2), "TFLOPs": round(tf, 1), "GBps": round(gbs, 1),
+                                  "bound": bound, "frac": round(frac, 4), "peak_kind": peak_kind,
+                                  "path": "gemv" if M <= 8 else "tcgen05 gemm", "weight_copies": copies}), flush=True)
+            del ws
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -413,8 +459,14 @@ def main():
     ap.add_argument("--soak", type=float, default=1.0, help="seconds of untimed load before timing (clock sampling)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-tensor-abi", dest="tensor_abi", action="store_false")
+    ap.add_argument("--config", default="c2", choices=["c2", "c3"],
+                    help="c2: the headline decode step (default); c3: GEMM sweep, one line per shape")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.config == "c3":
+        import torch
+        run_c3(args, torch)
+        return
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

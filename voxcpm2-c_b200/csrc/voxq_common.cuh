@@ -138,19 +138,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 enum : int { VOXQ_DEVERR_NONE = 0, VOXQ_DEVERR_WAIT_FULL = 1, VOXQ_DEVERR_WAIT_EMPTY = 2,
              VOXQ_DEVERR_WAIT_MMA = 3, VOXQ_DEVERR_WAIT_TMEM = 4 };
 
-// Spins on a barrier phase at most `limit` polls (about a second with the
-// back-off); returns false and records `site` when the phase never completes.
+// try_wait that lets the hardware suspend the warp (instead of spinning)
+// for up to `ns` nanoseconds while the phase is incomplete.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for a barrier phase for at most `limit` suspended polls of up to
+// 1 ms each (about a second); returns false and records `site` when the phase
+// never completes.  A waiting warp is parked by the hardware, so waiting costs
+// no issue slots of the warps doing the work.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int site, int* err,
-                                                  uint32_t limit = (1u << 24)) {
+                                                  uint32_t limit = 1000u) {
     if (mbar_try_wait(bar, parity)) return true;
     for (uint32_t i = 0; i < limit; i++) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (i > 64) {
-            // once any wait has given up, later waits return at once so a
-            // failing kernel ends quickly instead of timing out per wait
-            if (i == 65 && site != VOXQ_DEVERR_NONE && *reinterpret_cast<volatile int*>(err) != 0) return false;
-            __nanosleep(64);
-        }
+        if (mbar_try_wait_suspend(bar, parity, 1000000u)) return true;
+        // once any wait has given up, later waits return at once so a
+        // failing kernel ends quickly instead of timing out per wait
+        if (i == 2 && site != VOXQ_DEVERR_NONE && *reinterpret_cast<volatile int*>(err) != 0) return false;
     }
     if (site != VOXQ_DEVERR_NONE) atomicCAS(err, 0, site);
     return false;

@@ -14,16 +14,19 @@
 //
 // Orientation (swap-AB): the MMA's M dimension is 128 weight rows, its N
 // dimension BN activation rows, so skinny batches (M = 16 .. 256) still fill
-// the 128-lane accumulator.  One CTA computes a 128 x BN tile over all K:
-//   warp 0      TMA producer: raw code + trailer tiles (2-D tensor maps) into
-//               a 4-deep ring; fp16 activation tiles (128-byte swizzle) into
-//               the operand ring
-//   warp 1      allocates tensor memory and issues tcgen05.mma (one thread);
-//               tcgen05.commit releases operand stages and signals the end
-//   warps 2-9   dequantize codes -> fp16 straight into the UMMA K-major
-//               128-byte-swizzled layout (codes never touch HBM twice), then
-//               run the epilogue: tcgen05.ld, row/column scaling, bias /
-//               residual / SwiGLU, coalesced fp32 stores.
+// the 128-lane accumulator.  Persistent CTAs walk 128 x BN output tiles (tiles
+// sharing a weight slice are adjacent, so it is read from HBM once):
+//   warp 0       TMA producer: raw code + trailer tiles (2-D tensor maps) into
+//                a 4-deep ring, fp16 activation tiles (128-byte swizzle) into
+//                their own 4-deep ring
+//   warp 1       allocates tensor memory (two accumulators) and issues
+//                tcgen05.mma (one thread); tcgen05.commit releases stages and
+//                hands a finished accumulator to the epilogue
+//   warps 2-9    dequantize codes -> fp16 straight into the UMMA K-major
+//                128-byte-swizzled layout (3-deep ring)
+//   warps 10-13  epilogue: tcgen05.ld, row/column scaling, bias / residual /
+//                SwiGLU, coalesced fp32 stores -- overlapping the next tile's
+//                main loop through the second accumulator.
 // Every wait is bounded; a wait that gives up records the error word.
 #include <cuda.h>
 
@@ -37,9 +40,11 @@ namespace voxq {
 constexpr int kBM = 128;       // weight rows per tile (MMA M)
 constexpr int kBK = 64;        // fp16 K per operand stage (one 128-byte swizzle atom)
 constexpr int kRaw = 4;        // raw code/trailer stages
-constexpr int kOps = 3;        // operand stages
-constexpr int kDeqWarps = 8;   // dequant + epilogue warps
-constexpr int kThreads = (2 + kDeqWarps) * 32;
+constexpr int kOpsA = 3;       // fp16 weight operand stages
+constexpr int kOpsB = 4;       // fp16 activation operand stages
+constexpr int kDeqWarps = 8;   // dequant warps
+constexpr int kEpiWarps = 4;   // epilogue warps (one per tensor-memory lane quarter)
+constexpr int kThreads = (2 + kDeqWarps + kEpiWarps) * 32;
 constexpr int kRawCodes = kBM * 64;   // bytes: 128 rows x 64 code bytes
 constexpr int kRawTr = kBM * 16;      // bytes: 128 rows x 16 trailer bytes
 constexpr int kA16 = kBM * kBK * 2;   // 16 KB fp16 weight operand
@@ -145,76 +150,104 @@ struct GemmArgs {
     int* err;
 };
 
-// Dequantizes 8 codes of one row into one 16-byte chunk of fp16 (q*s' + m').
+// Dequantizes 8 codes of one row into one 16-byte chunk of fp16 (q*s' + m'),
+// fp32 arithmetic on packed pairs: codes become exact floats 2^23 + q by byte
+// permutes / masks, 2^23 comes off with add.f32x2, then fma.f32x2 and one
+// fp16x2 conversion per pair.
 template <int QT, bool SIGNED>
 __device__ __forceinline__ uint4 deq8(uint32_t lo, uint32_t hi, float s, float m) {
-    float q[8];
+    uint64_t w[4];
     if (QT == VOXQ_Q8) {
         const uint32_t x = SIGNED ? 0x80808080u : 0u;
         const uint32_t w0 = lo ^ x, w1 = hi ^ x;
-        const float off = SIGNED ? 8388736.0f : 8388608.0f;  // 2^23 (+128 for int8)
+        const uint64_t bias = SIGNED ? 0xCB000080CB000080ull : 0xCB000000CB000000ull;  // -(2^23 [+128])
+        const uint64_t S2 = pk(s, s), M2 = pk(m, m);
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            q[i] = __uint_as_float(__byte_perm(w0, 0x4B000000u, 0x7440 + i)) - off;
-            q[4 + i] = __uint_as_float(__byte_perm(w1, 0x4B000000u, 0x7440 + i)) - off;
+        for (int i = 0; i < 2; i++) {
+            const uint32_t v = i ? w1 : w0;
+            const float f0 = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7440));
+            const float f1 = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7441));
+            const float f2 = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7442));
+            const float f3 = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7443));
+            w[2 * i] = fma2(add2(pk(f0, f1), bias), S2, M2);
+            w[2 * i + 1] = fma2(add2(pk(f2, f3), bias), S2, M2);
         }
     } else {
-        // lo holds 4 bytes = 8 codes, byte i = code[2i] << 4 | code[2i+1]
+        // byte i = code[2i] << 4 | code[2i+1]: the even code stays in place as
+        // 16 * code and is scaled by s / 16 (exact)
+        const uint64_t bias = 0xCB000000CB000000ull;
+        const uint64_t S2 = pk(s * 0.0625f, s), M2 = pk(m, m);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            const uint32_t b = (lo >> (8 * i)) & 0xffu;
-            q[2 * i] = (float)(b >> 4);
-            q[2 * i + 1] = (float)(b & 15u);
+            const uint32_t v = __byte_perm(lo, 0x4B000000u, 0x7440 + i);  // 2^23 + byte
+            const float fe = __uint_as_float(v & 0x4B0000F0u);             // 2^23 + 16 * even
+            const float fo = __uint_as_float(v & 0x4B00000Fu);             // 2^23 + odd
+            w[i] = fma2(add2(pk(fe, fo), bias), S2, M2);
         }
     }
-    uint4 r;
-    __half2 h0 = __floats2half2_rn(fmaf(q[0], s, m), fmaf(q[1], s, m));
-    __half2 h1 = __floats2half2_rn(fmaf(q[2], s, m), fmaf(q[3], s, m));
-    __half2 h2 = __floats2half2_rn(fmaf(q[4], s, m), fmaf(q[5], s, m));
-    __half2 h3 = __floats2half2_rn(fmaf(q[6], s, m), fmaf(q[7], s, m));
-    r.x = *reinterpret_cast<uint32_t*>(&h0);
-    r.y = *reinterpret_cast<uint32_t*>(&h1);
-    r.z = *reinterpret_cast<uint32_t*>(&h2);
-    r.w = *reinterpret_cast<uint32_t*>(&h3);
-    return r;
+    uint32_t h[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        float a, b;
+        upk(w[i], a, b);
+        __half2 t = __floats2half2_rn(a, b);
+        h[i] = *reinterpret_cast<uint32_t*>(&t);
+    }
+    return make_uint4(h[0], h[1], h[2], h[3]);
 }
+
+// Ring position helper: slot and parity of the c-th use of a ring of S slots.
+struct Ring {
+    uint32_t c = 0;
+    template <int S>
+    __device__ __forceinline__ int slot() const { return (int)(c % S); }
+    template <int S>
+    __device__ __forceinline__ uint32_t phase() const { return (c / S) & 1u; }
+};
 
 template <int QT, int BN, bool SIGNED>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmArgs g) {
     constexpr int RK = (QT == VOXQ_Q4) ? 2 : 1;  // operand stages per raw stage
     constexpr int kB = BN * kBK * 2;             // fp16 activation operand bytes
-    constexpr int TCOLS = BN < 32 ? 32 : BN;     // tensor-memory columns (power of two >= 32)
+    constexpr int TC = BN < 32 ? 32 : BN;        // tensor-memory columns per accumulator
     constexpr uint32_t IDESC = umma_idesc(BN);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    // 1024-byte aligned carve-up: operand stages first (swizzle atoms need it)
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t* opA = base;                                  // kOps x 16 KB
-    uint8_t* opB = opA + kOps * kA16;                     // kOps x kB
-    uint8_t* raw = opB + kOps * kB;                       // kRaw x (codes + trailers)
-    __shared__ uint64_t full_raw[kRaw], empty_raw[kRaw], full_a[kOps], full_b[kOps], empty_op[kOps], done_bar;
+    uint8_t* opA = base;                 // kOpsA x 16 KB (fp16 weights, SW128)
+    uint8_t* opB = opA + kOpsA * kA16;   // kOpsB x kB (fp16 activations, SW128)
+    uint8_t* raw = opB + kOpsB * kB;     // kRaw x (codes + trailers)
+    __shared__ uint64_t full_raw[kRaw], empty_raw[kRaw], full_a[kOpsA], empty_a[kOpsA], full_b[kOpsB],
+        empty_b[kOpsB], acc_full[2], acc_empty[2];
     __shared__ uint32_t tmem_slot;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BN, n0 = blockIdx.y * kBM;
     const int KU = g.K / kBK;  // operand stages along K
+    const int mt = (g.M + BN - 1) / BN, ntl = (g.N + kBM - 1) / kBM;
+    const int tiles = mt * ntl;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kRaw; i++) {
             mbar_init(&full_raw[i], 1);
             mbar_init(&empty_raw[i], kDeqWarps);
         }
-        for (int i = 0; i < kOps; i++) {
+        for (int i = 0; i < kOpsA; i++) {
             mbar_init(&full_a[i], kDeqWarps);
-            mbar_init(&full_b[i], 1);
-            mbar_init(&empty_op[i], 1);
+            mbar_init(&empty_a[i], 1);
         }
-        mbar_init(&done_bar, 1);
+        for (int i = 0; i < kOpsB; i++) {
+            mbar_init(&full_b[i], 1);
+            mbar_init(&empty_b[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], kEpiWarps);
+        }
         mbar_fence_init();
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
-                     "r"(TCOLS)
+                     "r"(2 * TC)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -225,120 +258,163 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
+        // Weight tiles may stream before the kernel waits on its predecessor
+        // (the activation prepass of this call, which waited on its own
+        // predecessor before it let this kernel start); activation tiles may not.
         if (lane == 0) {
-            for (int u = 0; u < KU; u++) {
-                if (u % RK == 0) {
-                    const int r = u / RK, slot = r % kRaw;
-                    if (r >= kRaw) mbar_wait_bounded(&empty_raw[slot], ((r / kRaw) & 1) ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
-                    mbar_arrive_expect_tx(&full_raw[slot], kRawCodes + kRawTr);
-                    uint8_t* rs = raw + slot * (kRawCodes + kRawTr);
-                    tma_load_2d(rs, &g.tm_codes, r * 64, n0, &full_raw[slot]);
-                    tma_load_2d(rs + kRawCodes, &g.tm_tr, r * 16, n0, &full_raw[slot]);
+            Ring rr, rb;
+            bool waited = false;
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+                const int m0 = (t % mt) * BN, n0 = (t / mt) * kBM;
+                for (int u = 0; u < KU; u++) {
+                    if (u % RK == 0) {
+                        const int s = rr.slot<kRaw>();
+                        if (rr.c >= kRaw) mbar_wait_bounded(&empty_raw[s], rr.phase<kRaw>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
+                        mbar_arrive_expect_tx(&full_raw[s], kRawCodes + kRawTr);
+                        uint8_t* rs = raw + s * (kRawCodes + kRawTr);
+                        tma_load_2d(rs, &g.tm_codes, (u / RK) * 64, n0, &full_raw[s]);
+                        tma_load_2d(rs + kRawCodes, &g.tm_tr, (u / RK) * 16, n0, &full_raw[s]);
+                        rr.c++;
+                    }
+                    if (!waited) {
+                        pdl_wait();
+                        pdl_launch_dependents();
+                        waited = true;
+                    }
+                    const int s = rb.slot<kOpsB>();
+                    if (rb.c >= kOpsB) mbar_wait_bounded(&empty_b[s], rb.phase<kOpsB>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
+                    mbar_arrive_expect_tx(&full_b[s], kB);
+                    tma_load_2d(opB + s * kB, &g.tm_act, u * kBK, m0, &full_b[s]);
+                    rb.c++;
                 }
-                const int o = u % kOps;
-                if (u >= kOps) mbar_wait_bounded(&empty_op[o], ((u / kOps) & 1) ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
-                mbar_arrive_expect_tx(&full_b[o], kB);
-                tma_load_2d(opB + o * kB, &g.tm_act, u * kBK, m0, &full_b[o]);
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            for (int u = 0; u < KU; u++) {
-                const int o = u % kOps;
-                const uint32_t ph = (u / kOps) & 1;
-                mbar_wait_bounded(&full_a[o], ph, VOXQ_DEVERR_WAIT_FULL, g.err);
-                mbar_wait_bounded(&full_b[o], ph, VOXQ_DEVERR_WAIT_FULL, g.err);
+            Ring ra, rb;
+            int it = 0;
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
+                const int as = it & 1;
+                if (it >= 2) mbar_wait_bounded(&acc_empty[as], ((it >> 1) & 1) ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
                 tc_fence_after();
-                const uint64_t ad = umma_desc(opA + o * kA16);
-                const uint64_t bd = umma_desc(opB + o * kB);
+                const uint32_t acc = tmem + (uint32_t)(as * TC);
+                for (int u = 0; u < KU; u++) {
+                    const int sa = ra.slot<kOpsA>(), sb = rb.slot<kOpsB>();
+                    mbar_wait_bounded(&full_a[sa], ra.phase<kOpsA>(), VOXQ_DEVERR_WAIT_FULL, g.err);
+                    mbar_wait_bounded(&full_b[sb], rb.phase<kOpsB>(), VOXQ_DEVERR_WAIT_FULL, g.err);
+                    tc_fence_after();
+                    const uint64_t ad = umma_desc(opA + sa * kA16);
+                    const uint64_t bd = umma_desc(opB + sb * kB);
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; kk++)  // +32 bytes = 16 fp16 along K
-                    umma_f16(tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (u > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&empty_op[o]);
+                    for (int kk = 0; kk < kBK / 16; kk++)  // +32 bytes = 16 fp16 along K
+                        umma_f16(acc, ad + 2 * kk, bd + 2 * kk, IDESC, (u > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(&empty_a[sa]);
+                    umma_commit(&empty_b[sb]);
+                    ra.c++;
+                    rb.c++;
+                }
+                umma_commit(&acc_full[as]);
             }
-            umma_commit(&done_bar);
         }
-    } else {
-        // ---------------- dequant (then epilogue) ----------------
-        const int t = threadIdx.x - 64;  // 0 .. 255
-        const int j = t & 7;             // 16-byte chunk (8 codes) within the 64-wide row slice
-        float rmul[kBM / 32];
-#pragma unroll
-        for (int i = 0; i < kBM / 32; i++) {
-            const int n = n0 + t / 8 + 32 * i;
-            rmul[i] = n < g.N ? g.rowmul[n] : 1.0f;
-        }
-        for (int u = 0; u < KU; u++) {
-            const int r = u / RK, slot = r % kRaw, h = u % RK;
-            const int o = u % kOps;
-            if (h == 0) mbar_wait_bounded(&full_raw[slot], (r / kRaw) & 1, VOXQ_DEVERR_WAIT_FULL, g.err);
-            if (u >= kOps) mbar_wait_bounded(&empty_op[o], ((u / kOps) & 1) ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
-            const uint8_t* rc = raw + slot * (kRawCodes + kRawTr);
-            const uint8_t* rt = rc + kRawCodes;
-            uint8_t* dstA = opA + o * kA16;
+    } else if (warp < 2 + kDeqWarps) {
+        // ---------------- dequant ----------------
+        const int t8 = threadIdx.x - 64;  // 0 .. 255
+        const int j = t8 & 7;             // 16-byte chunk (8 codes) of the 64-wide K slice
+        // reads only weights (rowmul, codes via shared memory): no predecessor wait
+        Ring rr, ra;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+            const int n0 = (t / mt) * kBM;
+            float rmul[kBM / 32];
 #pragma unroll
             for (int i = 0; i < kBM / 32; i++) {
-                const int row = t / 8 + 32 * i;
-                float s, m;
-                uint32_t lo, hi = 0;
-                if (QT == VOXQ_Q8) {
-                    const uint2 c = *reinterpret_cast<const uint2*>(rc + row * 64 + 8 * j);
-                    lo = c.x;
-                    hi = c.y;
-                    const float2 tr = *reinterpret_cast<const float2*>(rt + row * 16 + 8 * (j >> 2));
-                    s = tr.x;
-                    m = tr.y;
-                } else {
-                    lo = *reinterpret_cast<const uint32_t*>(rc + row * 64 + 32 * h + 4 * j);
-                    const uint32_t tr = *reinterpret_cast<const uint32_t*>(rt + row * 16 + 4 * (2 * h + (j >> 2)));
-                    s = __half2float(__ushort_as_half((unsigned short)(tr & 0xffff)));
-                    m = __half2float(__ushort_as_half((unsigned short)(tr >> 16)));
-                }
-                const uint4 v = deq8<QT, SIGNED>(lo, hi, s * rmul[i], m * rmul[i]);
-                // K-major 128-byte swizzle: chunk j of row `row` lands at j ^ (row & 7)
-                *reinterpret_cast<uint4*>(dstA + row * 128 + ((j ^ (row & 7)) << 4)) = v;
+                const int n = n0 + t8 / 8 + 32 * i;
+                rmul[i] = n < g.N ? g.rowmul[n] : 1.0f;
             }
-            // make the generic-proxy writes visible to the tensor core
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&full_a[o]);
-                if (h == RK - 1) mbar_arrive(&empty_raw[slot]);
+            for (int u = 0; u < KU; u++) {
+                const int h = u % RK;
+                const int s = rr.slot<kRaw>();
+                if (h == 0) mbar_wait_bounded(&full_raw[s], rr.phase<kRaw>(), VOXQ_DEVERR_WAIT_FULL, g.err);
+                const int sa = ra.slot<kOpsA>();
+                if (ra.c >= kOpsA) mbar_wait_bounded(&empty_a[sa], ra.phase<kOpsA>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
+                const uint8_t* rc = raw + s * (kRawCodes + kRawTr);
+                const uint8_t* rt = rc + kRawCodes;
+                uint8_t* dstA = opA + sa * kA16;
+#pragma unroll
+                for (int i = 0; i < kBM / 32; i++) {
+                    const int row = t8 / 8 + 32 * i;
+                    float sc, mn;
+                    uint32_t lo, hi = 0;
+                    if (QT == VOXQ_Q8) {
+                        const uint2 c = *reinterpret_cast<const uint2*>(rc + row * 64 + 8 * j);
+                        lo = c.x;
+                        hi = c.y;
+                        const float2 tr = *reinterpret_cast<const float2*>(rt + row * 16 + 8 * (j >> 2));
+                        sc = tr.x;
+                        mn = tr.y;
+                    } else {
+                        lo = *reinterpret_cast<const uint32_t*>(rc + row * 64 + 32 * h + 4 * j);
+                        const float2 tr =
+                            __half22float2(*reinterpret_cast<const __half2*>(rt + row * 16 + 4 * (2 * h + (j >> 2))));
+                        sc = tr.x;
+                        mn = tr.y;
+                    }
+                    const uint4 v = deq8<QT, SIGNED>(lo, hi, sc * rmul[i], mn * rmul[i]);
+                    // K-major 128-byte swizzle: chunk j of row `row` lands at j ^ (row & 7)
+                    *reinterpret_cast<uint4*>(dstA + row * 128 + ((j ^ (row & 7)) << 4)) = v;
+                }
+                // make the generic-proxy writes visible to the tensor core
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&full_a[sa]);
+                    if (h == RK - 1) mbar_arrive(&empty_raw[s]);
+                }
+                ra.c++;
+                if (h == RK - 1) rr.c++;
             }
         }
-
+    } else {
         // ---------------- epilogue ----------------
-        mbar_wait_bounded(&done_bar, 0, VOXQ_DEVERR_WAIT_MMA, g.err);
-        tc_fence_after();
-        const int q = warp & 3;               // tensor-memory lane quarter of this warp
-        const int half = (warp - 2) >> 2;     // which half of the columns
-        const int nrow = n0 + q * 32 + lane;  // weight row = output column n
-        const bool nok = nrow < g.N;
-        const float rinv = nok ? 1.0f / g.rowmul[nrow] : 0.0f;
-        const float bias = (nok && g.bias) ? g.bias[nrow] : 0.0f;
-        constexpr int CH = BN / 2 < 16 ? 16 : BN / 2;  // columns per half
-        for (int c0 = half * CH; c0 < (half + 1) * CH && c0 < BN; c0 += 16) {
-            uint32_t v[16];
-            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        pdl_wait();  // row scales of the prepass; residual / output of earlier work
+        pdl_launch_dependents();
+        const int q = warp & 3;  // tensor-memory lane quarter of this warp
+        int it = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
+            const int m0 = (t % mt) * BN, n0 = (t / mt) * kBM;
+            const int as = it & 1;
+            mbar_wait_bounded(&acc_full[as], (it >> 1) & 1, VOXQ_DEVERR_WAIT_MMA, g.err);
+            tc_fence_after();
+            const int nrow = n0 + q * 32 + lane;  // weight row = output column n
+            const bool nok = nrow < g.N;
+            const float rinv = nok ? 1.0f / g.rowmul[nrow] : 0.0f;
+            const float bias = (nok && g.bias) ? g.bias[nrow] : 0.0f;
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * TC + c0), v);
 #pragma unroll
-            for (int i = 0; i < 16; i++) {
-                const int m = m0 + c0 + i;
-                if (m < g.M && nok) {
-                    float y = __uint_as_float(v[i]) * (rinv * g.ainv[m]);
-                    if (g.gate) y = silu_f(g.gate[(int64_t)m * g.ldg + nrow]) * y;
-                    y += bias;
-                    if (g.residual) y += g.residual[(int64_t)m * g.ldr + nrow];
-                    g.out[(int64_t)m * g.ldo + nrow] = y;
+                for (int i = 0; i < 16; i++) {
+                    const int m = m0 + c0 + i;
+                    if (m < g.M && nok) {
+                        float y = __uint_as_float(v[i]) * (rinv * g.ainv[m]);
+                        if (g.gate) y = silu_f(g.gate[(int64_t)m * g.ldg + nrow]) * y;
+                        y += bias;
+                        if (g.residual) y += g.residual[(int64_t)m * g.ldr + nrow];
+                        g.out[(int64_t)m * g.ldo + nrow] = y;
+                    }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[as]);
         }
     }
+    // dequant / epilogue roles touch global outputs only after the wait below
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TC) : "memory");
     }
 }
 
@@ -388,12 +464,22 @@ static int pick_bn(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 
 template <int QT, int BN, bool SIGNED>
 static VoxCPMError launch_gemm_t(const GemmArgs& a, cudaStream_t st) {
     constexpr int kB = BN * kBK * 2;
-    constexpr int smem = 1024 + kOps * (kA16 + kB) + kRaw * (kRawCodes + kRawTr);
+    constexpr int smem = 1024 + kOpsA * kA16 + kOpsB * kB + kRaw * (kRawCodes + kRawTr);
+    constexpr int TC = BN < 32 ? 32 : BN;
     auto kern = gemm_kernel<QT, BN, SIGNED>;
+    static int occ = 1;
     static std::once_flag once;
-    std::call_once(once, [&] { cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); });
+    std::call_once(once, [&] {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem);
+        const int tmem_cap = 512 / (2 * TC);  // co-resident CTAs must fit tensor memory
+        if (occ > tmem_cap) occ = tmem_cap;
+        if (occ < 1) occ = 1;
+    });
+    const int tiles = ((a.M + BN - 1) / BN) * ((a.N + kBM - 1) / kBM);
+    const int cap = device_sm_count() * occ;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((a.M + BN - 1) / BN, (a.N + kBM - 1) / kBM);
+    cfg.gridDim = dim3(tiles < cap ? tiles : cap);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;

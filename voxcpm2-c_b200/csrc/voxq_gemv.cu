@@ -367,7 +367,7 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32) gemv_kernel(const __gri
             if (*reinterpret_cast<volatile int*>(p.err) != 0) {
                 const int n = te - tb;
                 for (int j = (n > kStages ? n - kStages : 0); j < n; j++)
-                    mbar_wait_bounded(&full[j % kStages], (j / kStages) & 1, VOXQ_DEVERR_WAIT_FULL, p.err, 1u << 14);
+                    mbar_wait_bounded(&full[j % kStages], (j / kStages) & 1, VOXQ_DEVERR_WAIT_FULL, p.err, 20u);
             }
         }
         pdl_launch_dependents();
