@@ -72,6 +72,29 @@ __device__ __forceinline__ float4 ldg_f4(const float* p) {
     return __ldg(reinterpret_cast<const float4*>(p));
 }
 
+// Read-only load whose issue stays where it is written (an asm volatile is not
+// moved across other asm volatile statements, e.g. barrier waits), so a value
+// wanted later can be fetched ahead of a wait.  __ldg may be sunk to its use.
+__device__ __forceinline__ float ldg_ordered(const float* p) {
+    float r;
+    asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(r) : "l"(p));
+    return r;
+}
+
+// 16-byte global -> shared copy that completes asynchronously (cp.async
+// groups); both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(dst_smem))),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Packed fp32 pair arithmetic (sm_100 f32x2 forms).
 struct f2 {
     float x, y;
@@ -166,6 +189,24 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
         if (i == 2 && site != VOXQ_DEVERR_NONE && *reinterpret_cast<volatile int*>(err) != 0) return false;
     }
     if (site != VOXQ_DEVERR_NONE) atomicCAS(err, 0, site);
+    return false;
+}
+
+// Bounded wait for phases that are expected to take long (a whole main loop):
+// polls with a short sleep in between so the waiting warp leaves the issue
+// slots to the warps doing the work.  Gives up after about a second of clock.
+__device__ __forceinline__ bool mbar_wait_sleepy(uint64_t* bar, uint32_t parity, int site, int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (uint32_t i = 0;; i++) {
+        __nanosleep(200);
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63) == 63) {
+            if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+            if (clock64() - t0 > 2000000000ll) break;
+        }
+    }
+    atomicCAS(err, 0, site);
     return false;
 }
 

@@ -16,9 +16,11 @@
 // dimension BN activation rows, so skinny batches (M = 16 .. 256) still fill
 // the 128-lane accumulator.  Persistent CTAs walk 128 x BN output tiles (tiles
 // sharing a weight slice are adjacent, so it is read from HBM once):
-//   warp 0       TMA producer: raw code + trailer tiles (2-D tensor maps) into
-//                a 4-deep ring, fp16 activation tiles (128-byte swizzle) into
-//                their own 4-deep ring
+//   warp 0       producer: raw code (128-byte rows, 128-byte swizzle) + trailer
+//                tiles by 2-D TMA into a 3-deep ring, each raw stage feeding
+//                2 (Q8) or 4 (Q4) operand stages; fp16 activation stages, laid
+//                out by the prepass as ready shared-memory images, by one bulk
+//                copy each
 //   warp 1       allocates tensor memory (two accumulators) and issues
 //                tcgen05.mma (one thread); tcgen05.commit releases stages and
 //                hands a finished accumulator to the epilogue
@@ -30,6 +32,8 @@
 // Every wait is bounded; a wait that gives up records the error word.
 #include <cuda.h>
 
+#include <cstdint>
+#include <cstdlib>
 #include <mutex>
 
 #include "voxq_common.cuh"
@@ -37,50 +41,82 @@
 
 namespace voxq {
 
-constexpr int kBM = 128;       // weight rows per tile (MMA M)
-constexpr int kBK = 64;        // fp16 K per operand stage (one 128-byte swizzle atom)
-constexpr int kRaw = 4;        // raw code/trailer stages
-constexpr int kOpsA = 3;       // fp16 weight operand stages
-constexpr int kOpsB = 4;       // fp16 activation operand stages
-constexpr int kDeqWarps = 8;   // dequant warps
-constexpr int kEpiWarps = 4;   // epilogue warps (one per tensor-memory lane quarter)
+constexpr int kBM = 128;        // weight rows per tile (MMA M)
+constexpr int kBK = 64;         // fp16 K per operand stage (one 128-byte swizzle atom)
+constexpr int kOpsA = 3;        // fp16 weight operand stages
+constexpr int kDeqWarps = 8;    // dequant warps
+constexpr int kEpiWarps = 4;    // epilogue warps (one per tensor-memory lane quarter)
 constexpr int kThreads = (2 + kDeqWarps + kEpiWarps) * 32;
-constexpr int kRawCodes = kBM * 64;   // bytes: 128 rows x 64 code bytes
-constexpr int kRawTr = kBM * 16;      // bytes: 128 rows x 16 trailer bytes
-constexpr int kA16 = kBM * kBK * 2;   // 16 KB fp16 weight operand
+constexpr int kRawRow = 128;    // code bytes per row and raw stage (Q8: 128 K, Q4: 256 K)
+constexpr int kRawTrRow = 32;   // trailer bytes per row and raw stage (Q8: 4 blocks, Q4: 8 blocks)
+constexpr int kRawCodes = kBM * kRawRow;
+constexpr int kRawStage = kRawCodes + kBM * kRawTrRow;  // 20 KB, a multiple of 1024
+constexpr int kA16 = kBM * kBK * 2;  // 16 KB fp16 weight operand
+constexpr int kMaxBN = 256;
+// Ring depths by activation tile width.  A TMA load takes about a microsecond
+// to land, so each ring is as deep (bytes in flight) as shared memory allows:
+// fp16 activation operand stages, raw code/trailer stages.
+constexpr int ops_b(int bn) { return bn >= 256 ? 3 : bn >= 128 ? 5 : bn >= 64 ? 8 : 16; }
+constexpr int raw_stages(int bn) { return bn >= 256 ? 3 : bn >= 128 ? 4 : 5; }
 
 // ---------------------------------------------------------------------------
-// Activation prepass: fp32 rows -> fp16 rows scaled by a power of two.
-// One warp per row; ainv[m] = 2^-a.
+// Activation prepass: fp32 rows -> fp16 rows scaled by a power of two, written
+// as ready-made shared-memory images: for m-tile t (BN rows) and K stage u,
+// the BN x 64 fp16 block sits contiguously at ((t * KU + u) * BN) * 128 bytes
+// in the UMMA K-major 128-byte-swizzled order (16-byte chunk j of row r at
+// chunk j ^ (r & 7)), so the GEMM fetches it with one bulk copy.  Rows M ..
+// Mpad-1 are zero; ainv[m] = 2^-a (0 for pad rows).  One block per row, one
+// thread per 8 values, so a row costs one load latency, not K/128 of them.
 // ---------------------------------------------------------------------------
-__global__ void act_f16_kernel(const float* __restrict__ a, int M, int K, int64_t lda, __half* __restrict__ a16,
-                               float* __restrict__ ainv) {
+constexpr int kActThreads = 128;
+
+__global__ void __launch_bounds__(kActThreads) act_tile_kernel(const float* __restrict__ a, int M, int K, int64_t lda,
+                                                               int bn, uint8_t* __restrict__ a16t,
+                                                               float* __restrict__ ainv) {
     pdl_wait();
     pdl_launch_dependents();
-    const int lane = threadIdx.x & 31;
-    for (int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < M; m += (gridDim.x * blockDim.x) >> 5) {
-        const float* row = a + (int64_t)m * lda;
-        float mx = 0.0f;
-        for (int k = lane * 4; k < K; k += 128) {
-            const float4 v = *reinterpret_cast<const float4*>(row + k);
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    __shared__ float red[kActThreads / 32];
+    const int m = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int KU = K / kBK, nch = K / 8;
+    const bool live = m < M;
+    const float* row = a + (int64_t)m * lda;
+    float mx = 0.0f;
+    if (live) {
+        for (int c = threadIdx.x; c < nch; c += kActThreads) {
+            const float4 v0 = *reinterpret_cast<const float4*>(row + 8 * c);
+            const float4 v1 = *reinterpret_cast<const float4*>(row + 8 * c + 4);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))));
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
         }
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        int e = 0;
-        if (mx > 0.0f && isfinite(mx)) {
-            int x;
-            frexpf(mx, &x);
-            e = min(max(14 - x, -120), 120);
-        }
-        const float mul = ldexpf(1.0f, e);
-        __half2* dst = reinterpret_cast<__half2*>(a16 + (int64_t)m * K);
-        for (int k = lane * 4; k < K; k += 128) {
-            const float4 v = *reinterpret_cast<const float4*>(row + k);
-            dst[k / 2] = __floats2half2_rn(v.x * mul, v.y * mul);
-            dst[k / 2 + 1] = __floats2half2_rn(v.z * mul, v.w * mul);
-        }
-        if (lane == 0) ainv[m] = ldexpf(1.0f, -e);
     }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[wid] = mx;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kActThreads / 32; w++) mx = fmaxf(mx, red[w]);
+    int e = 0;
+    if (mx > 0.0f && isfinite(mx)) {
+        int x;
+        frexpf(mx, &x);
+        e = min(max(14 - x, -120), 120);
+    }
+    const float mul = ldexpf(1.0f, e);
+    const int t = m / bn, r = m % bn;
+    uint8_t* tb = a16t + ((int64_t)t * KU * bn + r) * 128;
+    for (int c = threadIdx.x; c < nch; c += kActThreads) {
+        uint4 h = make_uint4(0u, 0u, 0u, 0u);
+        if (live) {
+            const float4 v0 = *reinterpret_cast<const float4*>(row + 8 * c);
+            const float4 v1 = *reinterpret_cast<const float4*>(row + 8 * c + 4);
+            __half2 p0 = __floats2half2_rn(v0.x * mul, v0.y * mul), p1 = __floats2half2_rn(v0.z * mul, v0.w * mul);
+            __half2 p2 = __floats2half2_rn(v1.x * mul, v1.y * mul), p3 = __floats2half2_rn(v1.z * mul, v1.w * mul);
+            h = make_uint4(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1),
+                           *reinterpret_cast<uint32_t*>(&p2), *reinterpret_cast<uint32_t*>(&p3));
+        }
+        const int u = c >> 3, j = c & 7;  // K stage, 16-byte chunk
+        *reinterpret_cast<uint4*>(tb + (int64_t)u * bn * 128 + ((j ^ (r & 7)) << 4)) = h;
+    }
+    if (threadIdx.x == 0) ainv[m] = live ? ldexpf(1.0f, -e) : 0.0f;
 }
 
 // ---------------------------------------------------------------------------
@@ -135,17 +171,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
 struct GemmArgs {
-    CUtensorMap tm_codes;   // u8 [N][rowb], box {64, 128}
-    CUtensorMap tm_tr;      // u8 [N][srow], box {16, 128}
-    CUtensorMap tm_act;     // f16 [M][K], box {64, BN}, 128-byte swizzle
+    CUtensorMap tm_codes;   // u8 [N][rowb], box {128, 128}, 128-byte swizzle
+    CUtensorMap tm_tr;      // u8 [N][srow], box {32, 128}
+    const uint8_t* a16t;    // tiled fp16 activation images (act_tile_kernel)
     const float* rowmul;    // [N]
-    const float* ainv;      // [M]
+    const float* ainv;      // [Mpad]
     float* out;
     const float* bias;
     const float* residual;
     const float* gate;      // SwiGLU: out = silu(gate) * (A W^T)
+    float* part;            // split-K partial accumulators [tiles][S][BN][128]
     int64_t ldo, ldr, ldg;
     int M, N, K;
+    int S, KUs;             // K splits per tile, operand stages per split
     int q8_signed;
     int* err;
 };
@@ -205,26 +243,41 @@ struct Ring {
     __device__ __forceinline__ uint32_t phase() const { return (c / S) & 1u; }
 };
 
+// Epilogue value for output row m (a tile column) and column n (this lane).
+__device__ __forceinline__ float epi_value(const GemmArgs& g, float acc, float scale, float bias, int64_t m, int n) {
+    float y = acc * scale;
+    if (g.gate) y = silu_f(__ldg(g.gate + m * g.ldg + n)) * y;
+    y += bias;
+    if (g.residual) y += __ldg(g.residual + m * g.ldr + n);
+    return y;
+}
+
 template <int QT, int BN, bool SIGNED>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmArgs g) {
-    constexpr int RK = (QT == VOXQ_Q4) ? 2 : 1;  // operand stages per raw stage
+    constexpr int RK = (QT == VOXQ_Q4) ? 4 : 2;  // operand stages per raw stage
+    constexpr int OB = ops_b(BN);
+    constexpr int kRaw = raw_stages(BN);
     constexpr int kB = BN * kBK * 2;             // fp16 activation operand bytes
     constexpr int TC = BN < 32 ? 32 : BN;        // tensor-memory columns per accumulator
     constexpr uint32_t IDESC = umma_idesc(BN);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    // 1024-byte aligned base, derived from the shared array by pointer arithmetic so
+    // every access below stays a shared-memory access
+    uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* opA = base;                 // kOpsA x 16 KB (fp16 weights, SW128)
-    uint8_t* opB = opA + kOpsA * kA16;   // kOpsB x kB (fp16 activations, SW128)
-    uint8_t* raw = opB + kOpsB * kB;     // kRaw x (codes + trailers)
-    __shared__ uint64_t full_raw[kRaw], empty_raw[kRaw], full_a[kOpsA], empty_a[kOpsA], full_b[kOpsB],
-        empty_b[kOpsB], acc_full[2], acc_empty[2];
+    uint8_t* opB = opA + kOpsA * kA16;   // OB x kB (fp16 activations, SW128)
+    uint8_t* raw = opB + OB * kB;        // kRaw x (codes SW128 + trailers)
+    __shared__ uint64_t full_raw[kRaw], empty_raw[kRaw], full_a[kOpsA], empty_a[kOpsA], full_b[OB], empty_b[OB],
+        acc_full[2], acc_empty[2];
     __shared__ uint32_t tmem_slot;
+    __shared__ __align__(16) float ainv_s[kEpiWarps][2][kMaxBN];  // epilogue: activation row scales
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KU = g.K / kBK;  // operand stages along K
     const int mt = (g.M + BN - 1) / BN, ntl = (g.N + kBM - 1) / kBM;
-    const int tiles = mt * ntl;
+    const int S = g.S, KUs = g.KUs;
+    const int units = mt * ntl * S;  // unit w: tile w / S, K split w % S
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kRaw; i++) {
@@ -235,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             mbar_init(&full_a[i], kDeqWarps);
             mbar_init(&empty_a[i], 1);
         }
-        for (int i = 0; i < kOpsB; i++) {
+        for (int i = 0; i < OB; i++) {
             mbar_init(&full_b[i], 1);
             mbar_init(&empty_b[i], 1);
         }
@@ -256,158 +309,254 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
 
+    // The producer and MMA roles run their loops on the whole warp (every lane
+    // takes the same waits, lane 0 alone issues), so each warp stays converged
+    // and meets the final CTA barrier as one.
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- producer ----------------
         // Weight tiles may stream before the kernel waits on its predecessor
         // (the activation prepass of this call, which waited on its own
         // predecessor before it let this kernel start); activation tiles may not.
         if (lane == 0) {
-            Ring rr, rb;
-            bool waited = false;
-            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-                const int m0 = (t % mt) * BN, n0 = (t / mt) * kBM;
-                for (int u = 0; u < KU; u++) {
-                    if (u % RK == 0) {
-                        const int s = rr.slot<kRaw>();
-                        if (rr.c >= kRaw) mbar_wait_bounded(&empty_raw[s], rr.phase<kRaw>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
-                        mbar_arrive_expect_tx(&full_raw[s], kRawCodes + kRawTr);
-                        uint8_t* rs = raw + s * (kRawCodes + kRawTr);
-                        tma_load_2d(rs, &g.tm_codes, (u / RK) * 64, n0, &full_raw[s]);
-                        tma_load_2d(rs + kRawCodes, &g.tm_tr, (u / RK) * 16, n0, &full_raw[s]);
-                        rr.c++;
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&g.tm_codes)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&g.tm_tr)) : "memory");
+        }
+        Ring rr, rb;
+        bool waited = false;
+        for (int w = blockIdx.x; w < units; w += gridDim.x) {
+            const int t = w / S, u0 = (w % S) * KUs, u1 = min(KU, u0 + KUs);
+            const int mi = t % mt, n0 = (t / mt) * kBM;
+            const uint8_t* bsrc = g.a16t + (size_t)mi * KU * kB;
+            for (int u = u0; u < u1; u++) {
+                if ((u - u0) % RK == 0) {  // u0 is a multiple of RK
+                    const int s = rr.slot<kRaw>();
+                    if (rr.c >= kRaw) mbar_wait_bounded(&empty_raw[s], rr.phase<kRaw>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(&full_raw[s], kRawStage);
+                        uint8_t* rs = raw + s * kRawStage;
+                        tma_load_2d(rs, &g.tm_codes, (u / RK) * kRawRow, n0, &full_raw[s]);
+                        tma_load_2d(rs + kRawCodes, &g.tm_tr, (u / RK) * kRawTrRow, n0, &full_raw[s]);
                     }
-                    if (!waited) {
-                        pdl_wait();
-                        pdl_launch_dependents();
-                        waited = true;
-                    }
-                    const int s = rb.slot<kOpsB>();
-                    if (rb.c >= kOpsB) mbar_wait_bounded(&empty_b[s], rb.phase<kOpsB>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
-                    mbar_arrive_expect_tx(&full_b[s], kB);
-                    tma_load_2d(opB + s * kB, &g.tm_act, u * kBK, m0, &full_b[s]);
-                    rb.c++;
+                    __syncwarp();
+                    rr.c++;
                 }
+                if (!waited) {
+                    pdl_wait();
+                    pdl_launch_dependents();
+                    waited = true;
+                }
+                const int s = rb.slot<OB>();
+                if (rb.c >= OB) mbar_wait_bounded(&empty_b[s], rb.phase<OB>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full_b[s], kB);
+                    bulk_g2s(opB + s * kB, bsrc + (size_t)u * kB, kB, &full_b[s]);
+                }
+                __syncwarp();
+                rb.c++;
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            Ring ra, rb;
-            int it = 0;
-            for (int t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
-                const int as = it & 1;
-                if (it >= 2) mbar_wait_bounded(&acc_empty[as], ((it >> 1) & 1) ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
+        Ring ra, rb;
+        int it = 0;
+        for (int w = blockIdx.x; w < units; w += gridDim.x, it++) {
+            const int u0 = (w % S) * KUs, u1 = min(KU, u0 + KUs);
+            const int as = it & 1;
+            if (it >= 2) mbar_wait_bounded(&acc_empty[as], ((it >> 1) & 1) ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
+            tc_fence_after();
+            const uint32_t acc = tmem + (uint32_t)(as * TC);
+            for (int u = u0; u < u1; u++) {
+                const int sa = ra.slot<kOpsA>(), sb = rb.slot<OB>();
+                mbar_wait_bounded(&full_a[sa], ra.phase<kOpsA>(), VOXQ_DEVERR_WAIT_FULL, g.err);
+                mbar_wait_bounded(&full_b[sb], rb.phase<OB>(), VOXQ_DEVERR_WAIT_FULL, g.err);
                 tc_fence_after();
-                const uint32_t acc = tmem + (uint32_t)(as * TC);
-                for (int u = 0; u < KU; u++) {
-                    const int sa = ra.slot<kOpsA>(), sb = rb.slot<kOpsB>();
-                    mbar_wait_bounded(&full_a[sa], ra.phase<kOpsA>(), VOXQ_DEVERR_WAIT_FULL, g.err);
-                    mbar_wait_bounded(&full_b[sb], rb.phase<kOpsB>(), VOXQ_DEVERR_WAIT_FULL, g.err);
-                    tc_fence_after();
+                if (lane == 0) {
                     const uint64_t ad = umma_desc(opA + sa * kA16);
                     const uint64_t bd = umma_desc(opB + sb * kB);
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; kk++)  // +32 bytes = 16 fp16 along K
-                        umma_f16(acc, ad + 2 * kk, bd + 2 * kk, IDESC, (u > 0 || kk > 0) ? 1u : 0u);
+                        umma_f16(acc, ad + 2 * kk, bd + 2 * kk, IDESC, (u > u0 || kk > 0) ? 1u : 0u);
                     umma_commit(&empty_a[sa]);
                     umma_commit(&empty_b[sb]);
-                    ra.c++;
-                    rb.c++;
                 }
-                umma_commit(&acc_full[as]);
+                __syncwarp();
+                ra.c++;
+                rb.c++;
             }
+            if (lane == 0) umma_commit(&acc_full[as]);
+            __syncwarp();
         }
     } else if (warp < 2 + kDeqWarps) {
         // ---------------- dequant ----------------
-        const int t8 = threadIdx.x - 64;  // 0 .. 255
-        const int j = t8 & 7;             // 16-byte chunk (8 codes) of the 64-wide K slice
+        // Raw codes arrive 128-byte swizzled (16-byte chunk c of row r at
+        // c ^ (r & 7)).  Thread -> (row, chunk): lane group g = lane / 8 takes row
+        // b + {0, 4, 2, 6}[g] (+ 32 i), b = 8 (w / 2) + (w % 2) for dequant warp w.
+        // The rows a half-warp reads then differ by 4 in (row & 7) (Q8: disjoint
+        // swizzled chunk sets) and the 4 rows of a warp have distinct (row & 7) / 2
+        // (Q4), so the shared-memory reads are free of bank conflicts.
+        const int dw = warp - 2;
+        const int j = lane & 7;  // 16-byte chunk (8 K values) of the 64-wide operand stage
+        const int r0 = 8 * (dw >> 1) + (dw & 1) + ((0x6240 >> (4 * (lane >> 3))) & 0xF);
         // reads only weights (rowmul, codes via shared memory): no predecessor wait
         Ring rr, ra;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-            const int n0 = (t / mt) * kBM;
+        // row multipliers of the next unit's tile are fetched one unit ahead
+        float rnext[kBM / 32];
+#pragma unroll
+        for (int i = 0; i < kBM / 32; i++) {
+            const int n = (blockIdx.x / S / mt) * kBM + r0 + 32 * i;
+            rnext[i] = n < g.N ? ldg_ordered(g.rowmul + n) : 1.0f;
+        }
+        for (int w = blockIdx.x; w < units; w += gridDim.x) {
+            const int u0 = (w % S) * KUs, u1 = min(KU, u0 + KUs);
             float rmul[kBM / 32];
+            const int wn = w + gridDim.x;
 #pragma unroll
             for (int i = 0; i < kBM / 32; i++) {
-                const int n = n0 + t8 / 8 + 32 * i;
-                rmul[i] = n < g.N ? g.rowmul[n] : 1.0f;
+                rmul[i] = rnext[i];
+                const int n = (wn / S / mt) * kBM + r0 + 32 * i;
+                rnext[i] = (wn < units && n < g.N) ? ldg_ordered(g.rowmul + n) : 1.0f;
             }
-            for (int u = 0; u < KU; u++) {
-                const int h = u % RK;
+            for (int u = u0; u < u1; u++) {
+                const int h = (u - u0) % RK;
+                const bool last_use = (h == RK - 1) || (u == u1 - 1);
                 const int s = rr.slot<kRaw>();
                 if (h == 0) mbar_wait_bounded(&full_raw[s], rr.phase<kRaw>(), VOXQ_DEVERR_WAIT_FULL, g.err);
                 const int sa = ra.slot<kOpsA>();
                 if (ra.c >= kOpsA) mbar_wait_bounded(&empty_a[sa], ra.phase<kOpsA>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
-                const uint8_t* rc = raw + s * (kRawCodes + kRawTr);
+                const uint8_t* rc = raw + s * kRawStage;
                 const uint8_t* rt = rc + kRawCodes;
                 uint8_t* dstA = opA + sa * kA16;
+                const int blk = 2 * h + (j >> 2);  // 32-value block index within the raw stage
 #pragma unroll
                 for (int i = 0; i < kBM / 32; i++) {
-                    const int row = t8 / 8 + 32 * i;
+                    const int row = r0 + 32 * i;
+                    const int sw = row & 7;
                     float sc, mn;
                     uint32_t lo, hi = 0;
                     if (QT == VOXQ_Q8) {
-                        const uint2 c = *reinterpret_cast<const uint2*>(rc + row * 64 + 8 * j);
+                        // logical bytes 64 h + 8 j .. +8: chunk 4 h + j / 2, half j & 1
+                        const uint2 c = *reinterpret_cast<const uint2*>(rc + row * kRawRow +
+                                                                        (((4 * h + (j >> 1)) ^ sw) << 4) + 8 * (j & 1));
                         lo = c.x;
                         hi = c.y;
-                        const float2 tr = *reinterpret_cast<const float2*>(rt + row * 16 + 8 * (j >> 2));
+                        const float2 tr = *reinterpret_cast<const float2*>(rt + row * kRawTrRow + 8 * blk);
                         sc = tr.x;
                         mn = tr.y;
                     } else {
-                        lo = *reinterpret_cast<const uint32_t*>(rc + row * 64 + 32 * h + 4 * j);
-                        const float2 tr =
-                            __half22float2(*reinterpret_cast<const __half2*>(rt + row * 16 + 4 * (2 * h + (j >> 2))));
+                        // logical bytes 32 h + 4 j .. +4: chunk 2 h + j / 4, word j & 3
+                        lo = *reinterpret_cast<const uint32_t*>(rc + row * kRawRow + (((2 * h + (j >> 2)) ^ sw) << 4) +
+                                                                4 * (j & 3));
+                        const float2 tr = __half22float2(*reinterpret_cast<const __half2*>(rt + row * kRawTrRow + 4 * blk));
                         sc = tr.x;
                         mn = tr.y;
                     }
                     const uint4 v = deq8<QT, SIGNED>(lo, hi, sc * rmul[i], mn * rmul[i]);
                     // K-major 128-byte swizzle: chunk j of row `row` lands at j ^ (row & 7)
-                    *reinterpret_cast<uint4*>(dstA + row * 128 + ((j ^ (row & 7)) << 4)) = v;
+                    *reinterpret_cast<uint4*>(dstA + row * 128 + ((j ^ sw) << 4)) = v;
                 }
                 // make the generic-proxy writes visible to the tensor core
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&full_a[sa]);
-                    if (h == RK - 1) mbar_arrive(&empty_raw[s]);
+                    if (last_use) mbar_arrive(&empty_raw[s]);
                 }
                 ra.c++;
-                if (h == RK - 1) rr.c++;
+                if (last_use) rr.c++;
             }
         }
     } else {
         // ---------------- epilogue ----------------
-        pdl_wait();  // row scales of the prepass; residual / output of earlier work
+        pdl_wait();  // row scales of the prepass; residual / gate / output of earlier work
         pdl_launch_dependents();
         const int q = warp & 3;  // tensor-memory lane quarter of this warp
+        float* ainv_w = &ainv_s[q][0][0];
+        // The tile's activation row scales go to shared memory by cp.async one
+        // unit ahead (ainv is padded to whole tiles); column scale and bias one
+        // unit ahead in registers.  Nothing the loop needs is fetched after the
+        // accumulator wait.
+#define VOXQ_EPI_FETCH(W, BUF)                                                                                   \
+    do {                                                                                                         \
+        const int fw = (W);                                                                                      \
+        if (fw < units) {                                                                                        \
+            const int ft = fw / S;                                                                               \
+            const int fm0 = (ft % mt) * BN, fn = (ft / mt) * kBM + q * 32 + lane;                                \
+            for (int c = lane; c < BN / 4; c += 32)                                                              \
+                cp_async16(ainv_w + (BUF) * kMaxBN + 4 * c, g.ainv + fm0 + 4 * c);                               \
+            rm_next = fn < g.N ? ldg_ordered(g.rowmul + fn) : 1.0f;                                              \
+            b_next = (fn < g.N && g.bias) ? ldg_ordered(g.bias + fn) : 0.0f;                                     \
+        }                                                                                                        \
+        cp_async_commit();                                                                                       \
+    } while (0)
+        float rm_next = 1.0f, b_next = 0.0f;
+        VOXQ_EPI_FETCH(blockIdx.x, 0);
         int it = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
+        for (int w = blockIdx.x; w < units; w += gridDim.x, it++) {
+            const int t = w / S, sp = w % S;
             const int m0 = (t % mt) * BN, n0 = (t / mt) * kBM;
             const int as = it & 1;
-            mbar_wait_bounded(&acc_full[as], (it >> 1) & 1, VOXQ_DEVERR_WAIT_MMA, g.err);
-            tc_fence_after();
             const int nrow = n0 + q * 32 + lane;  // weight row = output column n
             const bool nok = nrow < g.N;
-            const float rinv = nok ? 1.0f / g.rowmul[nrow] : 0.0f;
-            const float bias = (nok && g.bias) ? g.bias[nrow] : 0.0f;
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                uint32_t v[16];
-                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * TC + c0), v);
+            const float rinv = 1.0f / rm_next;
+            const float bias = b_next;
+            VOXQ_EPI_FETCH(w + gridDim.x, as ^ 1);
+            const int mlim = nok ? min(BN, g.M - m0) : 0;  // valid rows of this tile for this lane
+            const float* arow = ainv_w + as * kMaxBN;
+            const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * TC);
+            mbar_wait_sleepy(&acc_full[as], (it >> 1) & 1, VOXQ_DEVERR_WAIT_MMA, g.err);
+            tc_fence_after();
+            cp_async_wait<1>();  // this unit's row scales (the next unit's may be in flight)
+            __syncwarp();
+            if (S == 1) {
+                // kept as a loop: a fully unrolled epilogue thrashes the instruction cache
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(tacc + (uint32_t)c0, v);
+                    float am[16];
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    const int m = m0 + c0 + i;
-                    if (m < g.M && nok) {
-                        float y = __uint_as_float(v[i]) * (rinv * g.ainv[m]);
-                        if (g.gate) y = silu_f(g.gate[(int64_t)m * g.ldg + nrow]) * y;
-                        y += bias;
-                        if (g.residual) y += g.residual[(int64_t)m * g.ldr + nrow];
-                        g.out[(int64_t)m * g.ldo + nrow] = y;
+                    for (int i = 0; i < 4; i++) {
+                        const float4 x = *reinterpret_cast<const float4*>(arow + c0 + 4 * i);
+                        am[4 * i] = x.x;
+                        am[4 * i + 1] = x.y;
+                        am[4 * i + 2] = x.z;
+                        am[4 * i + 3] = x.w;
+                    }
+                    float* o = g.out + (int64_t)(m0 + c0) * g.ldo + nrow;
+                    if (!g.gate && !g.residual) {
+#pragma unroll
+                        for (int i = 0; i < 16; i++)
+                            if (c0 + i < mlim) o[(int64_t)i * g.ldo] = __uint_as_float(v[i]) * (rinv * am[i]) + bias;
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; i++)
+                            if (c0 + i < mlim)
+                                o[(int64_t)i * g.ldo] =
+                                    epi_value(g, __uint_as_float(v[i]), rinv * am[i], bias, m0 + c0 + i, nrow);
                     }
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[as]);
+            } else {
+                // Split K: park the raw partial sum ([BN][128] per unit) for the
+                // reduction kernel, which adds the S partials in split order and
+                // applies the epilogue.
+                float* pp = g.part + ((size_t)(t * S + sp) * BN) * kBM + q * 32 + lane;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(tacc + (uint32_t)c0, v);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) pp[(c0 + i) * kBM] = __uint_as_float(v[i]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[as]);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[as]);
         }
+        cp_async_wait<0>();
+#undef VOXQ_EPI_FETCH
     }
     // dequant / epilogue roles touch global outputs only after the wait below
     tc_fence_before();
@@ -415,6 +564,43 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TC) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Split-K reduction: out[m, n] = epilogue(sum over splits k = 0 .. S-1 of
+// part[t][k][m - m0][n - n0]), the splits added in order (deterministic).  One
+// thread per 4 consecutive columns of one row; float4 loads of the partials.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const __grid_constant__ GemmArgs g, int bn) {
+    pdl_wait();  // the GEMM's partials
+    pdl_launch_dependents();
+    const int mt = (g.M + bn - 1) / bn;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over tiles x bn x 32
+    const int c4 = (int)(idx & 31);
+    const int64_t rt = idx >> 5;
+    const int c = (int)(rt % bn);
+    const int t = (int)(rt / bn);
+    const int m = (t % mt) * bn + c, n = (t / mt) * kBM + 4 * c4;
+    if (t >= mt * ((g.N + kBM - 1) / kBM) || m >= g.M || n >= g.N) return;
+    const float* p = g.part + ((size_t)t * g.S * bn + c) * kBM + 4 * c4;
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(p));
+    for (int k = 1; k < g.S; k++) {
+        const float4 x = __ldcg(reinterpret_cast<const float4*>(p + (size_t)k * bn * kBM));
+        acc.x += x.x;
+        acc.y += x.y;
+        acc.z += x.z;
+        acc.w += x.w;
+    }
+    const float am = g.ainv[m];
+    const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int nn = n + i;
+        if (nn < g.N) {
+            const float bias = g.bias ? g.bias[nn] : 0.0f;
+            g.out[(int64_t)m * g.ldo + nn] = epi_value(g, a4[i], am / g.rowmul[nn], bias, m, nn);
+        }
     }
 }
 
@@ -452,19 +638,76 @@ static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, ui
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-static size_t act_bytes(int M, int K) { return align256((size_t)M * K * 2) + align256((size_t)M * 4); }
+static int64_t pad_rows(int M) { return ((int64_t)M + kMaxBN - 1) / kMaxBN * kMaxBN; }
 
-size_t gemm_workspace_bytes(int M, int N, int K, bool swiglu) {
-    // fp16 activations + their row scales (+ the SwiGLU gate result)
-    return act_bytes(M, K) + (swiglu ? align256((size_t)M * N * 4) : 0);
+static size_t act_bytes(int M, int K) {
+    return align256((size_t)pad_rows(M) * K * 2) + align256((size_t)pad_rows(M) * 4);
 }
 
-static int pick_bn(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256; }
+// Launch plan.  A 128 x N x 16 tcgen05.mma takes the same time for every
+// N <= 256 (about 128 cycles), so a tile is as wide as the batch allows (BN =
+// 256 once M > 128).  When the tiles cannot fill the SMs, the K range of each
+// tile may be split over S CTAs (whole raw stages each); a reduction kernel then
+// adds the S partials.  S minimises a simple model: per-CTA operand stages at
+// ~0.3 us + pipeline fill, plus for S > 1 the partial traffic at ~4 TB/s and a
+// launch.  VOXQ_GEMM_BN / VOXQ_GEMM_SPLIT override (tuning).
+struct GemmPlan {
+    int bn, S, KUs, tiles;
+};
+
+static int env_int(const char* name) {
+    const char* e = getenv(name);
+    return e ? atoi(e) : 0;
+}
+
+static GemmPlan plan_gemm(int M, int N, int K, int qt) {
+    static const int forced_bn = env_int("VOXQ_GEMM_BN"), forced_s = env_int("VOXQ_GEMM_SPLIT");
+    GemmPlan p;
+    if (forced_bn == 16 || forced_bn == 32 || forced_bn == 64 || forced_bn == 128 || forced_bn == 256) {
+        p.bn = forced_bn;
+    } else {
+        p.bn = 16;
+        while (p.bn < M && p.bn < kMaxBN) p.bn *= 2;
+    }
+    const int KU = K / kBK, RK = (qt == VOXQ_Q4) ? 4 : 2;
+    p.tiles = ((M + p.bn - 1) / p.bn) * ((N + kBM - 1) / kBM);
+    const int sms = device_sm_count();
+    const int smax = KU / RK > 1 ? KU / RK : 1;
+    double best = 1e30;
+    p.S = 1;
+    p.KUs = KU;
+    for (int s = 1; s <= smax; s++) {
+        if (forced_s > 0 && s != (forced_s < smax ? forced_s : smax)) continue;
+        int kus = (KU + s - 1) / s;
+        kus = (kus + RK - 1) / RK * RK;
+        const int S = (KU + kus - 1) / kus;
+        const int64_t units = (int64_t)p.tiles * S;
+        const int64_t per_cta = (units + sms - 1) / sms;
+        double t = (double)per_cta * kus * 0.3 + 1.5;
+        if (S > 1) t += 1.0 + 2.0 * S * p.tiles * p.bn * kBM * 4.0 / 4.0e6;
+        if (t < best - 1e-9) {
+            best = t;
+            p.S = S;
+            p.KUs = kus;
+        }
+    }
+    return p;
+}
+
+static size_t part_bytes(const GemmPlan& p) {
+    return p.S > 1 ? align256((size_t)p.S * p.tiles * p.bn * kBM * 4) : 0;
+}
+
+size_t gemm_workspace_bytes(int M, int N, int K, int qtype, bool swiglu) {
+    // tiled fp16 activations + row scales, split-K partials (+ the SwiGLU gate result)
+    const GemmPlan p = plan_gemm(M, N, K, qtype);
+    return act_bytes(M, K) + part_bytes(p) + (swiglu ? align256((size_t)M * N * 4) : 0);
+}
 
 template <int QT, int BN, bool SIGNED>
 static VoxCPMError launch_gemm_t(const GemmArgs& a, cudaStream_t st) {
     constexpr int kB = BN * kBK * 2;
-    constexpr int smem = 1024 + kOpsA * kA16 + kOpsB * kB + kRaw * (kRawCodes + kRawTr);
+    constexpr int smem = 1024 + kOpsA * kA16 + ops_b(BN) * kB + raw_stages(BN) * kRawStage;
     constexpr int TC = BN < 32 ? 32 : BN;
     auto kern = gemm_kernel<QT, BN, SIGNED>;
     static int occ = 1;
@@ -476,10 +719,10 @@ static VoxCPMError launch_gemm_t(const GemmArgs& a, cudaStream_t st) {
         if (occ > tmem_cap) occ = tmem_cap;
         if (occ < 1) occ = 1;
     });
-    const int tiles = ((a.M + BN - 1) / BN) * ((a.N + kBM - 1) / kBM);
+    const int units = ((a.M + BN - 1) / BN) * ((a.N + kBM - 1) / kBM) * a.S;
     const int cap = device_sm_count() * occ;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(tiles < cap ? tiles : cap);
+    cfg.gridDim = dim3(units < cap ? units : cap);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -536,37 +779,58 @@ static VoxCPMError gemm_by_rows(const float* a, int M, int64_t lda, const voxq_q
     return VOXCPM_SUCCESS;
 }
 
-// One GEMM launch: out = epilogue(A W^T) with optional gate (SwiGLU second half).
-static VoxCPMError gemm_one(const float* ainv, const __half* a16, int M, const voxq_qweight* w, float* out,
-                            int64_t ldo, const float* bias, const float* residual, int64_t ldr, const float* gate,
-                            int64_t ldg, cudaStream_t st) {
+static void pdl_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, cudaStream_t st) {
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+}
+
+// One GEMM (+ split-K reduction): out = epilogue(A W^T) with optional gate
+// (SwiGLU second half).
+static VoxCPMError gemm_one(const GemmPlan& pl, const float* ainv, const uint8_t* a16t, int M, const voxq_qweight* w,
+                            float* out, int64_t ldo, const float* bias, const float* residual, int64_t ldr,
+                            const float* gate, int64_t ldg, float* part, cudaStream_t st) {
     const int N = w->N, K = w->K, qt = w->qtype;
-    const int bn = pick_bn(M);
     static thread_local GemmArgs ga;
     const uint64_t rowb = (uint64_t)codes_row_bytes(K, qt);
     const uint64_t srow = (uint64_t)(K / VOXQ_QBLK) * scale_bytes(qt);
-    if (!make_map(&ga.tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->codes, rowb, (uint64_t)N, rowb, 64, kBM,
-                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map(&ga.tm_tr, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->scales, srow, (uint64_t)N, srow, 16, kBM,
-                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map(&ga.tm_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kBK,
-                  (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!make_map(&ga.tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->codes, rowb, (uint64_t)N, rowb, kRawRow, kBM,
+                  CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&ga.tm_tr, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->scales, srow, (uint64_t)N, srow, kRawTrRow, kBM,
+                  CU_TENSOR_MAP_SWIZZLE_NONE))
         return VOXCPM_ERR_INTERNAL;
+    ga.a16t = a16t;
     ga.rowmul = reinterpret_cast<const float*>(static_cast<const uint8_t*>(w->scales) + rowmul_offset(N, K, qt));
     ga.ainv = ainv;
     ga.out = out;
     ga.bias = bias;
     ga.residual = residual;
     ga.gate = gate;
+    ga.part = part;
     ga.ldo = ldo;
     ga.ldr = ldr;
     ga.ldg = ldg;
     ga.M = M;
     ga.N = N;
     ga.K = K;
+    ga.S = pl.S;
+    ga.KUs = pl.KUs;
     ga.q8_signed = w->q8_signed;
     ga.err = device_error_word();
-    return qt == VOXQ_Q4 ? launch_bn<VOXQ_Q4>(ga, bn, false, st) : launch_bn<VOXQ_Q8>(ga, bn, w->q8_signed != 0, st);
+    const int bn = pl.bn;
+    VoxCPMError e =
+        qt == VOXQ_Q4 ? launch_bn<VOXQ_Q4>(ga, bn, false, st) : launch_bn<VOXQ_Q8>(ga, bn, w->q8_signed != 0, st);
+    if (e || pl.S == 1) return e;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    const int64_t threads = (int64_t)pl.tiles * bn * 32;
+    cfg.gridDim = dim3((unsigned)((threads + 255) / 256));
+    cfg.blockDim = dim3(256);
+    pdl_config(cfg, attr, st);
+    VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, splitk_reduce_kernel, ga, bn));
+    return VOXCPM_SUCCESS;
 }
 
 VoxCPMError gemm_launch(const float* a, int M, int64_t lda, const voxq_qweight* w, float* out, int64_t ldo,
@@ -579,33 +843,32 @@ VoxCPMError gemm_launch(const float* a, int M, int64_t lda, const voxq_qweight* 
         return gemm_by_rows(a, M, lda, w, out, ldo, epi, st);
     if ((reinterpret_cast<uintptr_t>(w->codes) & 15) || (reinterpret_cast<uintptr_t>(w->scales) & 15))
         return VOXCPM_ERR_UNSUPPORTED;
+    const GemmPlan pl = plan_gemm(M, N, K, w->qtype);
+    const int mpad = (M + pl.bn - 1) / pl.bn * pl.bn;
+    // workspace: a16t | ainv | split-K partials | SwiGLU gate
     uint8_t* wsb = static_cast<uint8_t*>(ws);
-    __half* a16 = reinterpret_cast<__half*>(wsb);
-    float* ainv = reinterpret_cast<float*>(wsb + align256((size_t)M * K * 2));
+    uint8_t* a16t = wsb;
+    float* ainv = reinterpret_cast<float*>(wsb + align256((size_t)pad_rows(M) * K * 2));
+    float* part = reinterpret_cast<float*>(wsb + act_bytes(M, K));
+    float* gbuf = reinterpret_cast<float*>(wsb + act_bytes(M, K) + part_bytes(pl));
     {
         cudaLaunchConfig_t cfg = {};
-        const int blocks = (M + 7) / 8;
-        cfg.gridDim = dim3(blocks < 1 ? 1 : blocks);
-        cfg.blockDim = dim3(256);
-        cfg.stream = st;
         cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, act_f16_kernel, a, M, K, lda, a16, ainv));
+        cfg.gridDim = dim3(mpad);
+        cfg.blockDim = dim3(kActThreads);
+        pdl_config(cfg, attr, st);
+        VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, act_tile_kernel, a, M, K, lda, pl.bn, a16t, ainv));
     }
     const float* bias = epi ? epi->bias : nullptr;
     const float* res = epi ? epi->residual : nullptr;
     const int64_t ldr = epi ? epi->ldr : 0;
     if (epi && epi->up) {
         // SwiGLU: gate into the workspace, then up with silu(gate) * y fused
-        float* gbuf = reinterpret_cast<float*>(wsb + act_bytes(M, K));
-        VoxCPMError e = gemm_one(ainv, a16, M, w, gbuf, N, nullptr, nullptr, 0, nullptr, 0, st);
+        VoxCPMError e = gemm_one(pl, ainv, a16t, M, w, gbuf, N, nullptr, nullptr, 0, nullptr, 0, part, st);
         if (e) return e;
-        return gemm_one(ainv, a16, M, epi->up, out, ldo, bias, res, ldr, gbuf, N, st);
+        return gemm_one(pl, ainv, a16t, M, epi->up, out, ldo, bias, res, ldr, gbuf, N, part, st);
     }
-    return gemm_one(ainv, a16, M, w, out, ldo, bias, res, ldr, nullptr, 0, st);
+    return gemm_one(pl, ainv, a16t, M, w, out, ldo, bias, res, ldr, nullptr, 0, part, st);
 }
 
 }  // namespace voxq

@@ -27,8 +27,8 @@ VoxCPMError gemv_launch_ws(const voxq_gemv_item* items, int count, cudaStream_t 
 VoxCPMError gemv_k0(const voxq_gemv_item& x, cudaStream_t st);
 
 // Tensor-core GEMM for M > 8 (voxq_gemm.cu).  `ws` is a device workspace of
-// at least gemm_workspace_bytes(M, N, K, swiglu) bytes, 256-byte aligned.
-size_t gemm_workspace_bytes(int M, int N, int K, bool swiglu);
+// at least gemm_workspace_bytes(M, N, K, qtype, swiglu) bytes, 256-byte aligned.
+size_t gemm_workspace_bytes(int M, int N, int K, int qtype, bool swiglu);
 VoxCPMError gemm_launch(const float* a, int M, int64_t lda, const voxq_qweight* w, float* out, int64_t ldo,
                         const voxq_epilogue* epi, void* ws, cudaStream_t st);
 

@@ -216,7 +216,7 @@ extern "C" VoxCPMError voxq_matmul_nt_q(const float* d_a, int M, int64_t lda, co
         }
         return gemv_launch(&it, 1, st);
     }
-    void* ws = workspace(gemm_workspace_bytes(M, w->N, w->K, up != nullptr));
+    void* ws = workspace(gemm_workspace_bytes(M, w->N, w->K, w->qtype, up != nullptr));
     if (!ws) return VOXCPM_ERR_OOM;
     return gemm_launch(d_a, M, lda, w, d_out, ldo, epi, ws, st);
 }
@@ -473,7 +473,7 @@ extern "C" VoxCPMError tensor_matmul_nt_cuda(const Tensor* a, const Tensor* b, T
         const QRec& q = qit->second;
         voxq_qweight w = {q.codes, q.scales, q.N, q.K, q.qtype, 0};
         if (M > 8) {
-            void* ws = slot_get(*s, 3, gemm_workspace_bytes(M, N, K, false));
+            void* ws = slot_get(*s, 3, gemm_workspace_bytes(M, N, K, q.qtype, false));
             if (!ws) return VOXCPM_ERR_OOM;
             lk.unlock();
             e = gemm_launch(d_a, M, K, &w, d_o, N, nullptr, ws, st);
