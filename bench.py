@@ -190,7 +190,9 @@ def run_ours(args, torch, dist, rank, world, local_rank):
     traffic = None
     tp = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(tp):
-        traffic = json.load(open(tp)).get("gemv_c2_q4")
+        t = json.load(open(tp)).get("gemv_c2_q4")
+        if t:  # dram__bytes_read.sum + dram__bytes_write.sum of one launch (ncu)
+            traffic = t["dram_read_bytes"] + t["dram_write_bytes"]
 
     if rank == 0:
         line = {
@@ -217,7 +219,7 @@ def run_ours(args, torch, dist, rank, world, local_rank):
                          "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
                          "traffic": traffic, "kernel": "voxq::gemv_kernel<Q4,1,8,...,192>"},
             "e2e": e2e,
-            "gpu_launches": args.steps,
+            "gpu_launches": 2 * args.steps,  # per step: limb prepass + grouped GEMV
             "clocks": sampler.summary(),
         }
         if e2e_abi is not None:
@@ -406,8 +408,13 @@ def run_reference(args, rank, world):
 
 def run_c3(args, torch):
     """BASELINE config 3 sweep (one JSON line per shape): K = 1024, N in {1024, 4096},
-    M in {16, 64, 256, 2048}, Q8 and Q4, one voxq_matmul_nt_q call per step.  Weight copies
-    are rotated so the weights of consecutive steps never share L2 (> 126 MB in total)."""
+    M in {16, 64, 256, 2048}, Q8 and Q4, one voxq_matmul_nt_q call per step.
+
+    `us` is device time per call: the calls (prepass, GEMM and any split-K reduction
+    kernel each) are captured in a CUDA graph and replayed, so host launch cost is
+    excluded; `us_eager` is the same loop launched from Python call by call.  Weight
+    copies are rotated so the weights of consecutive calls never share L2 (> 126 MB
+    in total)."""
     import voxq
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -415,27 +422,55 @@ def run_c3(args, torch):
     st = torch.cuda.Stream(dev)
     K = 1024
     g = torch.Generator(device=dev).manual_seed(3)
+    only = None
+    if args.shape:  # "M,N,q8|q4": one shape (profiling)
+        m_, n_, q_ = args.shape.split(",")
+        only = (int(m_), int(n_), voxq.Q8 if q_.lower() == "q8" else voxq.Q4)
     for qt in (voxq.Q8, voxq.Q4):
         for N in (1024, 4096):
+            if only and (qt != only[2] or N != only[1]):
+                continue
             wbytes = int(N * K * (1.25 if qt == voxq.Q8 else 0.625))
-            copies = max(2, int(300e6 // wbytes) + 1)
+            # rotate > 300 MB of weights (no L2 reuse); a single profiled shape uses 4 copies
+            copies = 4 if only else max(2, int(300e6 // wbytes) + 1)
             ws = [voxq.QWeight.from_float(torch.randn(N, K, device=dev, generator=g) * 0.02, qt)
                   for _ in range(copies)]
             for M in (16, 64, 256, 2048):
+                if only and M != only[0]:
+                    continue
                 a = torch.randn(M, K, device=dev, generator=g)
                 out = torch.empty(M, N, device=dev)
+                reps = max(copies, 64)
                 with torch.cuda.stream(st):
-                    for i in range(args.warmup):
+                    for i in range(max(args.warmup, 3)):
                         voxq.matmul_nt_q(a, ws[i % copies], out=out, stream=st)
-                    e0 = torch.cuda.Event(enable_timing=True)
-                    e1 = torch.cuda.Event(enable_timing=True)
-                    reps = max(args.steps, copies)
+                torch.cuda.synchronize(dev)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=st):
+                    for i in range(reps):
+                        voxq.matmul_nt_q(a, ws[i % copies], out=out, stream=st)
+                with torch.cuda.stream(st):
+                    graph.replay()
+                torch.cuda.synchronize(dev)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                loops = max(1, args.steps // reps)
+                with torch.cuda.stream(st):  # replay() launches on the current stream
+                    e0.record(st)
+                    for _ in range(loops):
+                        graph.replay()
+                    e1.record(st)
+                torch.cuda.synchronize(dev)
+                ms = e0.elapsed_time(e1) / (loops * reps)
+                del graph
+                with torch.cuda.stream(st):
                     e0.record(st)
                     for i in range(reps):
                         voxq.matmul_nt_q(a, ws[i % copies], out=out, stream=st)
                     e1.record(st)
                 torch.cuda.synchronize(dev)
-                ms = e0.elapsed_time(e1) / reps
+                ms_eager = e0.elapsed_time(e1) / reps
+                err = voxq.lib().voxq_device_error(1)
                 flops = 2.0 * M * N * K
                 byts = wbytes + 4 * M * K + 4 * M * N
                 tf = flops / (ms * 1e-3) / 1e12
@@ -444,9 +479,11 @@ def run_c3(args, torch):
                 bound = "tensor" if ai > bf16 * 1e12 / (hbm * 1e9) else "hbm"
                 frac = tf / bf16 if bound == "tensor" else gbs / hbm
                 print(json.dumps({"config": "c3", "qtype": "q8" if qt == voxq.Q8 else "q4", "M": M, "N": N, "K": K,
-                                  "us": round(ms * 1e3, 2), "TFLOPs": round(tf, 1), "GBps": round(gbs, 1),
-                                  "bound": bound, "frac": round(frac, 4), "peak_kind": peak_kind,
-                                  "path": "gemv" if M <= 8 else "tcgen05 gemm", "weight_copies": copies}), flush=True)
+                                  "us": round(ms * 1e3, 2), "us_eager": round(ms_eager * 1e3, 2),
+                                  "TFLOPs": round(tf, 1), "GBps": round(gbs, 1), "bound": bound,
+                                  "frac": round(frac, 4), "peak_kind": peak_kind,
+                                  "path": "gemv" if M <= 8 else "tcgen05 gemm", "weight_copies": copies,
+                                  "device_error": err}), flush=True)
             del ws
 
 
@@ -459,6 +496,7 @@ def main():
     ap.add_argument("--soak", type=float, default=1.0, help="seconds of untimed load before timing (clock sampling)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-tensor-abi", dest="tensor_abi", action="store_false")
+    ap.add_argument("--shape", default="", help="c3 only: one shape 'M,N,q8|q4'")
     ap.add_argument("--config", default="c2", choices=["c2", "c3"],
                     help="c2: the headline decode step (default); c3: GEMM sweep, one line per shape")
     args = ap.parse_args()
