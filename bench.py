@@ -406,6 +406,54 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_c1(args, torch):
+    """one Q8 GEMV, W [4096, 1024] = 0.02 N(0,1) quantized on device, x [1, 1024]
+    N(0,1), y [1, 4096].  The weight fits in L2, so 64 weight copies (> 335 MB) are rotated and the
+    calls are replayed from a CUDA graph (device time per call; host launch cost excluded)."""
+    import voxq
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hbm, bf16, bf16s, peak_kind = peaks()
+    st = torch.cuda.Stream(dev)
+    N, K, copies = 4096, 1024, 64
+    g = torch.Generator(device=dev).manual_seed(1)
+    ws = [voxq.QWeight.from_float(torch.randn(N, K, device=dev, generator=g) * 0.02, voxq.Q8) for _ in range(copies)]
+    x = torch.randn(1, K, device=dev, generator=g)
+    y = torch.empty(1, N, device=dev)
+    with torch.cuda.stream(st):
+        for i in range(max(args.warmup, 3)):
+            voxq.matmul_nt_q(x, ws[i % copies], out=y, stream=st)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        for i in range(copies):
+            voxq.matmul_nt_q(x, ws[i], out=y, stream=st)
+    loops = max(1, args.steps // copies)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        graph.replay()
+        e0.record(st)
+        for _ in range(loops):
+            graph.replay()
+        e1.record(st)
+    torch.cuda.synchronize(dev)
+    calls = loops * copies
+    ms = e0.elapsed_time(e1) / calls
+    byts = N * K * 5 // 4 + 4 * K + 4 * N  # 5,263,360 B
+    gbs = byts / (ms * 1e-3) / 1e9
+    print(json.dumps({"metric": "c1_q8_gemv_hbm_GBps", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
+                      "steps": calls, "warmup": max(args.warmup, 3), "us_per_call": round(ms * 1e3, 3),
+                      "higher_is_better": True, "dtype": "q8 weights, fp32 activations/accumulate",
+                      "data": "synthetic: 0.02*N(0,1) weights quantized on device to Q8, N(0,1) activation",
+                      "config": {"workload": "BASELINE config 1: Q8 GEMV N=4096 K=1024",
+                                 "algorithmic_bytes_per_call": byts, "weight_copies": copies,
+                                 "l2": "64 rotated weight copies (335 MB > L2)"},
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                   "frac": round(gbs / hbm, 4), "peak_kind": peak_kind},
+                      "gpu_launches": 2 * calls, "device_error": voxq.lib().voxq_device_error(1)}), flush=True)
+
+
 def run_c3(args, torch):
     """BASELINE config 3 sweep (one JSON line per shape): K = 1024, N in {1024, 4096},
     M in {16, 64, 256, 2048}, Q8 and Q4, one voxq_matmul_nt_q call per step.
@@ -497,13 +545,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-tensor-abi", dest="tensor_abi", action="store_false")
     ap.add_argument("--shape", default="", help="c3 only: one shape 'M,N,q8|q4'")
-    ap.add_argument("--config", default="c2", choices=["c2", "c3"],
-                    help="c2: the headline decode step (default); c3: GEMM sweep, one line per shape")
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3"],
+                    help="c2: the headline decode step (default); c1: one Q8 GEMV; c3: GEMM sweep, one line per shape")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.config == "c3":
+    if args.config in ("c1", "c3"):
         import torch
-        run_c3(args, torch)
+        (run_c1 if args.config == "c1" else run_c3)(args, torch)
         return
 
     rank = int(os.environ.get("RANK", "0"))

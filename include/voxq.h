@@ -134,6 +134,14 @@ VOXQ_API VoxCPMError voxq_set_device(int device);
  * the word.  Returns -1 if the word cannot be read. */
 VOXQ_API int voxq_device_error(int clear);
 
+/* Failure-detection self-test (no counterpart in the reference): launches one
+ * kernel that waits, through the same bounded wait the GEMV/GEMM kernels use,
+ * on a barrier that nothing ever completes, giving up after `polls` suspended
+ * polls of at most 1 ms.  Returns the device error code the kernel recorded
+ * (expected: 1, full-stage wait) and clears it, or a negative VoxCPMError if
+ * the launch failed.  The context stays usable; no fault is raised. */
+VOXQ_API int voxq_selftest_wait_timeout(int polls);
+
 /* Bytes of the quantize.py block stream for n elements: ceil(n/32) blocks of
  * 20 (Q4) or 40 (Q8) bytes (scripts/quantize.py:88-104 without its 20-byte
  * tensor header). */
