@@ -285,7 +285,7 @@ __device__ __forceinline__ void chunk_dot(const uint32_t (&ca)[NW][RG][(QT == VO
     for (int w = 0; w < NW; w++)
 #pragma unroll
         for (int r = 0; r < RG; r++) {
-            float dot = 0.0f;
+            int SL[NLIMB];
 #pragma unroll
             for (int L = NLIMB - 1; L >= 0; L--) {
                 uint32_t so = 0u, se = 0u;
@@ -300,9 +300,12 @@ __device__ __forceinline__ void chunk_dot(const uint32_t (&ca)[NW][RG][(QT == VO
                 }
                 // Q4: 16 * (odd + even) = 16 * odd + (16 * even)
                 const int S = (QT == VOXQ_Q4) ? (int)(se + (so << 4)) : (int)so;
-                const float d = L == 0 ? d1 : L == 1 ? d2 : d3;
-                dot = fmaf(d, (float)S, dot);
+                SL[L] = S;
             }
+            // d1 = 254 d2 up to one rounding of d2, so d1 S1 + d2 S2 = d2 (254 S1 + S2);
+            // 254 S1 + S2 stays well inside int32 (|S| < 2^20 for a 16-byte chunk)
+            float dot = d2 * (float)(SL[0] * 254 + SL[1]);
+            if (NLIMB == 3) dot = fmaf(d3, (float)SL[NLIMB - 1], dot);
             const float a2 = fmaf(sc[w][r], dot, fmaf(mn[w][r], xs, acc[w][r][m]));
             acc[w][r][m] = live ? a2 : acc[w][r][m];
         }
