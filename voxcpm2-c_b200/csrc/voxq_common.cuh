@@ -81,6 +81,25 @@ __device__ __forceinline__ float ldg_ordered(const float* p) {
     return r;
 }
 
+// Shared-memory accesses of a fixed width at a 32-bit shared address.  Used
+// where the compiler cannot prove the alignment of a runtime-aligned base and
+// would otherwise split a vector access into narrower ones (whose bank pattern
+// differs from the intended conflict-free one).  Volatile: these read buffers
+// that asynchronous copies rewrite, so they must stay behind the barrier waits.
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+
 // 16-byte global -> shared copy that completes asynchronously (cp.async
 // groups); both addresses 16-byte aligned.
 __device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {

@@ -16,17 +16,18 @@
 // dimension BN activation rows, so skinny batches (M = 16 .. 256) still fill
 // the 128-lane accumulator.  Persistent CTAs walk 128 x BN output tiles (tiles
 // sharing a weight slice are adjacent, so it is read from HBM once):
-//   warp 0       producer: raw code (128-byte rows, 128-byte swizzle) + trailer
-//                tiles by 2-D TMA into a 3-deep ring, each raw stage feeding
-//                2 (Q8) or 4 (Q4) operand stages; fp16 activation stages, laid
-//                out by the prepass as ready shared-memory images, by one bulk
-//                copy each
+//   warp 0       raw producer: code (128-byte rows, 128-byte swizzle) + trailer
+//                tiles by 2-D TMA into their ring, each raw stage feeding 2 (Q8)
+//                or 4 (Q4) operand stages
+//   warp 26      activation producer: fp16 activation stages, laid out by the
+//                prepass as ready shared-memory images, one bulk copy each
 //   warp 1       allocates tensor memory (two accumulators) and issues
 //                tcgen05.mma (one thread); tcgen05.commit releases stages and
 //                hands a finished accumulator to the epilogue
-//   warps 2-9    dequantize codes -> fp16 straight into the UMMA K-major
+//   warps 2-17   dequantize codes -> fp16 straight into the UMMA K-major
 //                128-byte-swizzled layout (3-deep ring)
-//   warps 10-13  epilogue: tcgen05.ld, row/column scaling, bias / residual /
+//   warps 18-25  epilogue (two per tensor-memory lane quarter, each half of the
+//                tile's columns): tcgen05.ld, row/column scaling, bias / residual /
 //                SwiGLU, coalesced fp32 stores -- overlapping the next tile's
 //                main loop through the second accumulator.
 // Every wait is bounded; a wait that gives up records the error word.
@@ -44,9 +45,11 @@ namespace voxq {
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kBK = 64;         // fp16 K per operand stage (one 128-byte swizzle atom)
 constexpr int kOpsA = 3;        // fp16 weight operand stages
-constexpr int kDeqWarps = 8;    // dequant warps
-constexpr int kEpiWarps = 4;    // epilogue warps (one per tensor-memory lane quarter)
-constexpr int kThreads = (2 + kDeqWarps + kEpiWarps) * 32;
+constexpr int kDeqWarps = 16;   // dequant warps (2 rows x 8 chunks per thread and stage)
+constexpr int kEpiWarps = 8;    // epilogue warps: two per tensor-memory lane quarter, each half the columns
+constexpr int kEpiParts = kEpiWarps / 4;
+constexpr int kThreads = (3 + kDeqWarps + kEpiWarps) * 32;  // + raw producer, MMA, activation producer
+constexpr int kBWarp = 2 + kDeqWarps + kEpiWarps;                // the activation producer warp
 constexpr int kRawRow = 128;    // code bytes per row and raw stage (Q8: 128 K, Q4: 256 K)
 constexpr int kRawTrRow = 32;   // trailer bytes per row and raw stage (Q8: 4 blocks, Q4: 8 blocks)
 constexpr int kRawCodes = kBM * kRawRow;
@@ -271,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     __shared__ uint64_t full_raw[kRaw], empty_raw[kRaw], full_a[kOpsA], empty_a[kOpsA], full_b[OB], empty_b[OB],
         acc_full[2], acc_empty[2];
     __shared__ uint32_t tmem_slot;
-    __shared__ __align__(16) float ainv_s[kEpiWarps][2][kMaxBN];  // epilogue: activation row scales
+    __shared__ __align__(16) float ainv_s[kEpiWarps][2][kMaxBN / kEpiParts];  // epilogue: activation row scales
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KU = g.K / kBK;  // operand stages along K
@@ -313,38 +316,43 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     // takes the same waits, lane 0 alone issues), so each warp stays converged
     // and meets the final CTA barrier as one.
     if (warp == 0) {
-        // ---------------- producer ----------------
-        // Weight tiles may stream before the kernel waits on its predecessor
-        // (the activation prepass of this call, which waited on its own
-        // predecessor before it let this kernel start); activation tiles may not.
+        // ---------------- raw producer: weight codes + trailers ----------------
+        // Weights never depend on the predecessor kernel, so this warp streams from
+        // the start.  It has a ring of its own, so it runs ahead of the tensor core
+        // by the full raw ring, independently of the activation ring.
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&g.tm_codes)) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&g.tm_tr)) : "memory");
         }
-        Ring rr, rb;
-        bool waited = false;
+        Ring rr;
         for (int w = blockIdx.x; w < units; w += gridDim.x) {
             const int t = w / S, u0 = (w % S) * KUs, u1 = min(KU, u0 + KUs);
-            const int mi = t % mt, n0 = (t / mt) * kBM;
+            const int n0 = (t / mt) * kBM;
+            for (int u = u0; u < u1; u += RK) {  // u0 is a multiple of RK
+                const int s = rr.slot<kRaw>();
+                if (rr.c >= kRaw) mbar_wait_bounded(&empty_raw[s], rr.phase<kRaw>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full_raw[s], kRawStage);
+                    uint8_t* rs = raw + s * kRawStage;
+                    tma_load_2d(rs, &g.tm_codes, (u / RK) * kRawRow, n0, &full_raw[s]);
+                    tma_load_2d(rs + kRawCodes, &g.tm_tr, (u / RK) * kRawTrRow, n0, &full_raw[s]);
+                }
+                __syncwarp();
+                rr.c++;
+            }
+        }
+    } else if (warp == kBWarp) {
+        // ---------------- activation producer ----------------
+        // The fp16 activation images come from the prepass of this call, which
+        // let this kernel start early: wait for it before the first load.
+        pdl_wait();
+        pdl_launch_dependents();
+        Ring rb;
+        for (int w = blockIdx.x; w < units; w += gridDim.x) {
+            const int t = w / S, u0 = (w % S) * KUs, u1 = min(KU, u0 + KUs);
+            const int mi = t % mt;
             const uint8_t* bsrc = g.a16t + (size_t)mi * KU * kB;
             for (int u = u0; u < u1; u++) {
-                if ((u - u0) % RK == 0) {  // u0 is a multiple of RK
-                    const int s = rr.slot<kRaw>();
-                    if (rr.c >= kRaw) mbar_wait_bounded(&empty_raw[s], rr.phase<kRaw>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
-                    if (lane == 0) {
-                        mbar_arrive_expect_tx(&full_raw[s], kRawStage);
-                        uint8_t* rs = raw + s * kRawStage;
-                        tma_load_2d(rs, &g.tm_codes, (u / RK) * kRawRow, n0, &full_raw[s]);
-                        tma_load_2d(rs + kRawCodes, &g.tm_tr, (u / RK) * kRawTrRow, n0, &full_raw[s]);
-                    }
-                    __syncwarp();
-                    rr.c++;
-                }
-                if (!waited) {
-                    pdl_wait();
-                    pdl_launch_dependents();
-                    waited = true;
-                }
                 const int s = rb.slot<OB>();
                 if (rb.c >= OB) mbar_wait_bounded(&empty_b[s], rb.phase<OB>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
                 if (lane == 0) {
@@ -390,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         // ---------------- dequant ----------------
         // Raw codes arrive 128-byte swizzled (16-byte chunk c of row r at
         // c ^ (r & 7)).  Thread -> (row, chunk): lane group g = lane / 8 takes row
-        // b + {0, 4, 2, 6}[g] (+ 32 i), b = 8 (w / 2) + (w % 2) for dequant warp w.
+        // b + {0, 4, 2, 6}[g] (+ 64 i), b = 8 (w / 2) + (w % 2) for dequant warp w.
         // The rows a half-warp reads then differ by 4 in (row & 7) (Q8: disjoint
         // swizzled chunk sets) and the 4 rows of a warp have distinct (row & 7) / 2
         // (Q4), so the shared-memory reads are free of bank conflicts.
@@ -399,21 +407,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         const int r0 = 8 * (dw >> 1) + (dw & 1) + ((0x6240 >> (4 * (lane >> 3))) & 0xF);
         // reads only weights (rowmul, codes via shared memory): no predecessor wait
         Ring rr, ra;
+        constexpr int RPT = kBM * 8 / (kDeqWarps * 32);  // rows per thread and stage
+        constexpr int RST = kBM / RPT;                     // row stride between them
         // row multipliers of the next unit's tile are fetched one unit ahead
-        float rnext[kBM / 32];
+        float rnext[RPT];
 #pragma unroll
-        for (int i = 0; i < kBM / 32; i++) {
-            const int n = (blockIdx.x / S / mt) * kBM + r0 + 32 * i;
+        for (int i = 0; i < RPT; i++) {
+            const int n = (blockIdx.x / S / mt) * kBM + r0 + RST * i;
             rnext[i] = n < g.N ? ldg_ordered(g.rowmul + n) : 1.0f;
         }
         for (int w = blockIdx.x; w < units; w += gridDim.x) {
             const int u0 = (w % S) * KUs, u1 = min(KU, u0 + KUs);
-            float rmul[kBM / 32];
+            float rmul[RPT];
             const int wn = w + gridDim.x;
 #pragma unroll
-            for (int i = 0; i < kBM / 32; i++) {
+            for (int i = 0; i < RPT; i++) {
                 rmul[i] = rnext[i];
-                const int n = (wn / S / mt) * kBM + r0 + 32 * i;
+                const int n = (wn / S / mt) * kBM + r0 + RST * i;
                 rnext[i] = (wn < units && n < g.N) ? ldg_ordered(g.rowmul + n) : 1.0f;
             }
             for (int u = u0; u < u1; u++) {
@@ -423,36 +433,35 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 if (h == 0) mbar_wait_bounded(&full_raw[s], rr.phase<kRaw>(), VOXQ_DEVERR_WAIT_FULL, g.err);
                 const int sa = ra.slot<kOpsA>();
                 if (ra.c >= kOpsA) mbar_wait_bounded(&empty_a[sa], ra.phase<kOpsA>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
-                const uint8_t* rc = raw + s * kRawStage;
-                const uint8_t* rt = rc + kRawCodes;
-                uint8_t* dstA = opA + sa * kA16;
+                const uint32_t rc = smem_u32(raw) + s * kRawStage;
+                const uint32_t rt = rc + kRawCodes;
+                const uint32_t dstA = smem_u32(opA) + sa * kA16;
                 const int blk = 2 * h + (j >> 2);  // 32-value block index within the raw stage
 #pragma unroll
-                for (int i = 0; i < kBM / 32; i++) {
-                    const int row = r0 + 32 * i;
+                for (int i = 0; i < RPT; i++) {
+                    const int row = r0 + RST * i;
                     const int sw = row & 7;
                     float sc, mn;
                     uint32_t lo, hi = 0;
                     if (QT == VOXQ_Q8) {
                         // logical bytes 64 h + 8 j .. +8: chunk 4 h + j / 2, half j & 1
-                        const uint2 c = *reinterpret_cast<const uint2*>(rc + row * kRawRow +
-                                                                        (((4 * h + (j >> 1)) ^ sw) << 4) + 8 * (j & 1));
+                        const uint2 c = lds64(rc + row * kRawRow + (((4 * h + (j >> 1)) ^ sw) << 4) + 8 * (j & 1));
                         lo = c.x;
                         hi = c.y;
-                        const float2 tr = *reinterpret_cast<const float2*>(rt + row * kRawTrRow + 8 * blk);
-                        sc = tr.x;
-                        mn = tr.y;
+                        const uint2 tr = lds64(rt + row * kRawTrRow + 8 * blk);
+                        sc = __uint_as_float(tr.x);
+                        mn = __uint_as_float(tr.y);
                     } else {
                         // logical bytes 32 h + 4 j .. +4: chunk 2 h + j / 4, word j & 3
-                        lo = *reinterpret_cast<const uint32_t*>(rc + row * kRawRow + (((2 * h + (j >> 2)) ^ sw) << 4) +
-                                                                4 * (j & 3));
-                        const float2 tr = __half22float2(*reinterpret_cast<const __half2*>(rt + row * kRawTrRow + 4 * blk));
+                        lo = lds32(rc + row * kRawRow + (((2 * h + (j >> 2)) ^ sw) << 4) + 4 * (j & 3));
+                        const uint32_t t = lds32(rt + row * kRawTrRow + 4 * blk);
+                        const float2 tr = __half22float2(*reinterpret_cast<const __half2*>(&t));
                         sc = tr.x;
                         mn = tr.y;
                     }
                     const uint4 v = deq8<QT, SIGNED>(lo, hi, sc * rmul[i], mn * rmul[i]);
                     // K-major 128-byte swizzle: chunk j of row `row` lands at j ^ (row & 7)
-                    *reinterpret_cast<uint4*>(dstA + row * 128 + ((j ^ sw) << 4)) = v;
+                    sts128(dstA + row * 128 + ((j ^ sw) << 4), v);
                 }
                 // make the generic-proxy writes visible to the tensor core
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -465,12 +474,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 if (last_use) rr.c++;
             }
         }
-    } else {
+    } else if (warp < 2 + kDeqWarps + kEpiWarps) {
         // ---------------- epilogue ----------------
         pdl_wait();  // row scales of the prepass; residual / gate / output of earlier work
         pdl_launch_dependents();
-        const int q = warp & 3;  // tensor-memory lane quarter of this warp
-        float* ainv_w = &ainv_s[q][0][0];
+        // warp e: tensor-memory lane quarter q = warp % 4 (the hardware's access rule),
+        // tile columns [cb, ce) = part e / 4 of the tile (all of it below 2 x 16 columns)
+        const int e = warp - (2 + kDeqWarps);
+        const int q = warp & 3;
+        constexpr int CWID = (BN / kEpiParts >= 16) ? BN / kEpiParts : BN;
+        const int cb = (e / 4) * CWID, ce = min(BN, cb + CWID);
+        float* ainv_w = &ainv_s[e][0][0];
         // The tile's activation row scales go to shared memory by cp.async one
         // unit ahead (ainv is padded to whole tiles); column scale and bias one
         // unit ahead in registers.  Nothing the loop needs is fetched after the
@@ -481,8 +495,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (fw < units) {                                                                                        \
             const int ft = fw / S;                                                                               \
             const int fm0 = (ft % mt) * BN, fn = (ft / mt) * kBM + q * 32 + lane;                                \
-            for (int c = lane; c < BN / 4; c += 32)                                                              \
-                cp_async16(ainv_w + (BUF) * kMaxBN + 4 * c, g.ainv + fm0 + 4 * c);                               \
+            for (int c = lane; c < (ce - cb) / 4; c += 32)                                                       \
+                cp_async16(ainv_w + (BUF) * (kMaxBN / kEpiParts) + 4 * c, g.ainv + fm0 + cb + 4 * c);            \
             rm_next = fn < g.N ? ldg_ordered(g.rowmul + fn) : 1.0f;                                              \
             b_next = (fn < g.N && g.bias) ? ldg_ordered(g.bias + fn) : 0.0f;                                     \
         }                                                                                                        \
@@ -501,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             const float bias = b_next;
             VOXQ_EPI_FETCH(w + gridDim.x, as ^ 1);
             const int mlim = nok ? min(BN, g.M - m0) : 0;  // valid rows of this tile for this lane
-            const float* arow = ainv_w + as * kMaxBN;
+            const float* arow = ainv_w + as * (kMaxBN / kEpiParts) - cb;  // indexed by tile column
             const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * TC);
             mbar_wait_sleepy(&acc_full[as], (it >> 1) & 1, VOXQ_DEVERR_WAIT_MMA, g.err);
             tc_fence_after();
@@ -510,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             if (S == 1) {
                 // kept as a loop: a fully unrolled epilogue thrashes the instruction cache
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
+                for (int c0 = cb; c0 < ce; c0 += 16) {
                     uint32_t v[16];
                     tmem_ld16(tacc + (uint32_t)c0, v);
                     float am[16];
@@ -544,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 // applies the epilogue.
                 float* pp = g.part + ((size_t)(t * S + sp) * BN) * kBM + q * 32 + lane;
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
+                for (int c0 = cb; c0 < ce; c0 += 16) {
                     uint32_t v[16];
                     tmem_ld16(tacc + (uint32_t)c0, v);
 #pragma unroll
