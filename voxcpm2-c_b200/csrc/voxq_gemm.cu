@@ -72,14 +72,13 @@ constexpr int raw_stages(int bn) { return bn >= 256 ? 3 : bn >= 128 ? 4 : 5; }
 // thread per 8 values, so a row costs one load latency, not K/128 of them.
 // ---------------------------------------------------------------------------
 constexpr int kActThreads = 128;
+constexpr int kPrepChunks = 4;    // weight chunks per prepass thread
+constexpr int kW16Rows = 256;     // rows per tile of the tiled fp16 weight (covers NT = 1 and 2)
 
-__global__ void __launch_bounds__(kActThreads) act_tile_kernel(const float* __restrict__ a, int M, int K, int64_t lda,
-                                                               int bn, uint8_t* __restrict__ a16t,
-                                                               float* __restrict__ ainv) {
-    pdl_wait();
-    pdl_launch_dependents();
+__device__ __forceinline__ void act_row(const float* __restrict__ a, int M, int K, int64_t lda, int bn,
+                                        uint8_t* __restrict__ a16t, float* __restrict__ ainv, int m) {
     __shared__ float red[kActThreads / 32];
-    const int m = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int KU = K / kBK, nch = K / 8;
     const bool live = m < M;
     const float* row = a + (int64_t)m * lda;
@@ -120,6 +119,14 @@ __global__ void __launch_bounds__(kActThreads) act_tile_kernel(const float* __re
         *reinterpret_cast<uint4*>(tb + (int64_t)u * bn * 128 + ((j ^ (r & 7)) << 4)) = h;
     }
     if (threadIdx.x == 0) ainv[m] = live ? ldexpf(1.0f, -e) : 0.0f;
+}
+
+__global__ void __launch_bounds__(kActThreads) act_tile_kernel(const float* __restrict__ a, int M, int K, int64_t lda,
+                                                               int bn, uint8_t* __restrict__ a16t,
+                                                               float* __restrict__ ainv) {
+    pdl_wait();
+    pdl_launch_dependents();
+    act_row(a, M, K, lda, bn, a16t, ainv, blockIdx.x);
 }
 
 // ---------------------------------------------------------------------------
@@ -176,6 +183,7 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g));
 struct GemmArgs {
     CUtensorMap tm_codes;   // u8 [N][rowb], box {128, 128}, 128-byte swizzle
     CUtensorMap tm_tr;      // u8 [N][srow], box {32, 128}
+    const uint8_t* w16t;    // two-phase path: tiled fp16 weight images (prep_f16_kernel)
     const uint8_t* a16t;    // tiled fp16 activation images (act_tile_kernel)
     const float* rowmul;    // [N]
     const float* ainv;      // [Mpad]
@@ -253,6 +261,114 @@ __device__ __forceinline__ float epi_value(const GemmArgs& g, float acc, float s
     y += bias;
     if (g.residual) y += __ldg(g.residual + m * g.ldr + n);
     return y;
+}
+
+// Epilogue role (kEpiWarps warps): tcgen05.ld of a finished accumulator, row /
+// column scaling, bias / residual / SwiGLU gate, coalesced fp32 stores -- or,
+// for split K, the raw partial sums for the reduction kernel.  Warp e (0 ..
+// kEpiWarps-1) reads tensor-memory lane quarter q = warp % 4 and columns part e / 4.
+// Tiles are NT x 128 weight rows (sub-tiles, one accumulator each) x BN
+// activation rows; NACC accumulator sets alternate between tiles.  Warp e
+// serves sub-tile (e / 4) % NT and column part (e / 4) / NT of CP.
+template <int BN, int TC, int NT, int NACC, int CP>
+__device__ __forceinline__ void epilogue_role(const GemmArgs& g, uint32_t tmem, uint64_t* acc_full, uint64_t* acc_empty,
+                                              float* ainv_all, int units, int mt, int S, int e, int q, int lane) {
+        pdl_wait();  // row scales of the prepass; residual / gate / output of earlier work
+        pdl_launch_dependents();
+        // warp e: tensor-memory lane quarter q = warp % 4 (the hardware's access rule),
+        // tile columns [cb, ce) = its column part (all of them below CP x 16 columns)
+        constexpr int CWID = (BN / CP >= 16) ? BN / CP : BN;
+        constexpr int TN = kBM * NT;  // weight rows per tile
+        const int sub = (e / 4) % NT, part = (e / 4) / NT;
+        const int cb = part * CWID, ce = min(BN, cb + CWID);
+        float* ainv_w = ainv_all + e * 2 * (kMaxBN / CP);
+        // The tile's activation row scales go to shared memory by cp.async one
+        // unit ahead (ainv is padded to whole tiles); column scale and bias one
+        // unit ahead in registers.  Nothing the loop needs is fetched after the
+        // accumulator wait.
+#define VOXQ_EPI_FETCH(W, BUF)                                                                                   \
+    do {                                                                                                         \
+        const int fw = (W);                                                                                      \
+        if (fw < units) {                                                                                        \
+            const int ft = fw / S;                                                                               \
+            const int fm0 = (ft % mt) * BN, fn = (ft / mt) * TN + sub * kBM + q * 32 + lane;                     \
+            for (int c = lane; c < (ce - cb) / 4; c += 32)                                                       \
+                cp_async16(ainv_w + (BUF) * (kMaxBN / CP) + 4 * c, g.ainv + fm0 + cb + 4 * c);                   \
+            rm_next = fn < g.N ? ldg_ordered(g.rowmul + fn) : 1.0f;                                              \
+            b_next = (fn < g.N && g.bias) ? ldg_ordered(g.bias + fn) : 0.0f;                                     \
+        }                                                                                                        \
+        cp_async_commit();                                                                                       \
+    } while (0)
+        float rm_next = 1.0f, b_next = 0.0f;
+        VOXQ_EPI_FETCH(blockIdx.x, 0);
+        int it = 0;
+        for (int w = blockIdx.x; w < units; w += gridDim.x, it++) {
+            const int t = w / S, sp = w % S;
+            const int m0 = (t % mt) * BN, n0 = (t / mt) * TN + sub * kBM;
+            const int ab = it & 1;        // row-scale staging buffer
+            const int as = it % NACC;     // accumulator set
+            const int nrow = n0 + q * 32 + lane;  // weight row = output column n
+            const bool nok = nrow < g.N;
+            const float rinv = 1.0f / rm_next;
+            const float bias = b_next;
+            VOXQ_EPI_FETCH(w + gridDim.x, ab ^ 1);
+            const int mlim = nok ? min(BN, g.M - m0) : 0;  // valid rows of this tile for this lane
+            const float* arow = ainv_w + ab * (kMaxBN / CP) - cb;  // indexed by tile column
+            const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((as * NT + sub) * TC);
+            mbar_wait_sleepy(&acc_full[as], (it / NACC) & 1, VOXQ_DEVERR_WAIT_MMA, g.err);
+            tc_fence_after();
+            cp_async_wait<1>();  // this unit's row scales (the next unit's may be in flight)
+            __syncwarp();
+            if (S == 1) {
+                // kept as a loop: a fully unrolled epilogue thrashes the instruction cache
+#pragma unroll 1
+                for (int c0 = cb; c0 < ce; c0 += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(tacc + (uint32_t)c0, v);
+                    float am[16];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float4 x = *reinterpret_cast<const float4*>(arow + c0 + 4 * i);
+                        am[4 * i] = x.x;
+                        am[4 * i + 1] = x.y;
+                        am[4 * i + 2] = x.z;
+                        am[4 * i + 3] = x.w;
+                    }
+                    float* o = g.out + (int64_t)(m0 + c0) * g.ldo + nrow;
+                    if (!g.gate && !g.residual) {
+#pragma unroll
+                        for (int i = 0; i < 16; i++)
+                            if (c0 + i < mlim) o[(int64_t)i * g.ldo] = __uint_as_float(v[i]) * (rinv * am[i]) + bias;
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; i++)
+                            if (c0 + i < mlim)
+                                o[(int64_t)i * g.ldo] =
+                                    epi_value(g, __uint_as_float(v[i]), rinv * am[i], bias, m0 + c0 + i, nrow);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[as]);
+            } else {
+                // Split K: park the raw partial sum ([BN][128] per unit) for the
+                // reduction kernel, which adds the S partials in split order and
+                // applies the epilogue.
+                float* pp = g.part + ((size_t)(t * S + sp) * BN) * TN + sub * kBM + q * 32 + lane;
+#pragma unroll 1
+                for (int c0 = cb; c0 < ce; c0 += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(tacc + (uint32_t)c0, v);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) pp[(c0 + i) * TN] = __uint_as_float(v[i]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[as]);
+            }
+        }
+        cp_async_wait<0>();
+#undef VOXQ_EPI_FETCH
 }
 
 template <int QT, int BN, bool SIGNED>
@@ -476,101 +592,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
     } else if (warp < 2 + kDeqWarps + kEpiWarps) {
         // ---------------- epilogue ----------------
-        pdl_wait();  // row scales of the prepass; residual / gate / output of earlier work
-        pdl_launch_dependents();
-        // warp e: tensor-memory lane quarter q = warp % 4 (the hardware's access rule),
-        // tile columns [cb, ce) = part e / 4 of the tile (all of it below 2 x 16 columns)
-        const int e = warp - (2 + kDeqWarps);
-        const int q = warp & 3;
-        constexpr int CWID = (BN / kEpiParts >= 16) ? BN / kEpiParts : BN;
-        const int cb = (e / 4) * CWID, ce = min(BN, cb + CWID);
-        float* ainv_w = &ainv_s[e][0][0];
-        // The tile's activation row scales go to shared memory by cp.async one
-        // unit ahead (ainv is padded to whole tiles); column scale and bias one
-        // unit ahead in registers.  Nothing the loop needs is fetched after the
-        // accumulator wait.
-#define VOXQ_EPI_FETCH(W, BUF)                                                                                   \
-    do {                                                                                                         \
-        const int fw = (W);                                                                                      \
-        if (fw < units) {                                                                                        \
-            const int ft = fw / S;                                                                               \
-            const int fm0 = (ft % mt) * BN, fn = (ft / mt) * kBM + q * 32 + lane;                                \
-            for (int c = lane; c < (ce - cb) / 4; c += 32)                                                       \
-                cp_async16(ainv_w + (BUF) * (kMaxBN / kEpiParts) + 4 * c, g.ainv + fm0 + cb + 4 * c);            \
-            rm_next = fn < g.N ? ldg_ordered(g.rowmul + fn) : 1.0f;                                              \
-            b_next = (fn < g.N && g.bias) ? ldg_ordered(g.bias + fn) : 0.0f;                                     \
-        }                                                                                                        \
-        cp_async_commit();                                                                                       \
-    } while (0)
-        float rm_next = 1.0f, b_next = 0.0f;
-        VOXQ_EPI_FETCH(blockIdx.x, 0);
-        int it = 0;
-        for (int w = blockIdx.x; w < units; w += gridDim.x, it++) {
-            const int t = w / S, sp = w % S;
-            const int m0 = (t % mt) * BN, n0 = (t / mt) * kBM;
-            const int as = it & 1;
-            const int nrow = n0 + q * 32 + lane;  // weight row = output column n
-            const bool nok = nrow < g.N;
-            const float rinv = 1.0f / rm_next;
-            const float bias = b_next;
-            VOXQ_EPI_FETCH(w + gridDim.x, as ^ 1);
-            const int mlim = nok ? min(BN, g.M - m0) : 0;  // valid rows of this tile for this lane
-            const float* arow = ainv_w + as * (kMaxBN / kEpiParts) - cb;  // indexed by tile column
-            const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * TC);
-            mbar_wait_sleepy(&acc_full[as], (it >> 1) & 1, VOXQ_DEVERR_WAIT_MMA, g.err);
-            tc_fence_after();
-            cp_async_wait<1>();  // this unit's row scales (the next unit's may be in flight)
-            __syncwarp();
-            if (S == 1) {
-                // kept as a loop: a fully unrolled epilogue thrashes the instruction cache
-#pragma unroll 1
-                for (int c0 = cb; c0 < ce; c0 += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(tacc + (uint32_t)c0, v);
-                    float am[16];
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const float4 x = *reinterpret_cast<const float4*>(arow + c0 + 4 * i);
-                        am[4 * i] = x.x;
-                        am[4 * i + 1] = x.y;
-                        am[4 * i + 2] = x.z;
-                        am[4 * i + 3] = x.w;
-                    }
-                    float* o = g.out + (int64_t)(m0 + c0) * g.ldo + nrow;
-                    if (!g.gate && !g.residual) {
-#pragma unroll
-                        for (int i = 0; i < 16; i++)
-                            if (c0 + i < mlim) o[(int64_t)i * g.ldo] = __uint_as_float(v[i]) * (rinv * am[i]) + bias;
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 16; i++)
-                            if (c0 + i < mlim)
-                                o[(int64_t)i * g.ldo] =
-                                    epi_value(g, __uint_as_float(v[i]), rinv * am[i], bias, m0 + c0 + i, nrow);
-                    }
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[as]);
-            } else {
-                // Split K: park the raw partial sum ([BN][128] per unit) for the
-                // reduction kernel, which adds the S partials in split order and
-                // applies the epilogue.
-                float* pp = g.part + ((size_t)(t * S + sp) * BN) * kBM + q * 32 + lane;
-#pragma unroll 1
-                for (int c0 = cb; c0 < ce; c0 += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(tacc + (uint32_t)c0, v);
-#pragma unroll
-                    for (int i = 0; i < 16; i++) pp[(c0 + i) * kBM] = __uint_as_float(v[i]);
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[as]);
-            }
-        }
-        cp_async_wait<0>();
-#undef VOXQ_EPI_FETCH
+        epilogue_role<BN, TC, 1, 2, kEpiParts>(g, tmem, acc_full, acc_empty, &ainv_s[0][0][0], units, mt, S,
+                                               warp - (2 + kDeqWarps), warp & 3, lane);
     }
     // dequant / epilogue roles touch global outputs only after the wait below
     tc_fence_before();
@@ -578,6 +601,195 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TC) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Two-phase path for large M (the tensor core is the bound).  Phase 1 (one
+// launch, one block of 128 threads per unit of work): the activation rows as
+// in act_tile_kernel, and the weight dequantized once into fp16 rows
+// w16[n][k] = fp16((q s + m) * rowmul[n]) with the same deq8 arithmetic as the
+// fused kernel's dequant warps (identical values).  Phase 2: a plain
+// TMA -> tcgen05 GEMM on the fp16 operands.  Dequantizing once per call
+// instead of once per activation tile removes the dequant warps, their
+// shared-memory round trip and proxy fences from the main loop.
+// ---------------------------------------------------------------------------
+template <int QT, bool SIGNED>
+__global__ void __launch_bounds__(kActThreads) prep_f16_kernel(const float* __restrict__ a, int M, int K, int64_t lda,
+                                                               int bn, uint8_t* __restrict__ a16t,
+                                                               float* __restrict__ ainv, int act_blocks,
+                                                               const uint8_t* __restrict__ codes,
+                                                               const uint8_t* __restrict__ scales,
+                                                               const float* __restrict__ rowmul, int N,
+                                                               __half* __restrict__ w16) {
+    pdl_wait();  // activations may come from the previous kernel; w16 may still be read by it
+    pdl_launch_dependents();
+    if ((int)blockIdx.x < act_blocks) {
+        act_row(a, M, K, lda, bn, a16t, ainv, blockIdx.x);
+        return;
+    }
+    // Weight chunks: thread c handles 8 consecutive weights (one 16-byte fp16
+    // chunk) of kPrepChunks chunk slots strided by the grid.  Output layout: the
+    // shared-memory image of each (256-row tile, 64-wide K stage) -- rows r of
+    // 128 bytes, 16-byte chunk j of row r at j ^ (r & 7) -- contiguous, so the
+    // GEMM fetches a stage's weights with one bulk copy.
+    const int cpr = K / 8, KU = K / kBK;
+    const int64_t total = (int64_t)N * cpr;
+    const int64_t rowb = codes_row_bytes(K, QT), srow = (int64_t)(K / VOXQ_QBLK) * scale_bytes(QT);
+    const int64_t nthreads = (int64_t)(gridDim.x - act_blocks) * kActThreads;
+    const int64_t t0 = (int64_t)(blockIdx.x - act_blocks) * kActThreads + threadIdx.x;
+#pragma unroll
+    for (int i = 0; i < kPrepChunks; i++) {
+        const int64_t chunk = t0 + i * nthreads;
+        if (chunk >= total) break;
+        const int n = (int)(chunk / cpr), c = (int)(chunk % cpr), k0 = c * 8;
+        const int blk = k0 / VOXQ_QBLK;
+        const float rm = __ldg(rowmul + n);
+        uint32_t lo, hi = 0;
+        float sc, mn;
+        if (QT == VOXQ_Q8) {
+            const uint2 cw = __ldg(reinterpret_cast<const uint2*>(codes + n * rowb + k0));
+            lo = cw.x;
+            hi = cw.y;
+            const float2 tr = __ldg(reinterpret_cast<const float2*>(scales + n * srow + 8 * blk));
+            sc = tr.x;
+            mn = tr.y;
+        } else {
+            lo = __ldg(reinterpret_cast<const uint32_t*>(codes + n * rowb + k0 / 2));
+            const float2 tr = __half22float2(*reinterpret_cast<const __half2*>(scales + n * srow + 4 * blk));
+            sc = tr.x;
+            mn = tr.y;
+        }
+        const int tp = n / kW16Rows, r = n % kW16Rows, u = c >> 3, j = c & 7;
+        uint8_t* dst = reinterpret_cast<uint8_t*>(w16) + (((int64_t)tp * KU + u) * kW16Rows + r) * 128 +
+                       ((j ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = deq8<QT, SIGNED>(lo, hi, sc * rm, mn * rm);
+    }
+}
+
+// Two-phase GEMM kernel.  NT = 2: a tile is 256 weight rows (two 128-row
+// sub-tiles, one accumulator each, sharing every activation stage) x BN
+// activation rows, so a stage carries 64 KB for 8 MMAs (~1024 cycles) and three
+// stages in flight cover the ~1.1-1.4 us TMA latency; the two accumulators fill
+// tensor memory, so tiles do not overlap their epilogues (16 epilogue warps keep
+// it short).  NT = 1: 128-row tiles with double-buffered accumulators.
+constexpr int f16_epi_warps(int nt) { return nt == 2 ? 16 : 8; }
+constexpr int f16_threads(int nt) { return (2 + f16_epi_warps(nt)) * 32; }
+constexpr int f16_stages(int bn, int nt) { return nt == 2 ? 3 : bn >= 256 ? 4 : bn >= 128 ? 6 : 8; }
+constexpr int f16_stage_bytes(int bn, int nt) { return nt * kA16 + bn * kBK * 2; }
+
+template <int BN, int NT>
+__global__ void __launch_bounds__(f16_threads(NT), 1) gemm_f16_kernel(const __grid_constant__ GemmArgs g) {
+    constexpr int R = f16_stages(BN, NT);
+    constexpr int kB = BN * kBK * 2;
+    constexpr int STG = f16_stage_bytes(BN, NT);
+    constexpr int TC = BN < 32 ? 32 : BN;
+    constexpr int NACC = NT == 1 ? 2 : 1;
+    constexpr int EPIW = f16_epi_warps(NT);
+    constexpr int CP = EPIW / (4 * NT);  // column parts per sub-tile
+    constexpr uint32_t IDESC = umma_idesc(BN);
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // R x (A NT x 16 KB | B kB)
+    __shared__ uint64_t full[R], empty[R], acc_full[NACC], acc_empty[NACC];
+    __shared__ uint32_t tmem_slot;
+    __shared__ __align__(16) float ainv_s[EPIW][2][kMaxBN / CP];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KU = g.K / kBK;
+    const int mt = (g.M + BN - 1) / BN, ntl = (g.N + kBM * NT - 1) / (kBM * NT);
+    const int S = g.S, KUs = g.KUs;
+    const int units = mt * ntl * S;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < R; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < NACC; i++) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], EPIW);
+        }
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"(NACC * NT * TC)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- producer: both operands of a stage, one barrier ----------------
+        pdl_wait();  // both operands come from the prepass of this call
+        pdl_launch_dependents();
+        Ring rr;
+        for (int w = blockIdx.x; w < units; w += gridDim.x) {
+            const int t = w / S, u0 = (w % S) * KUs, u1 = min(KU, u0 + KUs);
+            const int mi = t % mt, n0 = (t / mt) * (kBM * NT);
+            const uint8_t* bsrc = g.a16t + (size_t)mi * KU * kB;
+            for (int u = u0; u < u1; u++) {
+                const int s = rr.slot<R>();
+                if (rr.c >= R) mbar_wait_bounded(&empty[s], rr.phase<R>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[s], STG);
+                    uint8_t* st = base + s * STG;
+                    // weights: rows n0 .. n0 + 128 NT of the tiled fp16 image (256-row tiles)
+                    const uint8_t* wsrc = g.w16t + (((size_t)(n0 / kW16Rows) * KU + u) * kW16Rows +
+                                                    (n0 % kW16Rows)) * 128;
+                    bulk_g2s(st, wsrc, NT * kA16, &full[s]);
+                    bulk_g2s(st + NT * kA16, bsrc + (size_t)u * kB, kB, &full[s]);
+                }
+                __syncwarp();
+                rr.c++;
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        Ring rr;
+        int it = 0;
+        for (int w = blockIdx.x; w < units; w += gridDim.x, it++) {
+            const int u0 = (w % S) * KUs, u1 = min(KU, u0 + KUs);
+            const int as = it % NACC;
+            if (it >= NACC) mbar_wait_bounded(&acc_empty[as], ((it / NACC) & 1) ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
+            tc_fence_after();
+            for (int u = u0; u < u1; u++) {
+                const int s = rr.slot<R>();
+                mbar_wait_bounded(&full[s], rr.phase<R>(), VOXQ_DEVERR_WAIT_FULL, g.err);
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint64_t bd = umma_desc(base + s * STG + NT * kA16);
+#pragma unroll
+                    for (int sub = 0; sub < NT; sub++) {
+                        const uint64_t ad = umma_desc(base + s * STG + sub * kA16);
+                        const uint32_t acc = tmem + (uint32_t)((as * NT + sub) * TC);
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 16; kk++)
+                            umma_f16(acc, ad + 2 * kk, bd + 2 * kk, IDESC, (u > u0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                __syncwarp();
+                rr.c++;
+            }
+            if (lane == 0) umma_commit(&acc_full[as]);
+            __syncwarp();
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        epilogue_role<BN, TC, NT, NACC, CP>(g, tmem, acc_full, acc_empty, &ainv_s[0][0][0], units, mt, S, warp - 2,
+                                            warp & 3, lane);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NACC * NT * TC)
+                     : "memory");
     }
 }
 
@@ -667,6 +879,8 @@ static size_t act_bytes(int M, int K) {
 // launch.  VOXQ_GEMM_BN / VOXQ_GEMM_SPLIT override (tuning).
 struct GemmPlan {
     int bn, S, KUs, tiles;
+    bool two_phase;  // dequantize the weight once (prep_f16_kernel), then gemm_f16_kernel
+    int nt;          // two-phase: 128-row weight sub-tiles per tile (1 or 2)
 };
 
 static int env_int(const char* name) {
@@ -676,7 +890,12 @@ static int env_int(const char* name) {
 
 static GemmPlan plan_gemm(int M, int N, int K, int qt) {
     static const int forced_bn = env_int("VOXQ_GEMM_BN"), forced_s = env_int("VOXQ_GEMM_SPLIT");
+    static const int forced_path = env_int("VOXQ_GEMM_TWO_PHASE");  // 1: always, -1: never
     GemmPlan p;
+    // Large batches are tensor-bound: dequantizing the weight once per call (about
+    // 2.6 B/weight of extra traffic) is cheaper than the dequant pipeline of the
+    // fused kernel, which repeats it for every activation tile.
+    p.two_phase = forced_path > 0 || (forced_path == 0 && M >= 512);
     if (forced_bn == 16 || forced_bn == 32 || forced_bn == 64 || forced_bn == 128 || forced_bn == 256) {
         p.bn = forced_bn;
     } else {
@@ -684,8 +903,20 @@ static GemmPlan plan_gemm(int M, int N, int K, int qt) {
         while (p.bn < M && p.bn < kMaxBN) p.bn *= 2;
     }
     const int KU = K / kBK, RK = (qt == VOXQ_Q4) ? 4 : 2;
-    p.tiles = ((M + p.bn - 1) / p.bn) * ((N + kBM - 1) / kBM);
     const int sms = device_sm_count();
+    p.nt = 1;
+    if (p.two_phase && p.bn == 256) {
+        // 256-row tiles when they still cover most SMs (no split K with them)
+        const int tiles2 = ((M + p.bn - 1) / p.bn) * ((N + 2 * kBM - 1) / (2 * kBM));
+        if (tiles2 * 5 >= sms * 3) {
+            p.nt = 2;
+            p.tiles = tiles2;
+            p.S = 1;
+            p.KUs = KU;
+            return p;
+        }
+    }
+    p.tiles = ((M + p.bn - 1) / p.bn) * ((N + kBM - 1) / kBM);
     const int smax = KU / RK > 1 ? KU / RK : 1;
     double best = 1e30;
     p.S = 1;
@@ -712,10 +943,17 @@ static size_t part_bytes(const GemmPlan& p) {
     return p.S > 1 ? align256((size_t)p.S * p.tiles * p.bn * kBM * 4) : 0;
 }
 
+static size_t w16_bytes(const GemmPlan& p, int N, int K) {
+    // tiled image: whole 256-row tiles (rows past N are never read: bulk copies
+    // stop at the tile's last sub-tile, whose rows past N only feed discarded outputs)
+    return p.two_phase ? align256((size_t)(N + kW16Rows - 1) / kW16Rows * kW16Rows * K * 2) : 0;
+}
+
 size_t gemm_workspace_bytes(int M, int N, int K, int qtype, bool swiglu) {
-    // tiled fp16 activations + row scales, split-K partials (+ the SwiGLU gate result)
+    // tiled fp16 activations + row scales, split-K partials, fp16 weight (two-phase)
+    // (+ the SwiGLU gate result)
     const GemmPlan p = plan_gemm(M, N, K, qtype);
-    return act_bytes(M, K) + part_bytes(p) + (swiglu ? align256((size_t)M * N * 4) : 0);
+    return act_bytes(M, K) + part_bytes(p) + w16_bytes(p, N, K) + (swiglu ? align256((size_t)M * N * 4) : 0);
 }
 
 template <int QT, int BN, bool SIGNED>
@@ -747,6 +985,39 @@ static VoxCPMError launch_gemm_t(const GemmArgs& a, cudaStream_t st) {
     cfg.numAttrs = 1;
     VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
     return VOXCPM_SUCCESS;
+}
+
+template <int BN, int NT>
+static VoxCPMError launch_f16_t(const GemmArgs& a, cudaStream_t st) {
+    constexpr int smem = 1024 + f16_stages(BN, NT) * f16_stage_bytes(BN, NT);
+    auto kern = gemm_f16_kernel<BN, NT>;
+    static std::once_flag once;
+    std::call_once(once, [&] { cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); });
+    const int units = ((a.M + BN - 1) / BN) * ((a.N + kBM * NT - 1) / (kBM * NT)) * a.S;
+    const int cap = device_sm_count();  // one CTA per SM (tensor memory)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(units < cap ? units : cap);
+    cfg.blockDim = dim3(f16_threads(NT));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
+    return VOXCPM_SUCCESS;
+}
+
+static VoxCPMError launch_f16(const GemmArgs& a, int bn, int nt, cudaStream_t st) {
+    if (nt == 2) return launch_f16_t<256, 2>(a, st);
+    switch (bn) {
+        case 16: return launch_f16_t<16, 1>(a, st);
+        case 32: return launch_f16_t<32, 1>(a, st);
+        case 64: return launch_f16_t<64, 1>(a, st);
+        case 128: return launch_f16_t<128, 1>(a, st);
+        default: return launch_f16_t<256, 1>(a, st);
+    }
 }
 
 template <int QT>
@@ -805,16 +1076,18 @@ static void pdl_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, cudaS
 // (SwiGLU second half).
 static VoxCPMError gemm_one(const GemmPlan& pl, const float* ainv, const uint8_t* a16t, int M, const voxq_qweight* w,
                             float* out, int64_t ldo, const float* bias, const float* residual, int64_t ldr,
-                            const float* gate, int64_t ldg, float* part, cudaStream_t st) {
+                            const float* gate, int64_t ldg, float* part, const __half* w16, cudaStream_t st) {
     const int N = w->N, K = w->K, qt = w->qtype;
     static thread_local GemmArgs ga;
     const uint64_t rowb = (uint64_t)codes_row_bytes(K, qt);
     const uint64_t srow = (uint64_t)(K / VOXQ_QBLK) * scale_bytes(qt);
-    if (!make_map(&ga.tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->codes, rowb, (uint64_t)N, rowb, kRawRow, kBM,
-                  CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map(&ga.tm_tr, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->scales, srow, (uint64_t)N, srow, kRawTrRow, kBM,
-                  CU_TENSOR_MAP_SWIZZLE_NONE))
+    ga.w16t = reinterpret_cast<const uint8_t*>(w16);
+    if (!pl.two_phase && (!make_map(&ga.tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->codes, rowb, (uint64_t)N, rowb, kRawRow, kBM,
+                         CU_TENSOR_MAP_SWIZZLE_128B) ||
+               !make_map(&ga.tm_tr, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->scales, srow, (uint64_t)N, srow, kRawTrRow, kBM,
+                         CU_TENSOR_MAP_SWIZZLE_NONE))) {
         return VOXCPM_ERR_INTERNAL;
+    }
     ga.a16t = a16t;
     ga.rowmul = reinterpret_cast<const float*>(static_cast<const uint8_t*>(w->scales) + rowmul_offset(N, K, qt));
     ga.ainv = ainv;
@@ -834,8 +1107,9 @@ static VoxCPMError gemm_one(const GemmPlan& pl, const float* ainv, const uint8_t
     ga.q8_signed = w->q8_signed;
     ga.err = device_error_word();
     const int bn = pl.bn;
-    VoxCPMError e =
-        qt == VOXQ_Q4 ? launch_bn<VOXQ_Q4>(ga, bn, false, st) : launch_bn<VOXQ_Q8>(ga, bn, w->q8_signed != 0, st);
+    VoxCPMError e = pl.two_phase ? launch_f16(ga, bn, pl.nt, st)
+                    : qt == VOXQ_Q4 ? launch_bn<VOXQ_Q4>(ga, bn, false, st)
+                                    : launch_bn<VOXQ_Q8>(ga, bn, w->q8_signed != 0, st);
     if (e || pl.S == 1) return e;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -857,6 +1131,8 @@ VoxCPMError gemm_launch(const float* a, int M, int64_t lda, const voxq_qweight* 
         return gemm_by_rows(a, M, lda, w, out, ldo, epi, st);
     if ((reinterpret_cast<uintptr_t>(w->codes) & 15) || (reinterpret_cast<uintptr_t>(w->scales) & 15))
         return VOXCPM_ERR_UNSUPPORTED;
+    if (epi && epi->up && (epi->up->N != N || epi->up->K != K || epi->up->qtype != w->qtype))
+        return VOXCPM_ERR_SHAPE_MISMATCH;
     const GemmPlan pl = plan_gemm(M, N, K, w->qtype);
     const int mpad = (M + pl.bn - 1) / pl.bn * pl.bn;
     // workspace: a16t | ainv | split-K partials | SwiGLU gate
@@ -864,25 +1140,53 @@ VoxCPMError gemm_launch(const float* a, int M, int64_t lda, const voxq_qweight* 
     uint8_t* a16t = wsb;
     float* ainv = reinterpret_cast<float*>(wsb + align256((size_t)pad_rows(M) * K * 2));
     float* part = reinterpret_cast<float*>(wsb + act_bytes(M, K));
-    float* gbuf = reinterpret_cast<float*>(wsb + act_bytes(M, K) + part_bytes(pl));
-    {
+    __half* w16 = reinterpret_cast<__half*>(wsb + act_bytes(M, K) + part_bytes(pl));
+    float* gbuf = reinterpret_cast<float*>(wsb + act_bytes(M, K) + part_bytes(pl) + w16_bytes(pl, N, K));
+    // prepass: activations (+ for the two-phase plan, weight wq -> fp16), one launch
+    auto prep = [&](const voxq_qweight* wq, bool act) -> VoxCPMError {
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
-        cfg.gridDim = dim3(mpad);
         cfg.blockDim = dim3(kActThreads);
         pdl_config(cfg, attr, st);
-        VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, act_tile_kernel, a, M, K, lda, pl.bn, a16t, ainv));
-    }
+        const int act_blocks = act ? mpad : 0;
+        if (!pl.two_phase) {
+            cfg.gridDim = dim3(mpad);
+            VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, act_tile_kernel, a, M, K, lda, pl.bn, a16t, ainv));
+            return VOXCPM_SUCCESS;
+        }
+        const int64_t chunks = (int64_t)N * (K / 8);
+        const int64_t per_block = (int64_t)kActThreads * kPrepChunks;
+        cfg.gridDim = dim3((unsigned)(act_blocks + (chunks + per_block - 1) / per_block));
+        const uint8_t* codes = static_cast<const uint8_t*>(wq->codes);
+        const uint8_t* sc = static_cast<const uint8_t*>(wq->scales);
+        const float* rm = reinterpret_cast<const float*>(sc + rowmul_offset(N, K, wq->qtype));
+        if (wq->qtype == VOXQ_Q4)
+            VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, prep_f16_kernel<VOXQ_Q4, false>, a, M, K, lda, pl.bn, a16t, ainv,
+                                             act_blocks, codes, sc, rm, N, w16));
+        else if (wq->q8_signed)
+            VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, prep_f16_kernel<VOXQ_Q8, true>, a, M, K, lda, pl.bn, a16t, ainv,
+                                             act_blocks, codes, sc, rm, N, w16));
+        else
+            VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, prep_f16_kernel<VOXQ_Q8, false>, a, M, K, lda, pl.bn, a16t, ainv,
+                                             act_blocks, codes, sc, rm, N, w16));
+        return VOXCPM_SUCCESS;
+    };
+    VoxCPMError e = prep(w, true);
+    if (e) return e;
     const float* bias = epi ? epi->bias : nullptr;
     const float* res = epi ? epi->residual : nullptr;
     const int64_t ldr = epi ? epi->ldr : 0;
     if (epi && epi->up) {
         // SwiGLU: gate into the workspace, then up with silu(gate) * y fused
-        VoxCPMError e = gemm_one(pl, ainv, a16t, M, w, gbuf, N, nullptr, nullptr, 0, nullptr, 0, part, st);
+        e = gemm_one(pl, ainv, a16t, M, w, gbuf, N, nullptr, nullptr, 0, nullptr, 0, part, w16, st);
         if (e) return e;
-        return gemm_one(pl, ainv, a16t, M, epi->up, out, ldo, bias, res, ldr, gbuf, N, part, st);
+        if (pl.two_phase) {  // the up weight replaces the gate weight in w16 once the gate GEMM is done
+            e = prep(epi->up, false);
+            if (e) return e;
+        }
+        return gemm_one(pl, ainv, a16t, M, epi->up, out, ldo, bias, res, ldr, gbuf, N, part, w16, st);
     }
-    return gemm_one(pl, ainv, a16t, M, w, out, ldo, bias, res, ldr, nullptr, 0, part, st);
+    return gemm_one(pl, ainv, a16t, M, w, out, ldo, bias, res, ldr, nullptr, 0, part, w16, st);
 }
 
 }  // namespace voxq
