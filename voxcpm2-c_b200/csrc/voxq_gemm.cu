@@ -73,20 +73,40 @@ constexpr int raw_stages(int bn) { return bn >= 256 ? 3 : bn >= 128 ? 4 : 5; }
 // ---------------------------------------------------------------------------
 constexpr int kActThreads = 128;
 constexpr int kPrepChunks = 4;    // weight chunks per prepass thread
+constexpr int kActRegChunks = 4;  // activation chunks per prepass thread held in registers
 constexpr int kW16Rows = 256;     // rows per tile of the tiled fp16 weight (covers NT = 1 and 2)
 
 __device__ __forceinline__ void act_row(const float* __restrict__ a, int M, int K, int64_t lda, int bn,
                                         uint8_t* __restrict__ a16t, float* __restrict__ ainv, int m) {
+    // Each thread keeps its first kActRegChunks chunks (8 values each) in registers
+    // between the max pass and the conversion, so a row costs one load latency
+    // (K <= 128 x 8 x kActRegChunks); chunks beyond that are read again.
+    constexpr int RC = kActRegChunks;
     __shared__ float red[kActThreads / 32];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int KU = K / kBK, nch = K / 8;
     const bool live = m < M;
     const float* row = a + (int64_t)m * lda;
+    float4 v[RC][2];
     float mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < RC; i++) {
+        const int c = threadIdx.x + i * kActThreads;
+        v[i][0] = v[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (live && c < nch) {
+            v[i][0] = __ldg(reinterpret_cast<const float4*>(row + 8 * c));
+            v[i][1] = __ldg(reinterpret_cast<const float4*>(row + 8 * c + 4));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < RC; i++)
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i][h].x), fabsf(v[i][h].y)), fmaxf(fabsf(v[i][h].z), fabsf(v[i][h].w))));
     if (live) {
-        for (int c = threadIdx.x; c < nch; c += kActThreads) {
-            const float4 v0 = *reinterpret_cast<const float4*>(row + 8 * c);
-            const float4 v1 = *reinterpret_cast<const float4*>(row + 8 * c + 4);
+        for (int c = threadIdx.x + RC * kActThreads; c < nch; c += kActThreads) {
+            const float4 v0 = __ldg(reinterpret_cast<const float4*>(row + 8 * c));
+            const float4 v1 = __ldg(reinterpret_cast<const float4*>(row + 8 * c + 4));
             mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))));
             mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
         }
@@ -105,18 +125,26 @@ __device__ __forceinline__ void act_row(const float* __restrict__ a, int M, int 
     const float mul = ldexpf(1.0f, e);
     const int t = m / bn, r = m % bn;
     uint8_t* tb = a16t + ((int64_t)t * KU * bn + r) * 128;
-    for (int c = threadIdx.x; c < nch; c += kActThreads) {
-        uint4 h = make_uint4(0u, 0u, 0u, 0u);
-        if (live) {
-            const float4 v0 = *reinterpret_cast<const float4*>(row + 8 * c);
-            const float4 v1 = *reinterpret_cast<const float4*>(row + 8 * c + 4);
-            __half2 p0 = __floats2half2_rn(v0.x * mul, v0.y * mul), p1 = __floats2half2_rn(v0.z * mul, v0.w * mul);
-            __half2 p2 = __floats2half2_rn(v1.x * mul, v1.y * mul), p3 = __floats2half2_rn(v1.z * mul, v1.w * mul);
-            h = make_uint4(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1),
-                           *reinterpret_cast<uint32_t*>(&p2), *reinterpret_cast<uint32_t*>(&p3));
-        }
+    auto put = [&](int c, const float4& v0, const float4& v1) {
+        __half2 p0 = __floats2half2_rn(v0.x * mul, v0.y * mul), p1 = __floats2half2_rn(v0.z * mul, v0.w * mul);
+        __half2 p2 = __floats2half2_rn(v1.x * mul, v1.y * mul), p3 = __floats2half2_rn(v1.z * mul, v1.w * mul);
+        const uint4 h = make_uint4(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1),
+                                   *reinterpret_cast<uint32_t*>(&p2), *reinterpret_cast<uint32_t*>(&p3));
         const int u = c >> 3, j = c & 7;  // K stage, 16-byte chunk
         *reinterpret_cast<uint4*>(tb + (int64_t)u * bn * 128 + ((j ^ (r & 7)) << 4)) = h;
+    };
+#pragma unroll
+    for (int i = 0; i < RC; i++) {
+        const int c = threadIdx.x + i * kActThreads;
+        if (c < nch) put(c, v[i][0], v[i][1]);  // zeros for pad rows
+    }
+    for (int c = threadIdx.x + RC * kActThreads; c < nch; c += kActThreads) {
+        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+        if (live) {
+            v0 = __ldg(reinterpret_cast<const float4*>(row + 8 * c));
+            v1 = __ldg(reinterpret_cast<const float4*>(row + 8 * c + 4));
+        }
+        put(c, v0, v1);
     }
     if (threadIdx.x == 0) ainv[m] = live ? ldexpf(1.0f, -e) : 0.0f;
 }
