@@ -68,54 +68,52 @@ constexpr int raw_stages(int bn) { return bn >= 256 ? 3 : bn >= 128 ? 4 : 5; }
 // the BN x 64 fp16 block sits contiguously at ((t * KU + u) * BN) * 128 bytes
 // in the UMMA K-major 128-byte-swizzled order (16-byte chunk j of row r at
 // chunk j ^ (r & 7)), so the GEMM fetches it with one bulk copy.  Rows M ..
-// Mpad-1 are zero; ainv[m] = 2^-a (0 for pad rows).  One block per row, one
-// thread per 8 values, so a row costs one load latency, not K/128 of them.
+// Mpad-1 are zero; ainv[m] = 2^-a (0 for pad rows).  One warp per row: lane l
+// owns the 8-value chunks l, l + 32, ..., so every load of the row is in flight
+// before the first shuffle and no block barrier is needed.
 // ---------------------------------------------------------------------------
-constexpr int kActThreads = 128;
-constexpr int kPrepChunks = 4;    // weight chunks per prepass thread
-constexpr int kActRegChunks = 4;  // activation chunks per prepass thread held in registers
-constexpr int kW16Rows = 256;     // rows per tile of the tiled fp16 weight (covers NT = 1 and 2)
+constexpr int kPrepThreads = 256;                  // 8 independent row warps per block
+constexpr int kPrepRows = kPrepThreads / 32;
+constexpr int kRegIters = 4;                       // chunks per lane held in registers (K <= 1024 read once)
+constexpr int kW16Rows = 256;                      // rows per tile of the tiled fp16 weight (covers NT = 1 and 2)
+
+__device__ __forceinline__ uint4 half8(const float4& v0, const float4& v1, float mul) {
+    __half2 p0 = __floats2half2_rn(v0.x * mul, v0.y * mul), p1 = __floats2half2_rn(v0.z * mul, v0.w * mul);
+    __half2 p2 = __floats2half2_rn(v1.x * mul, v1.y * mul), p3 = __floats2half2_rn(v1.z * mul, v1.w * mul);
+    return make_uint4(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1),
+                      *reinterpret_cast<uint32_t*>(&p2), *reinterpret_cast<uint32_t*>(&p3));
+}
+
+__device__ __forceinline__ float absmax8(const float4& v0, const float4& v1) {
+    return fmaxf(fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))),
+                 fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
+}
 
 __device__ __forceinline__ void act_row(const float* __restrict__ a, int M, int K, int64_t lda, int bn,
-                                        uint8_t* __restrict__ a16t, float* __restrict__ ainv, int m) {
-    // Each thread keeps its first kActRegChunks chunks (8 values each) in registers
-    // between the max pass and the conversion, so a row costs one load latency
-    // (K <= 128 x 8 x kActRegChunks); chunks beyond that are read again.
-    constexpr int RC = kActRegChunks;
-    __shared__ float red[kActThreads / 32];
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+                                        uint8_t* __restrict__ a16t, float* __restrict__ ainv, int m, int lane) {
+    constexpr int RI = kRegIters;
     const int KU = K / kBK, nch = K / 8;
     const bool live = m < M;
     const float* row = a + (int64_t)m * lda;
-    float4 v[RC][2];
-    float mx = 0.0f;
+    float4 v[RI][2];
 #pragma unroll
-    for (int i = 0; i < RC; i++) {
-        const int c = threadIdx.x + i * kActThreads;
+    for (int i = 0; i < RI; i++) {
+        const int c = lane + 32 * i;
         v[i][0] = v[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (live && c < nch) {
             v[i][0] = __ldg(reinterpret_cast<const float4*>(row + 8 * c));
             v[i][1] = __ldg(reinterpret_cast<const float4*>(row + 8 * c + 4));
         }
     }
+    float mx = 0.0f;
 #pragma unroll
-    for (int i = 0; i < RC; i++)
-#pragma unroll
-        for (int h = 0; h < 2; h++)
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i][h].x), fabsf(v[i][h].y)), fmaxf(fabsf(v[i][h].z), fabsf(v[i][h].w))));
+    for (int i = 0; i < RI; i++) mx = fmaxf(mx, absmax8(v[i][0], v[i][1]));
     if (live) {
-        for (int c = threadIdx.x + RC * kActThreads; c < nch; c += kActThreads) {
-            const float4 v0 = __ldg(reinterpret_cast<const float4*>(row + 8 * c));
-            const float4 v1 = __ldg(reinterpret_cast<const float4*>(row + 8 * c + 4));
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))));
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
-        }
+        for (int c = lane + 32 * RI; c < nch; c += 32)
+            mx = fmaxf(mx, absmax8(__ldg(reinterpret_cast<const float4*>(row + 8 * c)),
+                                   __ldg(reinterpret_cast<const float4*>(row + 8 * c + 4))));
     }
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) red[wid] = mx;
-    __syncthreads();
-#pragma unroll
-    for (int w = 0; w < kActThreads / 32; w++) mx = fmaxf(mx, red[w]);
     int e = 0;
     if (mx > 0.0f && isfinite(mx)) {
         int x;
@@ -125,36 +123,32 @@ __device__ __forceinline__ void act_row(const float* __restrict__ a, int M, int 
     const float mul = ldexpf(1.0f, e);
     const int t = m / bn, r = m % bn;
     uint8_t* tb = a16t + ((int64_t)t * KU * bn + r) * 128;
-    auto put = [&](int c, const float4& v0, const float4& v1) {
-        __half2 p0 = __floats2half2_rn(v0.x * mul, v0.y * mul), p1 = __floats2half2_rn(v0.z * mul, v0.w * mul);
-        __half2 p2 = __floats2half2_rn(v1.x * mul, v1.y * mul), p3 = __floats2half2_rn(v1.z * mul, v1.w * mul);
-        const uint4 h = make_uint4(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1),
-                                   *reinterpret_cast<uint32_t*>(&p2), *reinterpret_cast<uint32_t*>(&p3));
-        const int u = c >> 3, j = c & 7;  // K stage, 16-byte chunk
-        *reinterpret_cast<uint4*>(tb + (int64_t)u * bn * 128 + ((j ^ (r & 7)) << 4)) = h;
-    };
+    const int64_t ustride = (int64_t)bn * 128;
 #pragma unroll
-    for (int i = 0; i < RC; i++) {
-        const int c = threadIdx.x + i * kActThreads;
-        if (c < nch) put(c, v[i][0], v[i][1]);  // zeros for pad rows
+    for (int i = 0; i < RI; i++) {
+        const int c = lane + 32 * i;  // K stage c >> 3, 16-byte chunk c & 7
+        if (c < nch)
+            *reinterpret_cast<uint4*>(tb + (c >> 3) * ustride + (((c & 7) ^ (r & 7)) << 4)) =
+                half8(v[i][0], v[i][1], mul);  // zeros for pad rows
     }
-    for (int c = threadIdx.x + RC * kActThreads; c < nch; c += kActThreads) {
+    for (int c = lane + 32 * RI; c < nch; c += 32) {
         float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
         if (live) {
             v0 = __ldg(reinterpret_cast<const float4*>(row + 8 * c));
             v1 = __ldg(reinterpret_cast<const float4*>(row + 8 * c + 4));
         }
-        put(c, v0, v1);
+        *reinterpret_cast<uint4*>(tb + (c >> 3) * ustride + (((c & 7) ^ (r & 7)) << 4)) = half8(v0, v1, mul);
     }
-    if (threadIdx.x == 0) ainv[m] = live ? ldexpf(1.0f, -e) : 0.0f;
+    if (lane == 0) ainv[m] = live ? ldexpf(1.0f, -e) : 0.0f;
 }
 
-__global__ void __launch_bounds__(kActThreads) act_tile_kernel(const float* __restrict__ a, int M, int K, int64_t lda,
-                                                               int bn, uint8_t* __restrict__ a16t,
-                                                               float* __restrict__ ainv) {
+__global__ void __launch_bounds__(kPrepThreads) act_tile_kernel(const float* __restrict__ a, int M, int K, int64_t lda,
+                                                                int bn, uint8_t* __restrict__ a16t,
+                                                                float* __restrict__ ainv, int rows) {
     pdl_wait();
     pdl_launch_dependents();
-    act_row(a, M, K, lda, bn, a16t, ainv, blockIdx.x);
+    const int m = blockIdx.x * kPrepRows + (threadIdx.x >> 5);
+    if (m < rows) act_row(a, M, K, lda, bn, a16t, ainv, m, threadIdx.x & 31);
 }
 
 // ---------------------------------------------------------------------------
@@ -643,55 +637,65 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 // shared-memory round trip and proxy fences from the main loop.
 // ---------------------------------------------------------------------------
 template <int QT, bool SIGNED>
-__global__ void __launch_bounds__(kActThreads) prep_f16_kernel(const float* __restrict__ a, int M, int K, int64_t lda,
-                                                               int bn, uint8_t* __restrict__ a16t,
-                                                               float* __restrict__ ainv, int act_blocks,
-                                                               const uint8_t* __restrict__ codes,
-                                                               const uint8_t* __restrict__ scales,
-                                                               const float* __restrict__ rowmul, int N,
-                                                               __half* __restrict__ w16) {
+__global__ void __launch_bounds__(kPrepThreads) prep_f16_kernel(const float* __restrict__ a, int M, int K, int64_t lda,
+                                                                int bn, uint8_t* __restrict__ a16t,
+                                                                float* __restrict__ ainv, int act_rows,
+                                                                const uint8_t* __restrict__ codes,
+                                                                const uint8_t* __restrict__ scales,
+                                                                const float* __restrict__ rowmul, int N,
+                                                                __half* __restrict__ w16) {
     pdl_wait();  // activations may come from the previous kernel; w16 may still be read by it
     pdl_launch_dependents();
-    if ((int)blockIdx.x < act_blocks) {
-        act_row(a, M, K, lda, bn, a16t, ainv, blockIdx.x);
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kPrepRows + (threadIdx.x >> 5);
+    if (row < act_rows) {
+        act_row(a, M, K, lda, bn, a16t, ainv, row, lane);
         return;
     }
-    // Weight chunks: thread c handles 8 consecutive weights (one 16-byte fp16
-    // chunk) of kPrepChunks chunk slots strided by the grid.  Output layout: the
-    // shared-memory image of each (256-row tile, 64-wide K stage) -- rows r of
-    // 128 bytes, 16-byte chunk j of row r at j ^ (r & 7) -- contiguous, so the
-    // GEMM fetches a stage's weights with one bulk copy.
+    const int n = row - act_rows;
+    if (n >= N) return;
+    // Weight row n: lane l dequantizes the 8-weight chunks l, l + 32, ... (one
+    // 16-byte fp16 chunk each), all of a group's codes and trailers loaded before
+    // the first conversion.  Output layout: the shared-memory image of each
+    // (256-row tile, 64-wide K stage) -- rows r of 128 bytes, 16-byte chunk j of
+    // row r at j ^ (r & 7) -- contiguous, so the GEMM fetches a stage's weights
+    // with one bulk copy.
+    constexpr int RI = kRegIters;
     const int cpr = K / 8, KU = K / kBK;
-    const int64_t total = (int64_t)N * cpr;
     const int64_t rowb = codes_row_bytes(K, QT), srow = (int64_t)(K / VOXQ_QBLK) * scale_bytes(QT);
-    const int64_t nthreads = (int64_t)(gridDim.x - act_blocks) * kActThreads;
-    const int64_t t0 = (int64_t)(blockIdx.x - act_blocks) * kActThreads + threadIdx.x;
+    const uint8_t* crow = codes + n * rowb;
+    const uint8_t* srow_p = scales + n * srow;
+    const float rm = __ldg(rowmul + n);
+    const int tp = n / kW16Rows, r = n % kW16Rows;
+    uint8_t* tb = reinterpret_cast<uint8_t*>(w16) + ((int64_t)tp * KU * kW16Rows + r) * 128;
+    const int64_t ustride = (int64_t)kW16Rows * 128;
+    for (int c0 = 0; c0 < cpr; c0 += 32 * RI) {
+        uint32_t lo[RI], hi[RI];
+        float2 tr[RI];
 #pragma unroll
-    for (int i = 0; i < kPrepChunks; i++) {
-        const int64_t chunk = t0 + i * nthreads;
-        if (chunk >= total) break;
-        const int n = (int)(chunk / cpr), c = (int)(chunk % cpr), k0 = c * 8;
-        const int blk = k0 / VOXQ_QBLK;
-        const float rm = __ldg(rowmul + n);
-        uint32_t lo, hi = 0;
-        float sc, mn;
-        if (QT == VOXQ_Q8) {
-            const uint2 cw = __ldg(reinterpret_cast<const uint2*>(codes + n * rowb + k0));
-            lo = cw.x;
-            hi = cw.y;
-            const float2 tr = __ldg(reinterpret_cast<const float2*>(scales + n * srow + 8 * blk));
-            sc = tr.x;
-            mn = tr.y;
-        } else {
-            lo = __ldg(reinterpret_cast<const uint32_t*>(codes + n * rowb + k0 / 2));
-            const float2 tr = __half22float2(*reinterpret_cast<const __half2*>(scales + n * srow + 4 * blk));
-            sc = tr.x;
-            mn = tr.y;
+        for (int i = 0; i < RI; i++) {
+            const int c = c0 + lane + 32 * i;  // block c / 4 of 32 weights
+            lo[i] = hi[i] = 0u;
+            tr[i] = make_float2(0.f, 0.f);
+            if (c < cpr) {
+                if (QT == VOXQ_Q8) {
+                    const uint2 cw = __ldg(reinterpret_cast<const uint2*>(crow + 8 * c));
+                    lo[i] = cw.x;
+                    hi[i] = cw.y;
+                    tr[i] = __ldg(reinterpret_cast<const float2*>(srow_p + 8 * (c >> 2)));
+                } else {
+                    lo[i] = __ldg(reinterpret_cast<const uint32_t*>(crow + 4 * c));
+                    tr[i] = __half22float2(*reinterpret_cast<const __half2*>(srow_p + 4 * (c >> 2)));
+                }
+            }
         }
-        const int tp = n / kW16Rows, r = n % kW16Rows, u = c >> 3, j = c & 7;
-        uint8_t* dst = reinterpret_cast<uint8_t*>(w16) + (((int64_t)tp * KU + u) * kW16Rows + r) * 128 +
-                       ((j ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = deq8<QT, SIGNED>(lo, hi, sc * rm, mn * rm);
+#pragma unroll
+        for (int i = 0; i < RI; i++) {
+            const int c = c0 + lane + 32 * i;
+            if (c < cpr)
+                *reinterpret_cast<uint4*>(tb + (c >> 3) * ustride + (((c & 7) ^ (r & 7)) << 4)) =
+                    deq8<QT, SIGNED>(lo[i], hi[i], tr[i].x * rm, tr[i].y * rm);
+        }
     }
 }
 
@@ -1174,17 +1178,15 @@ VoxCPMError gemm_launch(const float* a, int M, int64_t lda, const voxq_qweight* 
     auto prep = [&](const voxq_qweight* wq, bool act) -> VoxCPMError {
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
-        cfg.blockDim = dim3(kActThreads);
+        cfg.blockDim = dim3(kPrepThreads);
         pdl_config(cfg, attr, st);
-        const int act_blocks = act ? mpad : 0;
+        const int act_blocks = act ? mpad : 0;  // activation rows (one warp each)
         if (!pl.two_phase) {
-            cfg.gridDim = dim3(mpad);
-            VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, act_tile_kernel, a, M, K, lda, pl.bn, a16t, ainv));
+            cfg.gridDim = dim3((unsigned)((mpad + kPrepRows - 1) / kPrepRows));
+            VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, act_tile_kernel, a, M, K, lda, pl.bn, a16t, ainv, mpad));
             return VOXCPM_SUCCESS;
         }
-        const int64_t chunks = (int64_t)N * (K / 8);
-        const int64_t per_block = (int64_t)kActThreads * kPrepChunks;
-        cfg.gridDim = dim3((unsigned)(act_blocks + (chunks + per_block - 1) / per_block));
+        cfg.gridDim = dim3((unsigned)(((int64_t)act_blocks + N + kPrepRows - 1) / kPrepRows));
         const uint8_t* codes = static_cast<const uint8_t*>(wq->codes);
         const uint8_t* sc = static_cast<const uint8_t*>(wq->scales);
         const float* rm = reinterpret_cast<const float*>(sc + rowmul_offset(N, K, wq->qtype));
