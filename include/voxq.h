@@ -255,6 +255,54 @@ typedef struct {
 
 VOXQ_API VoxCPMError voxq_gemv_batch(const voxq_gemv_item* items, int count, void* stream);
 
+/* ---- quantize.py weight containers (VXCPM2) ---------------------------
+ * Reads the container written by the reference's quantizer
+ * (scripts/quantize.py:110-312): a 256-byte header, the layer-group offset
+ * table, and tensors stored as (name_hash, ndim, dims[3]) + data in the file's
+ * quant type (f32, f16, 20-byte Q4 or 40-byte Q8 blocks over the flattened
+ * tensor).  The reference's C loader cannot read these files (it knows only
+ * the VXCP format, src/model.c:1715-1727, 1815-1858); this reader takes 2-D
+ * Q4 / Q8 tensors straight to the packed device layout, bytes unchanged.
+ * Host calls; the file stays mapped until voxq_vxcpm2_close. */
+typedef struct voxq_vxcpm2 voxq_vxcpm2;  /* opaque */
+typedef struct {
+    uint32_t version, n_layers, n_layers_enc, n_ralm_layers, n_dit_layers;
+    uint32_t d_model, d_ff, n_heads, n_kv_heads, head_dim, max_seq_len, vocab_size;
+    uint32_t quant;            /* 0 f32, 1 f16, 2 q4, 3 q8 (VOXQ_F32 .. VOXQ_Q8) */
+    uint32_t sample_rate, audio_vae_dim;
+    float rope_theta;
+    uint64_t checksum;         /* as stored at byte 72 */
+    uint32_t n_groups;
+} voxq_vxcpm2_header;
+typedef struct {
+    uint32_t name_hash, ndim, dims[3];
+    int32_t dtype;             /* the file's quant type */
+    int32_t group;             /* layer group */
+    uint64_t elements;         /* prod(dims[:ndim]) */
+    uint64_t offset, bytes;    /* data (after the 20-byte tensor header) in the file */
+} voxq_vxcpm2_tensor;
+
+/* VOXCPM_ERR_FILE_NOT_FOUND, _INVALID_MODEL (magic, bounds, truncated tensor)
+ * or _UNSUPPORTED (unknown quant type). */
+VOXQ_API VoxCPMError voxq_vxcpm2_open(const char* path, voxq_vxcpm2** out);
+VOXQ_API void voxq_vxcpm2_close(voxq_vxcpm2* f);
+VOXQ_API VoxCPMError voxq_vxcpm2_info(const voxq_vxcpm2* f, voxq_vxcpm2_header* hdr, int* n_tensors);
+VOXQ_API VoxCPMError voxq_vxcpm2_tensor_info(const voxq_vxcpm2* f, int i, voxq_vxcpm2_tensor* t);
+/* Host pointer to tensor i's data inside the mapped file. */
+VOXQ_API const uint8_t* voxq_vxcpm2_data(const voxq_vxcpm2* f, int i);
+/* SHA-256 checksum of scripts/quantize.py:309-315; VOXCPM_ERR_INVALID_MODEL on
+ * mismatch, VOXCPM_ERR_UNSUPPORTED when the stored value is 0 (the reference
+ * quantizer leaves it 0: it raises before writing it, scripts/quantize.py:308-310). */
+VOXQ_API VoxCPMError voxq_vxcpm2_verify(const voxq_vxcpm2* f);
+/* Tensor i as fp32 on the host (dequantize_q4_block / dequantize_q8_block of
+ * scripts/quantize.py:56-82; q8_signed selects the signed Q8 reading). */
+VOXQ_API VoxCPMError voxq_vxcpm2_dequantize(const voxq_vxcpm2* f, int i, int q8_signed, float* h_out);
+/* 2-D Q4 / Q8 tensor i ([N][K], K % 32 == 0) -> packed device weight
+ * (arrays sized by voxq_codes_bytes / voxq_scales_bytes).  Returns after the
+ * copy is complete. */
+VOXQ_API VoxCPMError voxq_vxcpm2_upload_qweight(const voxq_vxcpm2* f, int i, uint8_t* d_codes, void* d_scales,
+                                              void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -16,7 +16,8 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def header_functions():
     src = open(os.path.join(REPO, "include", "voxq.h")).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return re.findall(r"^VOXQ_API\s+(?:VoxCPMError|void|size_t|int|const char\s*\*)\s*(\w+)\s*\(", src, flags=re.M)
+    return re.findall(r"^VOXQ_API\s+(?:VoxCPMError|void|size_t|int|const char\s*\*|const uint8_t\s*\*)\s*(\w+)\s*\(",
+                      src, flags=re.M)
 
 
 def test_header_declares_reference_block():

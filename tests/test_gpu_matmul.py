@@ -133,6 +133,24 @@ def test_batch_equals_single_calls():
         assert torch.equal(s["out"], ref_out)
 
 
+@pytest.mark.parametrize("qt", [voxq.Q4, voxq.Q8])
+def test_gemv_result_independent_of_launch_size(qt):
+    """A single-row GEMV gives the same bits alone (small launch: short tiles)
+    and inside a large batch (full-height tiles), and matches the oracle."""
+    N, K, n = 4096, 1024, 48
+    qw, wdeq = make_weight(N, K, qt, seed=900)
+    a = O.rand_normal(901, K).reshape(1, K)
+    at = torch.from_numpy(a).cuda()
+    alone = voxq.matmul_nt_q(at, qw)
+    outs = [torch.full((1, N), float("nan"), device="cuda") for _ in range(n)]
+    voxq.gemv_batch(voxq.make_gemv_items([dict(w=qw, a=at, out=o) for o in outs]))
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o, alone)
+    y, sc = ref(a, wdeq)
+    assert_matmul_close(alone.cpu().numpy(), y, sc, TOL_GEMV)
+
+
 def test_batch_mixed_formats_and_epilogues():
     specs, wants = [], []
     for i, (qt, M, swi) in enumerate([(voxq.Q8, 1, False), (voxq.Q4, 2, True), (voxq.Q8, 5, True),

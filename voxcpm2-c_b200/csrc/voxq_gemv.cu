@@ -85,7 +85,6 @@ __global__ void __launch_bounds__(256) limb_kernel(const __grid_constant__ LimbP
     pdl_launch_dependents();
     constexpr int TPC = QT == VOXQ_Q4 ? 4 : 2;  // threads per chunk
     constexpr int G = limb_granules(QT);
-    const int lane = threadIdx.x & 31;
     int j = 0;
     // every chunk's threads sit in one warp (TPC divides 32), and the loop
     // stride is a multiple of 32, so shuffles stay within live groups
@@ -197,6 +196,7 @@ struct GemvItemDev {
     int32_t slabs;       // ceil(chunks / 32)
     int32_t T;           // rows per tile
     int32_t tile_begin;  // first global tile of this item
+    int32_t parts;       // tensor-path kernel: K parts of groups_per_part 4-chunk groups
     int32_t pad;
 };
 
@@ -249,6 +249,46 @@ __device__ __forceinline__ float transpose_reduce(float (&v)[V], int lane) {
 template <int MAXI>
 __device__ __forceinline__ void fix_item(const GemvParams<MAXI>& p, int tile, int& item) {
     while (item + 1 < p.count && tile >= p.it[item + 1].tile_begin) item++;
+}
+
+// Producer (lane 0 of the producer warp): streams the tiles [tb, te) into a
+// STAGES-deep ring, two cp.async.bulk copies per weight and stage (codes of
+// the tile's T rows, then the 16-byte aligned window of their trailers).
+template <int STAGES, int TILE, int TW, int NW, int MAXI>
+__device__ __forceinline__ void produce_tiles(const GemvParams<MAXI>& p, int tb, int te, uint64_t* full,
+                                              uint64_t* empty, uint8_t* smem) {
+    constexpr int CW = TILE / NW;
+    constexpr int STAGE = TILE + NW * TW;
+    int item = 0;
+    for (int t = tb, j = 0; t < te; ++t, ++j) {
+        fix_item(p, t, item);
+        const GemvItemDev& it = p.it[item];
+        const int s = j % STAGES;
+        if (j >= STAGES) mbar_wait_bounded(&empty[s], ((j / STAGES) & 1) ^ 1, VOXQ_DEVERR_WAIT_EMPTY, p.err);
+        const int row0 = (t - it.tile_begin) * it.T;
+        const int rows = min(it.T, it.N - row0);
+        const uint32_t cb = (uint32_t)(rows * it.rowb);
+        const int64_t so = (int64_t)row0 * it.srow;
+        const int64_t sa = so & ~(int64_t)15;
+        const uint32_t tbytes = (uint32_t)(((so - sa) + (int64_t)rows * it.srow + 15) & ~(int64_t)15);
+        mbar_arrive_expect_tx(&full[s], NW * (cb + tbytes));
+        uint8_t* st = smem + s * STAGE;
+#pragma unroll
+        for (int w = 0; w < NW; w++) {
+            const uint8_t* c = w ? it.up_codes : it.codes;
+            const uint8_t* sc = w ? it.up_scales : it.scales;
+            bulk_g2s(st + w * CW, c + (int64_t)row0 * it.rowb, cb, &full[s]);
+            bulk_g2s(st + TILE + w * TW, sc + sa, tbytes, &full[s]);
+        }
+    }
+    // Normally the consumers have waited for every copy.  If a wait gave up,
+    // give the copies still in flight a bounded moment to land before the
+    // CTA's shared memory is released.
+    if (*reinterpret_cast<volatile int*>(p.err) != 0) {
+        const int n = te - tb;
+        for (int j = (n > STAGES ? n - STAGES : 0); j < n; j++)
+            mbar_wait_bounded(&full[j % STAGES], (j / STAGES) & 1, VOXQ_DEVERR_WAIT_FULL, p.err, 20u);
+    }
 }
 
 // Epilogue of one finished output element.
@@ -340,39 +380,7 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32) gemv_kernel(const __gri
     const int te = (int)((int64_t)p.total_tiles * (blockIdx.x + 1) / gridDim.x);
 
     if (warp == kConsumers) {
-        // ---------------- producer ----------------
-        if (lane == 0) {
-            int item = 0;
-            for (int t = tb, j = 0; t < te; ++t, ++j) {
-                fix_item(p, t, item);
-                const GemvItemDev& it = p.it[item];
-                const int s = j % kStages;
-                if (j >= kStages) mbar_wait_bounded(&empty[s], ((j / kStages) & 1) ^ 1, VOXQ_DEVERR_WAIT_EMPTY, p.err);
-                const int row0 = (t - it.tile_begin) * it.T;
-                const int rows = min(it.T, it.N - row0);
-                const uint32_t cb = (uint32_t)(rows * it.rowb);
-                const int64_t so = (int64_t)row0 * it.srow;
-                const int64_t sa = so & ~(int64_t)15;
-                const uint32_t tbytes = (uint32_t)(((so - sa) + (int64_t)rows * it.srow + 15) & ~(int64_t)15);
-                mbar_arrive_expect_tx(&full[s], NW * (cb + tbytes));
-                uint8_t* st = smem + s * STAGE;
-#pragma unroll
-                for (int w = 0; w < NW; w++) {
-                    const uint8_t* c = w ? it.up_codes : it.codes;
-                    const uint8_t* sc = w ? it.up_scales : it.scales;
-                    bulk_g2s(st + w * CW, c + (int64_t)row0 * it.rowb, cb, &full[s]);
-                    bulk_g2s(st + kTile + w * TW, sc + sa, tbytes, &full[s]);
-                }
-            }
-            // Normally the consumers have waited for every copy.  If a wait gave
-            // up, give the copies still in flight a bounded moment to land before
-            // the CTA's shared memory is released.
-            if (*reinterpret_cast<volatile int*>(p.err) != 0) {
-                const int n = te - tb;
-                for (int j = (n > kStages ? n - kStages : 0); j < n; j++)
-                    mbar_wait_bounded(&full[j % kStages], (j / kStages) & 1, VOXQ_DEVERR_WAIT_FULL, p.err, 20u);
-            }
-        }
+        if (lane == 0) produce_tiles<kStages, kTile, TW, NW>(p, tb, te, full, empty, smem);
         pdl_launch_dependents();
         return;
     }
@@ -505,6 +513,260 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32) gemv_kernel(const __gri
     }
 }
 
+// ---------------------------------------------------------------------------
+// Single-row GEMV (M = 1, one weight per item) on the integer tensor path.
+//
+// The same exact limb formulation, with the integer dot products done by
+// mma.sync.m16n8k32 (u8 or s8 codes x s8 limbs, s32 accumulate) instead of
+// dp4a.  A tile of the MMA is 16 weight rows x 32 K-slots; lane (g, t) of
+// the warp (g = lane / 4, t = lane % 4) supplies the A bytes of rows g and
+// g + 8 for slots 4t .. 4t+3 and 16+4t .. 16+4t+3.  Each lane takes ONE
+// 16-byte code chunk c = 4 * group + t of those rows, so the four lanes t
+// of a group cover four consecutive chunks.  The activation limbs go into B
+// block-diagonally: column 2t + L holds limb L of chunk t on the slots of
+// lane t and zeros elsewhere, so D[row][2t + L] is exactly chunk t's limb-L
+// dot product -- the per-chunk scales and per-block trailers are applied to
+// the D fragment that lane t itself holds (c0, c1: row g; c2, c3: row g + 8).
+//   Q4 chunk (32 codes): words j, j+1 give one MMA on their odd codes
+//     (w & 0x0F0F0F0F) and one on 16 x their even codes (w & 0xF0F0F0F0),
+//     into separate accumulators (16 S = 16 D_odd + D_even, exact); the limb
+//     record stores the odd / even limbs of each word in the same order.
+//     Four MMAs per chunk.
+//   Q8 chunk (16 codes): words 2j, 2j+1 are a0, a2 as they are.  Two MMAs.
+// The third limb (rare: chunks with a dominant value) is a second block-
+// diagonal B in column 2t, issued only when a lane of the warp needs it.
+//
+// A stage holds T rows (at most 32 KB of codes); two stages per CTA and two
+// CTAs per SM, whose tiles run out of phase.  K is cut into fixed parts of
+// groups_per_part groups (four chunks each); a stage's work is (16-row tile,
+// K part) units spread over the 8 consumer warps, and each row's parts are
+// summed in part order through shared memory.  The summation order depends
+// only on K, not on T, so the launch may pick T (smaller tiles for small
+// launches) without changing a single bit of the result.
+// ---------------------------------------------------------------------------
+constexpr int kMmaWarps = 8;                     // consumer warps (+1 producer)
+constexpr int kMmaStages = 2;
+constexpr int kMmaTile = 32768;                  // code bytes per stage
+constexpr int kMmaTW = kMmaTile / 4 + 32;        // trailer window bytes per stage
+constexpr int kMmaSmem = kMmaStages * (kMmaTile + kMmaTW);
+// groups (four 16-byte chunks of a row) per K part: 256 bytes of Q4 codes, 128 of Q8
+__host__ __device__ constexpr int groups_per_part(int qtype) { return qtype == VOXQ_Q4 ? 4 : 2; }
+constexpr int kPartSlots = 256;                 // >= T x parts (T x rowb <= kMmaTile)
+
+template <bool SA>
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    if (SA)
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%0,%1,%2,%3};"
+                     : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                     : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else
+        asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%0,%1,%2,%3};"
+                     : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                     : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// The chunk's code dot products with one limb set: D += codes x B, where this
+// lane's B words are bw (Q4: 4 odd-code words then 4 even-code words; Q8: 4
+// words in element order) or zero.
+template <int QT, bool SIGNED>
+__device__ __forceinline__ void chunk_mma(int (&d)[4], const uint4& wa, const uint4& wb, const uint32_t (&bw)[8]) {
+    const uint32_t xa[4] = {wa.x, wa.y, wa.z, wa.w}, xb[4] = {wb.x, wb.y, wb.z, wb.w};
+    if (QT == VOXQ_Q4) {
+        int dh[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {
+            imma16832<false>(d, xa[j] & 0x0F0F0F0Fu, xb[j] & 0x0F0F0F0Fu, xa[j + 1] & 0x0F0F0F0Fu,
+                             xb[j + 1] & 0x0F0F0F0Fu, bw[j], bw[j + 1]);
+            imma16832<false>(dh, xa[j] & 0xF0F0F0F0u, xb[j] & 0xF0F0F0F0u, xa[j + 1] & 0xF0F0F0F0u,
+                             xb[j + 1] & 0xF0F0F0F0u, bw[4 + j], bw[5 + j]);
+        }
+        // 16 x (odd + even) sums
+#pragma unroll
+        for (int i = 0; i < 4; i++) d[i] = dh[i] + (d[i] << 4);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 2; j++) imma16832<SIGNED>(d, xa[2 * j], xb[2 * j], xa[2 * j + 1], xb[2 * j + 1], bw[2 * j], bw[2 * j + 1]);
+    }
+}
+
+__device__ const uint4 kZeroLimbs[2] = {};
+
+// Limb L (0 .. 2) of this lane's chunk, or zeros (read from a zero block, so
+// the loads are unconditional).
+template <int QT>
+__device__ __forceinline__ void load_limbs(uint32_t (&bw)[8], const uint4* lp, int chunks, int L, bool on) {
+    const uint4* po = on ? lp + (int64_t)((QT == VOXQ_Q4) ? 2 * L : L) * chunks : &kZeroLimbs[0];
+    const uint4 o = __ldg(po);
+    bw[0] = o.x; bw[1] = o.y; bw[2] = o.z; bw[3] = o.w;
+    if (QT == VOXQ_Q4) {
+        const uint4 e = __ldg(on ? po + chunks : &kZeroLimbs[1]);
+        bw[4] = e.x; bw[5] = e.y; bw[6] = e.z; bw[7] = e.w;
+    } else {
+        bw[4] = bw[5] = bw[6] = bw[7] = 0u;
+    }
+}
+
+template <int QT, bool SIGNED, int MAXI>
+__global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const __grid_constant__ GemvParams<MAXI> p) {
+    constexpr int G = limb_granules(QT);
+    constexpr int SB = (QT == VOXQ_Q4) ? 4 : 8;  // trailer bytes per block
+    constexpr int STAGE = kMmaTile + kMmaTW;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t full[kMmaStages], empty[kMmaStages];
+    // row sums of each (row tile, K part) unit; two sets, alternating between
+    // the tiles that combine parts, so a set is rewritten only after every
+    // warp has passed the next combining tile's barrier
+    __shared__ float part[2][kPartSlots];  // [row][K part] of a stage's rows
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kMmaStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kMmaWarps);
+        }
+    }
+    mbar_fence_init();
+    __syncthreads();
+
+    const int tb = (int)((int64_t)p.total_tiles * blockIdx.x / gridDim.x);
+    const int te = (int)((int64_t)p.total_tiles * (blockIdx.x + 1) / gridDim.x);
+
+    if (warp == kMmaWarps) {
+        if (lane == 0) produce_tiles<kMmaStages, kMmaTile, kMmaTW, 1>(p, tb, te, full, empty, smem);
+        pdl_launch_dependents();
+        return;
+    }
+
+    pdl_wait();  // limbs come from the prepass launched just before this kernel
+    pdl_launch_dependents();
+    const int g = lane >> 2, tq = lane & 3;
+    const int L = g - 2 * tq;  // limb this lane feeds into B (column 2t + L), if 0 or 1
+    const bool limb_lane = (unsigned)L < 2u;
+    int item = -1, pset = 0;
+    // per-item constants (refreshed when the tile range enters a new item)
+    int P = 1, rt0 = 0, kp0 = 0, ngr = 1, chunks = 1, rowb = 0, srow = 0, T = 1, N = 0, tbeg = 0;
+    const uint4* limbs = nullptr;
+    for (int t = tb, j = 0; t < te; ++t, ++j) {
+        int nitem = item < 0 ? 0 : item;
+        fix_item(p, t, nitem);
+        if (nitem != item) {
+            item = nitem;
+            const GemvItemDev& it = p.it[item];
+            P = it.parts;
+            rt0 = warp / P;  // this warp's first unit
+            kp0 = warp % P;
+            chunks = it.chunks;
+            ngr = (chunks + 3) >> 2;
+            rowb = it.rowb;
+            srow = it.srow;
+            T = it.T;
+            N = it.N;
+            tbeg = it.tile_begin;
+            limbs = it.limbs;
+        }
+        const int s = j % kMmaStages;
+        // a wait that gives up records the error and the tile is processed
+        // anyway (garbage), so every warp still meets the same barriers
+        mbar_wait_bounded(&full[s], (j / kMmaStages) & 1, VOXQ_DEVERR_WAIT_FULL, p.err);
+        const uint8_t* st = smem + s * STAGE;
+        const int row0 = (t - tbeg) * T;
+        const int rows = min(T, N - row0);
+        const uint8_t* trs = st + kMmaTile + (int)(((int64_t)row0 * srow) & 15);
+        const int nrt = (rows + 15) >> 4;  // 16-row tiles
+        for (int rt = rt0, kp = kp0; rt < nrt;) {
+            const int rA = min(rt * 16 + g, rows - 1), rB = min(rt * 16 + g + 8, rows - 1);
+            const uint8_t* pa = st + rA * rowb;
+            const uint8_t* pb = st + rB * rowb;
+            const uint8_t* ta = trs + rA * srow;
+            const uint8_t* tb2 = trs + rB * srow;
+            float accA = 0.0f, accB = 0.0f;
+            constexpr int GPP = groups_per_part(QT);
+            const int g1 = min(ngr, (kp + 1) * GPP);
+#pragma unroll
+            for (int gr = kp * GPP; gr < g1; gr++) {
+                const int c = gr * 4 + tq;  // this lane's chunk
+                const bool cok = c < chunks;
+                const int cc = cok ? c : chunks - 1;
+                const uint4 wa = *reinterpret_cast<const uint4*>(pa + cc * 16);
+                const uint4 wb = *reinterpret_cast<const uint4*>(pb + cc * 16);
+                const uint4* lp = limbs + cc;  // [granule][chunks] of activation row 0
+                const uint4 rec = __ldg(lp + (int64_t)(G - 1) * chunks);
+                uint32_t bw[8];
+                load_limbs<QT>(bw, lp, chunks, L, cok && limb_lane);
+                int d[4] = {0, 0, 0, 0};
+                chunk_mma<QT, SIGNED>(d, wa, wb, bw);
+                int d3v[4] = {0, 0, 0, 0};
+                const bool use3 = __any_sync(0xffffffffu, cok && rec.z != 0u);
+                if (use3) {
+                    load_limbs<QT>(bw, lp, chunks, 2, cok && L == 0);
+                    chunk_mma<QT, SIGNED>(d3v, wa, wb, bw);
+                }
+                if (cok) {
+                    const float kq = (QT == VOXQ_Q4) ? 0.0625f : 1.0f;  // Q4 sums are 16x
+                    const float d2 = __uint_as_float(rec.y) * kq, d3 = __uint_as_float(rec.z) * kq;
+                    const float xs = __uint_as_float(rec.w);
+                    const int blk = (QT == VOXQ_Q4) ? c : (c >> 1);
+                    float sa, ma, sb, mb;
+                    if (QT == VOXQ_Q4) {
+                        const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(ta + blk * SB));
+                        const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(tb2 + blk * SB));
+                        sa = fa.x; ma = fa.y; sb = fb.x; mb = fb.y;
+                    } else {
+                        const float2 fa = *reinterpret_cast<const float2*>(ta + blk * SB);
+                        const float2 fb = *reinterpret_cast<const float2*>(tb2 + blk * SB);
+                        sa = fa.x; ma = fa.y; sb = fb.x; mb = fb.y;
+                    }
+                    // d1 = 254 d2 up to one rounding of d2: d1 S1 + d2 S2 = d2 (254 S1 + S2)
+                    float dotA = d2 * (float)(d[0] * 254 + d[1]);
+                    float dotB = d2 * (float)(d[2] * 254 + d[3]);
+                    if (use3) {
+                        dotA = fmaf(d3, (float)d3v[0], dotA);
+                        dotB = fmaf(d3, (float)d3v[2], dotB);
+                    }
+                    accA = fmaf(sa, dotA, fmaf(ma, xs, accA));
+                    accB = fmaf(sb, dotB, fmaf(mb, xs, accB));
+                }
+            }
+            // the four chunk lanes of each row pair
+            accA += __shfl_xor_sync(0xffffffffu, accA, 1);
+            accB += __shfl_xor_sync(0xffffffffu, accB, 1);
+            accA += __shfl_xor_sync(0xffffffffu, accA, 2);
+            accB += __shfl_xor_sync(0xffffffffu, accB, 2);
+            if (tq == 0) {
+                const int ra = rt * 16 + g, rb = ra + 8;
+                if (P == 1) {
+                    const GemvItemDev& it = p.it[item];
+                    if (ra < rows) write_out(it, row0 + ra, 0, accA);
+                    if (rb < rows) write_out(it, row0 + rb, 0, accB);
+                } else {
+                    if (ra < rows) part[pset][ra * P + kp] = accA;
+                    if (rb < rows) part[pset][rb * P + kp] = accB;
+                }
+            }
+            // next unit of this warp: kMmaWarps units further in (row tile, part) order
+            kp += kMmaWarps;
+            while (kp >= P) {
+                kp -= P;
+                rt++;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (P > 1) {
+            // K parts of each row, summed in part order
+            asm volatile("bar.sync 1, %0;" ::"n"(kMmaWarps * 32) : "memory");
+            for (int r = warp * 32 + lane; r < rows; r += kMmaWarps * 32) {
+                float sum = 0.0f;
+                for (int kp = 0; kp < P; kp++) sum += part[pset][r * P + kp];
+                write_out(p.it[item], row0 + r, 0, sum);
+            }
+            pset ^= 1;
+        }
+    }
+}
+
 // Rows per consumer group for each activation-row count.
 template <int MT, bool SWI>
 struct Shape {
@@ -540,8 +802,48 @@ static VoxCPMError launch_t(const GemvParams<MAXI>& p, cudaStream_t st) {
     return VOXCPM_SUCCESS;
 }
 
+template <int QT, bool SIGNED, int MAXI>
+static VoxCPMError launch_mma_t(const GemvParams<MAXI>& p, cudaStream_t st) {
+    auto kern = gemv_mma_kernel<QT, SIGNED, MAXI>;
+    static int occ = 0;
+    static std::once_flag once;
+    std::call_once(once, [&] {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaSmem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, (kMmaWarps + 1) * 32, kMmaSmem);
+    });
+    const int cap = device_sm_count() * (occ > 0 ? occ : 1);
+    const int blocks = p.total_tiles < cap ? p.total_tiles : cap;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks < 1 ? 1 : blocks);
+    cfg.blockDim = dim3((kMmaWarps + 1) * 32);
+    cfg.dynamicSmemBytes = kMmaSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
+    return VOXCPM_SUCCESS;
+}
+
+// The tensor-path kernel serves single-row launches without SwiGLU
+// (VOXQ_GEMV_MMA=0 selects the dp4a kernel instead, for comparison).
+static bool mma_path(int mt, bool swi) {
+    static const bool on = [] {
+        const char* e = getenv("VOXQ_GEMV_MMA");
+        return !(e && e[0] == '0');
+    }();
+    return on && mt == 1 && !swi;
+}
+
 template <int MAXI>
 static VoxCPMError dispatch(const GemvParams<MAXI>& p, int qtype, int mt, bool swi, bool sgn, cudaStream_t st) {
+    if (mma_path(mt, swi)) {
+        if (qtype == VOXQ_Q4) return launch_mma_t<VOXQ_Q4, false, MAXI>(p, st);
+        if (qtype == VOXQ_Q8) return sgn ? launch_mma_t<VOXQ_Q8, true, MAXI>(p, st) : launch_mma_t<VOXQ_Q8, false, MAXI>(p, st);
+        return VOXCPM_ERR_UNSUPPORTED;
+    }
 #define VOXQ_GEMV_CASE(QT, MT)                                                                          \
     if (qtype == QT && mt == MT) {                                                                      \
         if (swi) return sgn ? launch_t<QT, MT, true, true, MAXI>(p, st) : launch_t<QT, MT, true, false, MAXI>(p, st); \
@@ -644,21 +946,39 @@ static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStr
         d.slabs = (d.chunks + 31) / 32;
         // rows per tile: fill the stage; rows spanning several slabs keep the
         // tile a whole number of 512-byte slabs so groups tile it exactly
-        int T = kTile / nw / d.rowb;
+        int T = (mma_path(mt, swi) ? kMmaTile : kTile / nw) / d.rowb;
         if (T > x.w.N) T = x.w.N;
         if (T < 1) T = 1;
-        if (d.slabs > 1) {
+        if (d.slabs > 1 && !mma_path(mt, swi)) {
             // partial-sum slots per tile: ceil(T / RG) * slabs <= 32
             const int rg = rows_per_group(mt, swi);
             if (T >= rg) T = T / rg * rg;
             while (T > 1 && ((T + rg - 1) / rg) * d.slabs > 32) T--;
         }
+        d.parts = ((d.chunks + 3) / 4 + groups_per_part(qt) - 1) / groups_per_part(qt);
+        d.pad = 0;
+        if (mma_path(mt, swi) && d.parts > 1 && T * d.parts > kPartSlots) T = kPartSlots / d.parts;
         d.T = T;
         d.tile_begin = tiles;
         tiles += (x.w.N + d.T - 1) / d.T;
         c++;
     }
     if (c == 0) return VOXCPM_SUCCESS;
+    if (mma_path(mt, swi)) {
+        // Small launches: shorter tiles (down to 16 rows) so every CTA slot gets
+        // work.  Results do not depend on T on this path.
+        const int want = 4 * device_sm_count();  // two stages of two CTAs per SM
+        if (tiles < want) {
+            const int f = (want + tiles - 1) / tiles;
+            tiles = 0;
+            for (int i = 0; i < c; i++) {
+                GemvItemDev& d = p.it[i];
+                if (d.T > 16) d.T = max(16, d.T / f / 16 * 16);
+                d.tile_begin = tiles;
+                tiles += (d.N + d.T - 1) / d.T;
+            }
+        }
+    }
     p.count = c;
     p.total_tiles = tiles;
     p.err = err ? err : device_error_word();
@@ -715,10 +1035,13 @@ VoxCPMError gemv_launch_ws(const voxq_gemv_item* items, int count, cudaStream_t 
         VoxCPMError e = validate_item(items[i]);
         if (e) return e;
     }
-    // group by kernel variant, preserving order inside a group
+    // group by kernel variant, preserving order inside a group; single-row items
+    // form their own group (tensor-path kernel), so an item's result does not
+    // depend on what it is batched with
     const voxq_gemv_item* sel[VOXQ_MAX_BATCH];
     bool done[VOXQ_MAX_BATCH] = {};
     size_t used = 0;
+    auto single = [](const voxq_gemv_item& x) { return mma_path(round_mt(x.M), x.up_codes != nullptr); };
     for (int i = 0; i < count; i++) {
         if (done[i]) continue;
         int n = 0;
@@ -726,7 +1049,7 @@ VoxCPMError gemv_launch_ws(const voxq_gemv_item* items, int count, cudaStream_t 
         for (int j = i; j < count; j++) {
             const voxq_gemv_item& b = items[j];
             if (!done[j] && b.w.qtype == a.w.qtype && (b.up_codes != nullptr) == (a.up_codes != nullptr) &&
-                (b.w.q8_signed != 0) == (a.w.q8_signed != 0)) {
+                (b.w.q8_signed != 0) == (a.w.q8_signed != 0) && single(b) == single(a)) {
                 sel[n++] = &items[j];
                 done[j] = true;
             }

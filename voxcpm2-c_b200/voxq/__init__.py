@@ -75,6 +75,20 @@ class GemvItem(C.Structure):
 
 
 # Every symbol include/voxq.h declares, with its ctypes signature.
+class Vxcpm2Header(C.Structure):
+    """voxq_vxcpm2_header (include/voxq.h)."""
+    _fields_ = [(n, C.c_uint32) for n in ("version", "n_layers", "n_layers_enc", "n_ralm_layers", "n_dit_layers",
+                                           "d_model", "d_ff", "n_heads", "n_kv_heads", "head_dim", "max_seq_len",
+                                           "vocab_size", "quant", "sample_rate", "audio_vae_dim")] + \
+               [("rope_theta", C.c_float), ("checksum", C.c_uint64), ("n_groups", C.c_uint32)]
+
+
+class Vxcpm2Tensor(C.Structure):
+    """voxq_vxcpm2_tensor (include/voxq.h)."""
+    _fields_ = [("name_hash", C.c_uint32), ("ndim", C.c_uint32), ("dims", C.c_uint32 * 3), ("dtype", C.c_int32),
+                ("group", C.c_int32), ("elements", C.c_uint64), ("offset", C.c_uint64), ("bytes", C.c_uint64)]
+
+
 _vp, _sz, _i, _i64 = C.c_void_p, C.c_size_t, C.c_int, C.c_int64
 _TP = C.POINTER(Tensor)
 SIGNATURES = {
@@ -101,6 +115,14 @@ SIGNATURES = {
     "voxq_matmul_nt_q_noalloc": ([_vp, _i, _i64, C.POINTER(QWeightDesc), _vp, _i64, C.POINTER(Epilogue), _vp], _i),
     "voxq_matmul_nt_dense": ([_vp, _i, _i64, _vp, _i, _i, _i, _vp, _i64, _vp], _i),
     "voxq_gemv_batch": ([C.POINTER(GemvItem), _i, _vp], _i),
+    "voxq_vxcpm2_open": ([C.c_char_p, C.POINTER(_vp)], _i),
+    "voxq_vxcpm2_close": ([_vp], None),
+    "voxq_vxcpm2_info": ([_vp, C.POINTER(Vxcpm2Header), C.POINTER(_i)], _i),
+    "voxq_vxcpm2_tensor_info": ([_vp, _i, C.POINTER(Vxcpm2Tensor)], _i),
+    "voxq_vxcpm2_data": ([_vp, _i], _vp),
+    "voxq_vxcpm2_verify": ([_vp], _i),
+    "voxq_vxcpm2_dequantize": ([_vp, _i, _i, _vp], _i),
+    "voxq_vxcpm2_upload_qweight": ([_vp, _i, _vp, _vp, _vp], _i),
 }
 
 _lib = None
