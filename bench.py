@@ -187,10 +187,13 @@ def run_ours(args, torch, dist, rank, world, local_rank):
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
         cpu = cpu_baseline(args.cpu_seconds, threads=1)
 
+    # the single-row launch runs the tensor-path GEMV unless VOXQ_GEMV_MMA=0
+    mma = os.environ.get("VOXQ_GEMV_MMA", "1")[:1] != "0"
+    kernel = "voxq::gemv_mma_kernel<Q4,false,192>" if mma else "voxq::gemv_kernel<Q4,1,4,false,false,192>"
     traffic = None
     tp = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(tp):
-        t = json.load(open(tp)).get("gemv_c2_q4")
+        t = json.load(open(tp)).get("gemv_mma_c2_q4" if mma else "gemv_c2_q4")
         if t:  # dram__bytes_read.sum + dram__bytes_write.sum of one launch (ncu)
             traffic = t["dram_read_bytes"] + t["dram_write_bytes"]
 
@@ -217,7 +220,7 @@ def run_ours(args, torch, dist, rank, world, local_rank):
             },
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
-                         "traffic": traffic, "kernel": "voxq::gemv_kernel<Q4,1,8,...,192>"},
+                         "traffic": traffic, "kernel": kernel},
             "e2e": e2e,
             "gpu_launches": 2 * args.steps,  # per step: limb prepass + grouped GEMV
             "clocks": sampler.summary(),
