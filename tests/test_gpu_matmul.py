@@ -151,6 +151,19 @@ def test_gemv_result_independent_of_launch_size(qt):
     assert_matmul_close(alone.cpu().numpy(), y, sc, TOL_GEMV)
 
 
+@pytest.mark.parametrize("qt,K", [(voxq.Q4, 160), (voxq.Q4, 96), (voxq.Q8, 96), (voxq.Q4, 4160)])
+def test_gemv_single_row_unaligned_trailer_rows(qt, K):
+    """Single-row GEMVs whose trailer rows are not 16-byte multiples (K % 128 != 0
+    for Q4, K % 64 != 0 for Q8): odd trailer windows, partial 4-chunk groups."""
+    N = 300
+    qw, wdeq = make_weight(N, K, qt, seed=950 + K)
+    a = O.rand_normal(951 + K, K).reshape(1, K)
+    bias = O.rand_normal(952 + K, N)
+    y = voxq.matmul_nt_q(torch.from_numpy(a).cuda(), qw, bias=torch.from_numpy(bias).cuda()).cpu().numpy()
+    want, sc = ref(a, wdeq)
+    assert_matmul_close(y, want + bias[None, :], sc, TOL_GEMV)
+
+
 def test_batch_mixed_formats_and_epilogues():
     specs, wants = [], []
     for i, (qt, M, swi) in enumerate([(voxq.Q8, 1, False), (voxq.Q4, 2, True), (voxq.Q8, 5, True),

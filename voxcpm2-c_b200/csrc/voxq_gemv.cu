@@ -609,7 +609,9 @@ __device__ __forceinline__ void load_limbs(uint32_t (&bw)[8], const uint4* lp, i
     }
 }
 
-template <int QT, bool SIGNED, int MAXI>
+// TRX (Q4, every item's trailer rows a multiple of 16 bytes): trailers handed
+// to the lanes through a per-warp scratch (see the unit loop).
+template <int QT, bool SIGNED, bool TRX, int MAXI>
 __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const __grid_constant__ GemvParams<MAXI> p) {
     constexpr int G = limb_granules(QT);
     constexpr int SB = (QT == VOXQ_Q4) ? 4 : 8;  // trailer bytes per block
@@ -620,6 +622,7 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
     // the tiles that combine parts, so a set is rewritten only after every
     // warp has passed the next combining tile's barrier
     __shared__ float part[2][kPartSlots];  // [row][K part] of a stage's rows
+    __shared__ __align__(16) uint32_t trx[TRX ? kMmaWarps : 1][2][8 * 20];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kMmaStages; s++) {
@@ -683,6 +686,21 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
             const uint8_t* tb2 = trs + rB * srow;
             float accA = 0.0f, accB = 0.0f;
             constexpr int GPP = groups_per_part(QT);
+            if (TRX) {
+                // The unit's trailers: lane t reads 16-byte chunk (first group + t) of
+                // its two rows (blocks 4k .. 4k+3) and the warp hands element t of
+                // chunk i to the lanes t of group i through a scratch with a 20-word
+                // row pitch (conflict-free reads).  One wide read per row instead of
+                // one narrow read per group, each of which hits the same banks for
+                // all eight rows.
+                const int k = min(kp * GPP + tq, ngr - 1);
+                const uint4 xa = *reinterpret_cast<const uint4*>(ta + 16 * k);
+                const uint4 xb = *reinterpret_cast<const uint4*>(tb2 + 16 * k);
+                __syncwarp();
+                *reinterpret_cast<uint4*>(&trx[warp][0][g * 20 + tq * 4]) = xa;
+                *reinterpret_cast<uint4*>(&trx[warp][1][g * 20 + tq * 4]) = xb;
+                __syncwarp();
+            }
             const int g1 = min(ngr, (kp + 1) * GPP);
 #pragma unroll
             for (int gr = kp * GPP; gr < g1; gr++) {
@@ -710,8 +728,11 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
                     const int blk = (QT == VOXQ_Q4) ? c : (c >> 1);
                     float sa, ma, sb, mb;
                     if (QT == VOXQ_Q4) {
-                        const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(ta + blk * SB));
-                        const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(tb2 + blk * SB));
+                        const int ii = gr - kp * GPP;
+                        const void* sa_p = TRX ? (const void*)&trx[warp][0][g * 20 + ii * 4 + tq] : (const void*)(ta + blk * SB);
+                        const void* sb_p = TRX ? (const void*)&trx[warp][1][g * 20 + ii * 4 + tq] : (const void*)(tb2 + blk * SB);
+                        const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(sa_p));
+                        const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(sb_p));
                         sa = fa.x; ma = fa.y; sb = fb.x; mb = fb.y;
                     } else {
                         const float2 fa = *reinterpret_cast<const float2*>(ta + blk * SB);
@@ -802,9 +823,9 @@ static VoxCPMError launch_t(const GemvParams<MAXI>& p, cudaStream_t st) {
     return VOXCPM_SUCCESS;
 }
 
-template <int QT, bool SIGNED, int MAXI>
+template <int QT, bool SIGNED, bool TRX, int MAXI>
 static VoxCPMError launch_mma_t(const GemvParams<MAXI>& p, cudaStream_t st) {
-    auto kern = gemv_mma_kernel<QT, SIGNED, MAXI>;
+    auto kern = gemv_mma_kernel<QT, SIGNED, TRX, MAXI>;
     static int occ = 0;
     static std::once_flag once;
     std::call_once(once, [&] {
@@ -840,8 +861,13 @@ static bool mma_path(int mt, bool swi) {
 template <int MAXI>
 static VoxCPMError dispatch(const GemvParams<MAXI>& p, int qtype, int mt, bool swi, bool sgn, cudaStream_t st) {
     if (mma_path(mt, swi)) {
-        if (qtype == VOXQ_Q4) return launch_mma_t<VOXQ_Q4, false, MAXI>(p, st);
-        if (qtype == VOXQ_Q8) return sgn ? launch_mma_t<VOXQ_Q8, true, MAXI>(p, st) : launch_mma_t<VOXQ_Q8, false, MAXI>(p, st);
+        if (qtype == VOXQ_Q4) {
+            bool trx = true;  // every item's trailer rows in whole 16-byte chunks
+            for (int i = 0; i < p.count; i++) trx = trx && (p.it[i].srow & 15) == 0;
+            return trx ? launch_mma_t<VOXQ_Q4, false, true, MAXI>(p, st) : launch_mma_t<VOXQ_Q4, false, false, MAXI>(p, st);
+        }
+        if (qtype == VOXQ_Q8)
+            return sgn ? launch_mma_t<VOXQ_Q8, true, false, MAXI>(p, st) : launch_mma_t<VOXQ_Q8, false, false, MAXI>(p, st);
         return VOXCPM_ERR_UNSUPPORTED;
     }
 #define VOXQ_GEMV_CASE(QT, MT)                                                                          \
