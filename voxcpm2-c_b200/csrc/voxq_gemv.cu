@@ -27,8 +27,11 @@
 // combined in shared memory behind one named barrier per tile.  CTAs own
 // contiguous tile ranges, so consecutive tiles share an item and its limbs
 // stay in L1.  The producer starts streaming before the kernel waits on its
-// predecessor, which is always the limb prepass of the same call (that
-// prepass never writes weights and waits on its own predecessor first).
+// predecessor: that predecessor is the limb prepass of the same call, or (the
+// tensor-path kernel, which splits its activations itself) whatever kernel ran
+// before; none of the library's kernels that write packed weights (quantize,
+// pack, rowmul) lets a dependent start early, so every weight write before
+// the call is complete when the stream reaches it.
 #include <mutex>
 
 #include "voxq_common.cuh"
@@ -77,8 +80,89 @@ __device__ __forceinline__ int8_t rint_clamp127(float v) {
     return (int8_t)(int)r;
 }
 
-// One thread per 8 consecutive activation values: Q4 chunks (32 values) are
-// 4 threads, Q8 chunks (16 values) 2 threads; chunk max / sum by shuffles.
+// One thread's share of one chunk's limb record: the chunk's TPC threads (Q4
+// chunks of 32 values: 4 threads, Q8 chunks of 16 values: 2 threads; `part` =
+// this thread's index, 8 consecutive values each) sit in one warp and reduce
+// the chunk max / sum by shuffles, so every lane of the warp must call this
+// (threads past the end with live = false).  `base` = granule 0 of the chunk,
+// granules `gstride` bytes apart.
+template <int QT>
+__device__ __forceinline__ void limb_part(const float* __restrict__ xrow, int c, int part, bool live, uint8_t* base,
+                                          int64_t gstride) {
+    constexpr int TPC = QT == VOXQ_Q4 ? 4 : 2;
+    constexpr int G = limb_granules(QT);
+    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (live) {
+        const float* x = xrow + (int64_t)c * (8 * TPC) + part * 8;
+        const float4 f0 = *reinterpret_cast<const float4*>(x);
+        const float4 f1 = *reinterpret_cast<const float4*>(x + 4);
+        v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+        v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+    }
+    float amax = 0.0f, sum = 0.0f, asum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        amax = fmaxf(amax, fabsf(v[i]));
+        sum += v[i];
+        asum += fabsf(v[i]);
+    }
+#pragma unroll
+    for (int o = 1; o < TPC; o <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        asum += __shfl_xor_sync(0xffffffffu, asum, o);
+    }
+    if (!live) return;
+    // d1: power of two with amax / d1 <= 127 (exact scaling); d2, d3 refine.
+    float d1 = 1.0f;
+    if (amax > 0.0f && isfinite(amax)) {
+        int e;
+        frexpf(amax * (1.0f / 127.0f), &e);
+        d1 = ldexpf(1.0f, e);
+        if (amax > 127.0f * d1) d1 *= 2.0f;
+    }
+    const float inv1 = 1.0f / d1;  // exact: power of two
+    const float d2 = d1 * (1.0f / 254.0f), d3 = d2 * (1.0f / 254.0f);
+    // Two limbs leave an error of at most ~3e-5 * amax per value; a chunk
+    // whose magnitude is spread (amax <= 5 * mean |x|) keeps that far below
+    // the matmul tolerance, so its third limb is dropped (d3 = 0).
+    const bool need3 = amax * (8 * TPC) > 5.0f * asum;
+    int8_t l[3][8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        float r = v[i];
+        const float a = fminf(fmaxf(rintf(r * inv1), -127.0f), 127.0f);
+        r = fmaf(-a, d1, r);
+        const float b = fminf(fmaxf(rintf(r * (254.0f * inv1)), -127.0f), 127.0f);
+        r = fmaf(-b, d2, r);
+        const float cc = need3 ? fminf(fmaxf(rintf(r * (64516.0f * inv1)), -127.0f), 127.0f) : 0.0f;
+        l[0][i] = (int8_t)(int)a;
+        l[1][i] = (int8_t)(int)b;
+        l[2][i] = (int8_t)(int)cc;
+    }
+    auto pack4 = [](int8_t a, int8_t b, int8_t c2, int8_t d) -> uint32_t {
+        return (uint32_t)(uint8_t)a | ((uint32_t)(uint8_t)b << 8) | ((uint32_t)(uint8_t)c2 << 16) |
+               ((uint32_t)(uint8_t)d << 24);
+    };
+#pragma unroll
+    for (int L = 0; L < 3; L++) {
+        if (QT == VOXQ_Q4) {
+            // this thread's 8 values are code word `part` of the chunk
+            *reinterpret_cast<uint32_t*>(base + (2 * L) * gstride + 4 * part) = pack4(l[L][1], l[L][3], l[L][5], l[L][7]);
+            *reinterpret_cast<uint32_t*>(base + (2 * L + 1) * gstride + 4 * part) =
+                pack4(l[L][0], l[L][2], l[L][4], l[L][6]);
+        } else {
+            *reinterpret_cast<uint2*>(base + L * gstride + 8 * part) =
+                make_uint2(pack4(l[L][0], l[L][1], l[L][2], l[L][3]), pack4(l[L][4], l[L][5], l[L][6], l[L][7]));
+        }
+    }
+    if (part == 0)
+        *reinterpret_cast<uint4*>(base + (G - 1) * gstride) = make_uint4(
+            __float_as_uint(d1), __float_as_uint(d2), __float_as_uint(need3 ? d3 : 0.0f), __float_as_uint(sum));
+}
+
+// Limb prepass of the dp4a GEMV: one thread per 8 consecutive activation
+// values of every job, written to the global limb records.
 template <int QT>
 __global__ void __launch_bounds__(256) limb_kernel(const __grid_constant__ LimbParams p) {
     pdl_wait();  // the activations may come from the previous kernel
@@ -105,78 +189,8 @@ __global__ void __launch_bounds__(256) limb_kernel(const __grid_constant__ LimbP
         const LimbJob& jb = p.job[j];
         const int local = cidx - jb.chunk_begin;
         const int m = local / jb.chunks, c = local % jb.chunks;
-        float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        if (live) {
-            const float* x = jb.a + (int64_t)m * jb.lda + (int64_t)c * (8 * TPC) + part * 8;
-            const float4 f0 = *reinterpret_cast<const float4*>(x);
-            const float4 f1 = *reinterpret_cast<const float4*>(x + 4);
-            v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
-            v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
-        }
-        float amax = 0.0f, sum = 0.0f, asum = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            amax = fmaxf(amax, fabsf(v[i]));
-            sum += v[i];
-            asum += fabsf(v[i]);
-        }
-#pragma unroll
-        for (int o = 1; o < TPC; o <<= 1) {
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            asum += __shfl_xor_sync(0xffffffffu, asum, o);
-        }
-        if (!live) continue;
-        // d1: power of two with amax / d1 <= 127 (exact scaling); d2, d3 refine.
-        float d1 = 1.0f;
-        if (amax > 0.0f && isfinite(amax)) {
-            int e;
-            frexpf(amax * (1.0f / 127.0f), &e);
-            d1 = ldexpf(1.0f, e);
-            if (amax > 127.0f * d1) d1 *= 2.0f;
-        }
-        const float inv1 = 1.0f / d1;  // exact: power of two
-        const float d2 = d1 * (1.0f / 254.0f), d3 = d2 * (1.0f / 254.0f);
-        // Two limbs leave an error of at most ~3e-5 * amax per value; a chunk
-        // whose magnitude is spread (amax <= 5 * mean |x|) keeps that far below
-        // the matmul tolerance, so its third limb is dropped (d3 = 0).
-        const bool need3 = amax * (8 * TPC) > 5.0f * asum;
-        int8_t l[3][8];
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            float r = v[i];
-            const float a = fminf(fmaxf(rintf(r * inv1), -127.0f), 127.0f);
-            r = fmaf(-a, d1, r);
-            const float b = fminf(fmaxf(rintf(r * (254.0f * inv1)), -127.0f), 127.0f);
-            r = fmaf(-b, d2, r);
-            const float cc = need3 ? fminf(fmaxf(rintf(r * (64516.0f * inv1)), -127.0f), 127.0f) : 0.0f;
-            l[0][i] = (int8_t)(int)a;
-            l[1][i] = (int8_t)(int)b;
-            l[2][i] = (int8_t)(int)cc;
-        }
-        auto pack4 = [](int8_t a, int8_t b, int8_t c2, int8_t d) -> uint32_t {
-            return (uint32_t)(uint8_t)a | ((uint32_t)(uint8_t)b << 8) | ((uint32_t)(uint8_t)c2 << 16) |
-                   ((uint32_t)(uint8_t)d << 24);
-        };
-        uint8_t* base = reinterpret_cast<uint8_t*>(jb.dst + (int64_t)m * G * jb.chunks + c);
-        const int64_t gstride = (int64_t)jb.chunks * 16;  // bytes between granules
-#pragma unroll
-        for (int L = 0; L < 3; L++) {
-            if (QT == VOXQ_Q4) {
-                // this thread's 8 values are code word `part` of the chunk
-                *reinterpret_cast<uint32_t*>(base + (2 * L) * gstride + 4 * part) =
-                    pack4(l[L][1], l[L][3], l[L][5], l[L][7]);
-                *reinterpret_cast<uint32_t*>(base + (2 * L + 1) * gstride + 4 * part) =
-                    pack4(l[L][0], l[L][2], l[L][4], l[L][6]);
-            } else {
-                *reinterpret_cast<uint2*>(base + L * gstride + 8 * part) =
-                    make_uint2(pack4(l[L][0], l[L][1], l[L][2], l[L][3]), pack4(l[L][4], l[L][5], l[L][6], l[L][7]));
-            }
-        }
-        if (part == 0)
-            *reinterpret_cast<uint4*>(base + (G - 1) * gstride) =
-                make_uint4(__float_as_uint(d1), __float_as_uint(d2), __float_as_uint(need3 ? d3 : 0.0f),
-                           __float_as_uint(sum));
+        limb_part<QT>(jb.a + (int64_t)m * jb.lda, c, part, live,
+                      reinterpret_cast<uint8_t*>(jb.dst + (int64_t)m * G * jb.chunks + c), (int64_t)jb.chunks * 16);
     }
 }
 
@@ -197,13 +211,16 @@ struct GemvItemDev {
     int32_t T;           // rows per tile
     int32_t tile_begin;  // first global tile of this item
     int32_t parts;       // tensor-path kernel: K parts of groups_per_part 4-chunk groups
-    int32_t pad;
+    int32_t lda;         // tensor-path kernel: activation row stride (elements)
+    const float* a;      // tensor-path kernel: the activation row (limbs computed in the kernel)
 };
 
 template <int MAXI>
 struct GemvParams {
     int32_t count;
     int32_t total_tiles;
+    int32_t limb_bytes;  // tensor-path kernel: largest item's limb record (shared-memory buffer)
+    int32_t pad;
     int* err;
     GemvItemDev it[MAXI];
 };
@@ -549,6 +566,7 @@ constexpr int kMmaStages = 2;
 constexpr int kMmaTile = 32768;                  // code bytes per stage
 constexpr int kMmaTW = kMmaTile / 4 + 32;        // trailer window bytes per stage
 constexpr int kMmaSmem = kMmaStages * (kMmaTile + kMmaTW);
+constexpr int kMmaLimbMax = 16384;               // limb record of the largest item (K <= 4096)
 // groups (four 16-byte chunks of a row) per K part: 256 bytes of Q4 codes, 128 of Q8
 __host__ __device__ constexpr int groups_per_part(int qtype) { return qtype == VOXQ_Q4 ? 4 : 2; }
 constexpr int kPartSlots = 256;                 // >= T x parts (T x rowb <= kMmaTile)
@@ -592,17 +610,17 @@ __device__ __forceinline__ void chunk_mma(int (&d)[4], const uint4& wa, const ui
     }
 }
 
-__device__ const uint4 kZeroLimbs[2] = {};
-
-// Limb L (0 .. 2) of this lane's chunk, or zeros (read from a zero block, so
-// the loads are unconditional).
+// Limb L (0 .. 2) of this lane's chunk from the item's shared-memory limb
+// record (chunk address lp, granules gstride bytes apart), or zeros from a
+// zero block.
 template <int QT>
-__device__ __forceinline__ void load_limbs(uint32_t (&bw)[8], const uint4* lp, int chunks, int L, bool on) {
-    const uint4* po = on ? lp + (int64_t)((QT == VOXQ_Q4) ? 2 * L : L) * chunks : &kZeroLimbs[0];
-    const uint4 o = __ldg(po);
+__device__ __forceinline__ void load_limbs(uint32_t (&bw)[8], uint32_t lp, uint32_t gstride, int L, bool on,
+                                           uint32_t zaddr) {
+    const uint32_t po = on ? lp + (uint32_t)((QT == VOXQ_Q4) ? 2 * L : L) * gstride : zaddr;
+    const uint4 o = lds128(po);
     bw[0] = o.x; bw[1] = o.y; bw[2] = o.z; bw[3] = o.w;
     if (QT == VOXQ_Q4) {
-        const uint4 e = __ldg(on ? po + chunks : &kZeroLimbs[1]);
+        const uint4 e = lds128(on ? po + gstride : zaddr + 16);
         bw[4] = e.x; bw[5] = e.y; bw[6] = e.z; bw[7] = e.w;
     } else {
         bw[4] = bw[5] = bw[6] = bw[7] = 0u;
@@ -623,12 +641,14 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
     // warp has passed the next combining tile's barrier
     __shared__ float part[2][kPartSlots];  // [row][K part] of a stage's rows
     __shared__ __align__(16) uint32_t trx[TRX ? kMmaWarps : 1][2][8 * 20];
+    __shared__ __align__(16) uint4 zlimb[2];  // B of the lanes that feed no limb
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kMmaStages; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kMmaWarps);
         }
+        zlimb[0] = zlimb[1] = make_uint4(0u, 0u, 0u, 0u);
     }
     mbar_fence_init();
     __syncthreads();
@@ -642,15 +662,16 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
         return;
     }
 
-    pdl_wait();  // limbs come from the prepass launched just before this kernel
+    pdl_wait();  // the activations may come from the previous kernel
     pdl_launch_dependents();
     const int g = lane >> 2, tq = lane & 3;
     const int L = g - 2 * tq;  // limb this lane feeds into B (column 2t + L), if 0 or 1
     const bool limb_lane = (unsigned)L < 2u;
+    // the current item's limb records, [granule][chunk] (16 bytes each)
+    const uint32_t limb_s = smem_u32(smem + kMmaStages * STAGE), zaddr = smem_u32(&zlimb[0]);
     int item = -1, pset = 0;
     // per-item constants (refreshed when the tile range enters a new item)
     int P = 1, rt0 = 0, kp0 = 0, ngr = 1, chunks = 1, rowb = 0, srow = 0, T = 1, N = 0, tbeg = 0;
-    const uint4* limbs = nullptr;
     for (int t = tb, j = 0; t < te; ++t, ++j) {
         int nitem = item < 0 ? 0 : item;
         fix_item(p, t, nitem);
@@ -667,7 +688,20 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
             T = it.T;
             N = it.N;
             tbeg = it.tile_begin;
-            limbs = it.limbs;
+            // The item's activation row split into limbs (the prepass arithmetic,
+            // limb_part) into the shared buffer, once every consumer warp is done
+            // with the previous item's; the producer keeps streaming meanwhile.
+            asm volatile("bar.sync 1, %0;" ::"n"(kMmaWarps * 32) : "memory");
+            {
+                constexpr int TPC = QT == VOXQ_Q4 ? 4 : 2;
+                const int total = chunks * TPC, span = (total + 31) & ~31;
+                for (int q = warp * 32 + lane; q < span; q += kMmaWarps * 32) {
+                    const bool live = q < total;
+                    const int c = live ? q / TPC : 0;
+                    limb_part<QT>(it.a, c, q % TPC, live, smem + kMmaStages * STAGE + c * 16, (int64_t)chunks * 16);
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(kMmaWarps * 32) : "memory");
         }
         const int s = j % kMmaStages;
         // a wait that gives up records the error and the tile is processed
@@ -709,16 +743,17 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
                 const int cc = cok ? c : chunks - 1;
                 const uint4 wa = *reinterpret_cast<const uint4*>(pa + cc * 16);
                 const uint4 wb = *reinterpret_cast<const uint4*>(pb + cc * 16);
-                const uint4* lp = limbs + cc;  // [granule][chunks] of activation row 0
-                const uint4 rec = __ldg(lp + (int64_t)(G - 1) * chunks);
+                const uint32_t lp = limb_s + (uint32_t)cc * 16;  // this chunk's granule 0
+                const uint32_t gs = (uint32_t)chunks * 16;
+                const uint4 rec = lds128(lp + (G - 1) * gs);
                 uint32_t bw[8];
-                load_limbs<QT>(bw, lp, chunks, L, cok && limb_lane);
+                load_limbs<QT>(bw, lp, gs, L, cok && limb_lane, zaddr);
                 int d[4] = {0, 0, 0, 0};
                 chunk_mma<QT, SIGNED>(d, wa, wb, bw);
                 int d3v[4] = {0, 0, 0, 0};
                 const bool use3 = __any_sync(0xffffffffu, cok && rec.z != 0u);
                 if (use3) {
-                    load_limbs<QT>(bw, lp, chunks, 2, cok && L == 0);
+                    load_limbs<QT>(bw, lp, gs, 2, cok && L == 0, zaddr);
                     chunk_mma<QT, SIGNED>(d3v, wa, wb, bw);
                 }
                 if (cok) {
@@ -826,18 +861,21 @@ static VoxCPMError launch_t(const GemvParams<MAXI>& p, cudaStream_t st) {
 template <int QT, bool SIGNED, bool TRX, int MAXI>
 static VoxCPMError launch_mma_t(const GemvParams<MAXI>& p, cudaStream_t st) {
     auto kern = gemv_mma_kernel<QT, SIGNED, TRX, MAXI>;
-    static int occ = 0;
+    // occupancy for each limb-buffer size, in 1 KB steps
+    static int occ[kMmaLimbMax / 1024 + 1] = {};
     static std::once_flag once;
     std::call_once(once, [&] {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaSmem);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, (kMmaWarps + 1) * 32, kMmaSmem);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaSmem + kMmaLimbMax);
     });
-    const int cap = device_sm_count() * (occ > 0 ? occ : 1);
+    const int lk = (p.limb_bytes + 1023) / 1024;
+    const int smem = kMmaSmem + lk * 1024;
+    if (occ[lk] == 0) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ[lk], kern, (kMmaWarps + 1) * 32, smem);
+    const int cap = device_sm_count() * (occ[lk] > 0 ? occ[lk] : 1);
     const int blocks = p.total_tiles < cap ? p.total_tiles : cap;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks < 1 ? 1 : blocks);
     cfg.blockDim = dim3((kMmaWarps + 1) * 32);
-    cfg.dynamicSmemBytes = kMmaSmem;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -847,6 +885,8 @@ static VoxCPMError launch_mma_t(const GemvParams<MAXI>& p, cudaStream_t st) {
     VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
     return VOXCPM_SUCCESS;
 }
+
+static int round_mt(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 
 // The tensor-path kernel serves single-row launches without SwiGLU
 // (VOXQ_GEMV_MMA=0 selects the dp4a kernel instead, for comparison).
@@ -858,9 +898,17 @@ static bool mma_path(int mt, bool swi) {
     return on && mt == 1 && !swi;
 }
 
+// Items the tensor-path kernel takes: single-row, no SwiGLU, and a limb record
+// (computed in the kernel) that fits its shared-memory buffer (K <= 4096).
+static bool mma_item(const voxq_gemv_item& x) {
+    const int64_t rec = (int64_t)codes_row_bytes(x.w.K, x.w.qtype) / 16 * limb_granules(x.w.qtype) * 16;
+    return mma_path(round_mt(x.M), x.up_codes != nullptr) && rec <= kMmaLimbMax;
+}
+
 template <int MAXI>
-static VoxCPMError dispatch(const GemvParams<MAXI>& p, int qtype, int mt, bool swi, bool sgn, cudaStream_t st) {
-    if (mma_path(mt, swi)) {
+static VoxCPMError dispatch(const GemvParams<MAXI>& p, int qtype, int mt, bool swi, bool sgn, bool mma,
+                            cudaStream_t st) {
+    if (mma) {
         if (qtype == VOXQ_Q4) {
             bool trx = true;  // every item's trailer rows in whole 16-byte chunks
             for (int i = 0; i < p.count; i++) trx = trx && (p.it[i].srow & 15) == 0;
@@ -887,7 +935,6 @@ static VoxCPMError dispatch(const GemvParams<MAXI>& p, int qtype, int mt, bool s
     return VOXCPM_ERR_UNSUPPORTED;
 }
 
-static int round_mt(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 
 VoxCPMError validate_item(const voxq_gemv_item& x) {
     const voxq_qweight& w = x.w;
@@ -927,8 +974,10 @@ static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStr
     for (int i = 0; i < n; i++) mt = max(mt, round_mt(sel[i]->M));
     const bool swi = f.up_codes != nullptr;
     const int nw = swi ? 2 : 1;
+    const bool use_mma = mma_item(f);  // uniform within a group (see gemv_launch_ws)
+    int limb_max = 0;
 
-    // distinct activations -> limb jobs
+    // distinct activations -> limb jobs (the tensor-path kernel computes its own)
     struct Act { const float* a; int M, lda, K; uint4* dst; };
     Act acts[VOXQ_MAX_BATCH];
     int nact = 0;
@@ -945,7 +994,7 @@ static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStr
         int ai = -1;
         for (int k = 0; k < nact; k++)
             if (acts[k].a == x.a && acts[k].M == x.M && acts[k].lda == x.lda && acts[k].K == x.w.K) ai = k;
-        if (ai < 0) {
+        if (ai < 0 && !use_mma) {
             const size_t b = limb_bytes(x.M, x.w.K, qt);
             if (off + b > ws_bytes) return VOXCPM_ERR_OOM;
             acts[nact] = {x.a, x.M, x.lda, x.w.K, reinterpret_cast<uint4*>(static_cast<uint8_t*>(ws) + off)};
@@ -957,7 +1006,11 @@ static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStr
         d.scales = reinterpret_cast<const uint8_t*>(x.w.scales);
         d.up_codes = x.up_codes;
         d.up_scales = reinterpret_cast<const uint8_t*>(x.up_scales);
-        d.limbs = acts[ai].dst;
+        d.limbs = use_mma ? nullptr : acts[ai].dst;
+        d.a = x.a;
+        d.lda = x.lda;
+        if (use_mma)
+            limb_max = max(limb_max, (int)(codes_row_bytes(x.w.K, qt) / 16 * limb_granules(qt) * 16));
         d.out = x.out;
         d.bias = x.bias;
         d.residual = x.residual;
@@ -972,25 +1025,25 @@ static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStr
         d.slabs = (d.chunks + 31) / 32;
         // rows per tile: fill the stage; rows spanning several slabs keep the
         // tile a whole number of 512-byte slabs so groups tile it exactly
-        int T = (mma_path(mt, swi) ? kMmaTile : kTile / nw) / d.rowb;
+        int T = (use_mma ? kMmaTile : kTile / nw) / d.rowb;
         if (T > x.w.N) T = x.w.N;
         if (T < 1) T = 1;
-        if (d.slabs > 1 && !mma_path(mt, swi)) {
+        if (d.slabs > 1 && !use_mma) {
             // partial-sum slots per tile: ceil(T / RG) * slabs <= 32
             const int rg = rows_per_group(mt, swi);
             if (T >= rg) T = T / rg * rg;
             while (T > 1 && ((T + rg - 1) / rg) * d.slabs > 32) T--;
         }
         d.parts = ((d.chunks + 3) / 4 + groups_per_part(qt) - 1) / groups_per_part(qt);
-        d.pad = 0;
-        if (mma_path(mt, swi) && d.parts > 1 && T * d.parts > kPartSlots) T = kPartSlots / d.parts;
+        if (use_mma && d.parts > 1 && T * d.parts > kPartSlots) T = kPartSlots / d.parts;
         d.T = T;
         d.tile_begin = tiles;
         tiles += (x.w.N + d.T - 1) / d.T;
         c++;
     }
     if (c == 0) return VOXCPM_SUCCESS;
-    if (mma_path(mt, swi)) {
+    p.limb_bytes = limb_max;
+    if (use_mma) {
         // Small launches: shorter tiles (down to 16 rows) so every CTA slot gets
         // work.  Results do not depend on T on this path.
         const int want = 4 * device_sm_count();  // two stages of two CTAs per SM
@@ -1043,7 +1096,7 @@ static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStr
         else
             VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, limb_kernel<VOXQ_Q8>, lp));
     }
-    return dispatch<MAXI>(p, qt, mt, swi, f.w.q8_signed != 0, st);
+    return dispatch<MAXI>(p, qt, mt, swi, f.w.q8_signed != 0, use_mma, st);
 }
 
 size_t gemv_workspace_bytes(const voxq_gemv_item* items, int count) {
@@ -1067,7 +1120,7 @@ VoxCPMError gemv_launch_ws(const voxq_gemv_item* items, int count, cudaStream_t 
     const voxq_gemv_item* sel[VOXQ_MAX_BATCH];
     bool done[VOXQ_MAX_BATCH] = {};
     size_t used = 0;
-    auto single = [](const voxq_gemv_item& x) { return mma_path(round_mt(x.M), x.up_codes != nullptr); };
+    auto single = [](const voxq_gemv_item& x) { return mma_item(x); };
     for (int i = 0; i < count; i++) {
         if (done[i]) continue;
         int n = 0;
