@@ -222,7 +222,9 @@ def run_ours(args, torch, dist, rank, world, local_rank):
                          "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
                          "traffic": traffic, "kernel": kernel},
             "e2e": e2e,
-            "gpu_launches": 2 * args.steps,  # per step: limb prepass + grouped GEMV
+            # per step: the tensor-path GEMV splits its activations itself (one launch);
+            # the dp4a kernel needs the limb prepass before it (two)
+            "gpu_launches": (1 if mma else 2) * args.steps,
             "clocks": sampler.summary(),
         }
         if e2e_abi is not None:
@@ -454,7 +456,8 @@ def run_c1(args, torch):
                                  "l2": "64 rotated weight copies (335 MB > L2)"},
                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                                    "frac": round(gbs / hbm, 4), "peak_kind": peak_kind},
-                      "gpu_launches": 2 * calls, "device_error": voxq.lib().voxq_device_error(1)}), flush=True)
+                      "gpu_launches": (1 if os.environ.get("VOXQ_GEMV_MMA", "1")[:1] != "0" else 2) * calls,
+                      "device_error": voxq.lib().voxq_device_error(1)}), flush=True)
 
 
 def run_c3(args, torch):
