@@ -667,7 +667,9 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
     const int g = lane >> 2, tq = lane & 3;
     const int L = g - 2 * tq;  // limb this lane feeds into B (column 2t + L), if 0 or 1
     const bool limb_lane = (unsigned)L < 2u;
-    // the current item's limb records, [granule][chunk] (16 bytes each)
+    // the current item's limb records, [chunk][granule] (16 bytes each): a chunk's
+    // granules in consecutive banks, so the two limb lanes of a quad read theirs
+    // without conflict
     const uint32_t limb_s = smem_u32(smem + kMmaStages * STAGE), zaddr = smem_u32(&zlimb[0]);
     int item = -1, pset = 0;
     // per-item constants (refreshed when the tile range enters a new item)
@@ -698,7 +700,7 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
                 for (int q = warp * 32 + lane; q < span; q += kMmaWarps * 32) {
                     const bool live = q < total;
                     const int c = live ? q / TPC : 0;
-                    limb_part<QT>(it.a, c, q % TPC, live, smem + kMmaStages * STAGE + c * 16, (int64_t)chunks * 16);
+                    limb_part<QT>(it.a, c, q % TPC, live, smem + kMmaStages * STAGE + c * (G * 16), 16);
                 }
             }
             asm volatile("bar.sync 1, %0;" ::"n"(kMmaWarps * 32) : "memory");
@@ -743,8 +745,8 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
                 const int cc = cok ? c : chunks - 1;
                 const uint4 wa = *reinterpret_cast<const uint4*>(pa + cc * 16);
                 const uint4 wb = *reinterpret_cast<const uint4*>(pb + cc * 16);
-                const uint32_t lp = limb_s + (uint32_t)cc * 16;  // this chunk's granule 0
-                const uint32_t gs = (uint32_t)chunks * 16;
+                const uint32_t lp = limb_s + (uint32_t)cc * (G * 16);  // this chunk's granule 0
+                constexpr uint32_t gs = 16;
                 const uint4 rec = lds128(lp + (G - 1) * gs);
                 uint32_t bw[8];
                 load_limbs<QT>(bw, lp, gs, L, cok && limb_lane, zaddr);
