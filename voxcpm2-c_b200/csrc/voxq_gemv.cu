@@ -565,7 +565,12 @@ constexpr int kMmaWarps = 8;                     // consumer warps (+1 producer)
 constexpr int kMmaStages = 2;
 constexpr int kMmaTile = 32768;                  // code bytes per stage
 constexpr int kMmaTW = kMmaTile / 4 + 32;        // trailer window bytes per stage
-constexpr int kMmaSmem = kMmaStages * (kMmaTile + kMmaTW);
+// A stage: the code region (two halves of the tile's rows, see split_tile)
+// and the trailer region, each with room for the gap between the halves.
+constexpr int kMmaCodeRgn = kMmaTile + 256;
+constexpr int kMmaTrRgn = kMmaTW + 256;
+constexpr int kMmaStage = kMmaCodeRgn + kMmaTrRgn;
+constexpr int kMmaSmem = kMmaStages * kMmaStage;
 constexpr int kMmaLimbMax = 16384;               // limb record of the largest item (K <= 4096)
 // groups (four 16-byte chunks of a row) per K part: 256 bytes of Q4 codes, 128 of Q8
 __host__ __device__ constexpr int groups_per_part(int qtype) { return qtype == VOXQ_Q4 ? 4 : 2; }
@@ -627,13 +632,78 @@ __device__ __forceinline__ void load_limbs(uint32_t (&bw)[8], uint32_t lp, uint3
     }
 }
 
+// How a tile's rows sit in a stage: the first acnt = min(8 nrt, rows) rows
+// (half A) and the rest (half B) are copied to regions whose starts differ by
+// 64 bytes modulo 128, for the codes and for the trailers.  The consumer gives
+// the even lanes of a quad group rows of half A and the odd lanes rows of half
+// B, so the two rows one quarter-warp reads sit in different banks (rows of one
+// half are a multiple of 128 bytes apart for the usual K).
+struct SplitTile {
+    int acnt;                  // rows in half A
+    int cB;                    // start of half B's codes in the code region
+    int tdA, tB;               // trailer region: half A's offset of row 0; start of half B's window
+    int tdB;                   // half B's offset of its row 0 in its window
+    uint32_t cbA, cbB, tbA, tbB;
+    int64_t saA, saB;          // 16-byte aligned trailer sources
+};
+__device__ __forceinline__ SplitTile split_tile(int row0, int rows, int rowb, int srow) {
+    SplitTile x;
+    const int nrt = (rows + 15) >> 4;
+    x.acnt = min(nrt * 8, rows);
+    x.cbA = (uint32_t)(x.acnt * rowb);
+    x.cbB = (uint32_t)((rows - x.acnt) * rowb);
+    x.cB = (int)((x.cbA + 127) & ~127u) + 64;
+    const int64_t soA = (int64_t)row0 * srow, soB = (int64_t)(row0 + x.acnt) * srow;
+    x.saA = soA & ~(int64_t)15;
+    x.saB = soB & ~(int64_t)15;
+    x.tdA = (int)(soA - x.saA);
+    x.tdB = (int)(soB - x.saB);
+    x.tbA = (uint32_t)((x.tdA + x.acnt * srow + 15) & ~15);
+    x.tbB = rows > x.acnt ? (uint32_t)((x.tdB + (rows - x.acnt) * srow + 15) & ~15) : 0u;
+    x.tB = (int)((x.tbA + 127) & ~127u) + 64;
+    return x;
+}
+
+// Producer of the tensor-path kernel (lane 0 of the producer warp): up to
+// four bulk copies per tile (codes and trailers of each half).
+template <int MAXI>
+__device__ __forceinline__ void produce_split(const GemvParams<MAXI>& p, int tb, int te, uint64_t* full,
+                                              uint64_t* empty, uint8_t* smem) {
+    int item = 0;
+    for (int t = tb, j = 0; t < te; ++t, ++j) {
+        fix_item(p, t, item);
+        const GemvItemDev& it = p.it[item];
+        const int s = j % kMmaStages;
+        if (j >= kMmaStages) mbar_wait_bounded(&empty[s], ((j / kMmaStages) & 1) ^ 1, VOXQ_DEVERR_WAIT_EMPTY, p.err);
+        const int row0 = (t - it.tile_begin) * it.T;
+        const int rows = min(it.T, it.N - row0);
+        const SplitTile x = split_tile(row0, rows, it.rowb, it.srow);
+        mbar_arrive_expect_tx(&full[s], x.cbA + x.cbB + x.tbA + x.tbB);
+        uint8_t* st = smem + s * kMmaStage;
+        bulk_g2s(st, it.codes + (int64_t)row0 * it.rowb, x.cbA, &full[s]);
+        bulk_g2s(st + kMmaCodeRgn, it.scales + x.saA, x.tbA, &full[s]);
+        if (x.cbB) {
+            bulk_g2s(st + x.cB, it.codes + (int64_t)(row0 + x.acnt) * it.rowb, x.cbB, &full[s]);
+            bulk_g2s(st + kMmaCodeRgn + x.tB, it.scales + x.saB, x.tbB, &full[s]);
+        }
+    }
+    // Normally the consumers have waited for every copy.  If a wait gave up,
+    // give the copies still in flight a bounded moment to land before the
+    // CTA's shared memory is released.
+    if (*reinterpret_cast<volatile int*>(p.err) != 0) {
+        const int n = te - tb;
+        for (int j = (n > kMmaStages ? n - kMmaStages : 0); j < n; j++)
+            mbar_wait_bounded(&full[j % kMmaStages], (j / kMmaStages) & 1, VOXQ_DEVERR_WAIT_FULL, p.err, 20u);
+    }
+}
+
 // TRX (Q4, every item's trailer rows a multiple of 16 bytes): trailers handed
 // to the lanes through a per-warp scratch (see the unit loop).
 template <int QT, bool SIGNED, bool TRX, int MAXI>
 __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const __grid_constant__ GemvParams<MAXI> p) {
     constexpr int G = limb_granules(QT);
     constexpr int SB = (QT == VOXQ_Q4) ? 4 : 8;  // trailer bytes per block
-    constexpr int STAGE = kMmaTile + kMmaTW;
+    constexpr int STAGE = kMmaStage;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[kMmaStages], empty[kMmaStages];
     // row sums of each (row tile, K part) unit; two sets, alternating between
@@ -657,7 +727,7 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
     const int te = (int)((int64_t)p.total_tiles * (blockIdx.x + 1) / gridDim.x);
 
     if (warp == kMmaWarps) {
-        if (lane == 0) produce_tiles<kMmaStages, kMmaTile, kMmaTW, 1>(p, tb, te, full, empty, smem);
+        if (lane == 0) produce_split(p, tb, te, full, empty, smem);
         pdl_launch_dependents();
         return;
     }
@@ -712,14 +782,24 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
         const uint8_t* st = smem + s * STAGE;
         const int row0 = (t - tbeg) * T;
         const int rows = min(T, N - row0);
-        const uint8_t* trs = st + kMmaTile + (int)(((int64_t)row0 * srow) & 15);
         const int nrt = (rows + 15) >> 4;  // 16-row tiles
+        const SplitTile x = split_tile(row0, rows, rowb, srow);
+        // this lane's half: even g -> half A, odd g -> half B (half A when B is empty)
+        const int half = g & 1;
+        const int hcnt = half ? rows - x.acnt : x.acnt;
+        const bool inB = half && hcnt > 0;
+        const int hc = inB ? hcnt : x.acnt;
+        const uint8_t* hcode = st + (inB ? x.cB : 0);
+        const uint8_t* htr = st + kMmaCodeRgn + (inB ? x.tB + x.tdB : x.tdA);
+        const int hbase = half ? x.acnt : 0;  // tile row of the half's row 0
         for (int rt = rt0, kp = kp0; rt < nrt;) {
-            const int rA = min(rt * 16 + g, rows - 1), rB = min(rt * 16 + g + 8, rows - 1);
-            const uint8_t* pa = st + rA * rowb;
-            const uint8_t* pb = st + rB * rowb;
-            const uint8_t* ta = trs + rA * srow;
-            const uint8_t* tb2 = trs + rB * srow;
+            // MMA rows g and g + 8 = rows i1 and i1 + 4 of this lane's half
+            const int i1 = rt * 8 + (g >> 1), i2 = i1 + 4;
+            const int c1 = min(i1, hc - 1), c2 = min(i2, hc - 1);
+            const uint8_t* pa = hcode + c1 * rowb;
+            const uint8_t* pb = hcode + c2 * rowb;
+            const uint8_t* ta = htr + c1 * srow;
+            const uint8_t* tb2 = htr + c2 * srow;
             float accA = 0.0f, accB = 0.0f;
             constexpr int GPP = groups_per_part(QT);
             if (TRX) {
@@ -793,14 +873,15 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
             accA += __shfl_xor_sync(0xffffffffu, accA, 2);
             accB += __shfl_xor_sync(0xffffffffu, accB, 2);
             if (tq == 0) {
-                const int ra = rt * 16 + g, rb = ra + 8;
+                const int ra = hbase + i1, rb = hbase + i2;  // tile rows
+                const bool oka = i1 < hcnt, okb = i2 < hcnt;
                 if (P == 1) {
                     const GemvItemDev& it = p.it[item];
-                    if (ra < rows) write_out(it, row0 + ra, 0, accA);
-                    if (rb < rows) write_out(it, row0 + rb, 0, accB);
+                    if (oka) write_out(it, row0 + ra, 0, accA);
+                    if (okb) write_out(it, row0 + rb, 0, accB);
                 } else {
-                    if (ra < rows) part[pset][ra * P + kp] = accA;
-                    if (rb < rows) part[pset][rb * P + kp] = accB;
+                    if (oka) part[pset][ra * P + kp] = accA;
+                    if (okb) part[pset][rb * P + kp] = accB;
                 }
             }
             // next unit of this warp: kMmaWarps units further in (row tile, part) order
