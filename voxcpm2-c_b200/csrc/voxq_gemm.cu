@@ -922,12 +922,15 @@ static int env_int(const char* name) {
 
 static GemmPlan plan_gemm(int M, int N, int K, int qt) {
     static const int forced_bn = env_int("VOXQ_GEMM_BN"), forced_s = env_int("VOXQ_GEMM_SPLIT");
-    static const int forced_path = env_int("VOXQ_GEMM_TWO_PHASE");  // 1: always, -1: never
+    static const int forced_path = env_int("VOXQ_GEMM_TWO_PHASE");  // -1: the fused kernel
     GemmPlan p;
-    // Large batches are tensor-bound: dequantizing the weight once per call (about
-    // 2.6 B/weight of extra traffic) is cheaper than the dequant pipeline of the
-    // fused kernel, which repeats it for every activation tile.
-    p.two_phase = forced_path > 0 || (forced_path == 0 && M >= 512);
+    // Dequantizing the weight once per call (about 2.6 B/weight of extra traffic)
+    // and running a plain TMA -> tcgen05 GEMM beats the fused kernel's dequant
+    // pipeline, which repeats the dequant for every activation tile, at every
+    // measured size: config-3 sweep on B200, M = 16 .. 2048, e.g. M = 256,
+    // N = 4096 15.3 vs 17.3 us (Q8) and 15.1 vs 18.0 us (Q4); the one exception,
+    // Q8 M = 64 N = 1024, is 3 % slower.  The fused kernel stays selectable.
+    p.two_phase = forced_path >= 0;
     if (forced_bn == 16 || forced_bn == 32 || forced_bn == 64 || forced_bn == 128 || forced_bn == 256) {
         p.bn = forced_bn;
     } else {
