@@ -553,8 +553,14 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32) gemv_kernel(const __gri
 // The third limb (rare: chunks with a dominant value) is a second block-
 // diagonal B in column 2t, issued only when a lane of the warp needs it.
 //
-// A stage holds T rows (at most 32 KB of codes); two stages per CTA and two
-// CTAs per SM, whose tiles run out of phase.  K is cut into fixed parts of
+// The limbs are computed by the kernel itself: when a CTA's tile range enters
+// a new item, its consumer warps split the item's activation row into a
+// shared-memory record (chunk-major; the arithmetic of the dp4a kernel's
+// prepass, limb_part), so no prepass launch precedes this kernel.
+//
+// A stage holds T rows (at most 32 KB of codes) in two halves (split_tile);
+// two stages per CTA and two CTAs per SM, whose tiles run out of phase.
+// K is cut into fixed parts of
 // groups_per_part groups (four chunks each); a stage's work is (16-row tile,
 // K part) units spread over the 8 consumer warps, and each row's parts are
 // summed in part order through shared memory.  The summation order depends
