@@ -10,11 +10,23 @@ weight bytes + fp32 activation and output bytes).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--config c2|c1|c3]
 
+The default line also carries, under "configs", the other BASELINE configs
+measured in the same run on GPU 0: config 1 (one Q8 GEMV), the config-3 GEMM
+sweep (16 shapes), the config-2 step as a dependent chain (each layer's
+inputs are the previous outputs: QKV -> O -> gate/up -> down, 120 launches
+replayed from a CUDA graph), per-call costs through the reference ABI
+(tensor_matmul_nt_cuda with host buffers), and the reference's own GPU path
+(src/tensor_cuda.cu + src/tensor.c built unchanged for sm_100: cuBLAS FP32
+SGEMM on dequantized weights) on the same workloads.
+
 Multi-GPU: the batch-1 path does not shard (replicas only); under torchrun
 each rank runs its own replica and `value` sums the ranks' bytes over the
-slowest rank's device time.  `--impl reference` times the reference's own CPU
-implementation (tensor_matmul_nt from src/tensor.c, built unchanged into
-oracle/_ref) on a bounded sample of the same workload, on all host threads.
+slowest rank's device time.  Each rank also runs its column shard of a
+config-3 GEMM (weight rows split across ranks, no collective on the data
+path) and the line reports per-rank device times.  `--impl reference` times
+the reference's own CPU implementation (tensor_matmul_nt from src/tensor.c,
+built unchanged into oracle/_ref) on a bounded sample of the same workload,
+on all host threads.
 """
 from __future__ import annotations
 
@@ -170,22 +182,52 @@ def run_ours(args, torch, dist, rank, world, local_rank):
         torch.cuda.synchronize(dev)
         barrier()
     ms = e0.elapsed_time(e1)
-    ms_max = ms
+    per_rank_ms = [ms]
     if dist is not None:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+        t = torch.zeros(world, device=dev)
+        t[rank] = ms
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        per_rank_ms = [float(v) for v in t.tolist()]
+    ms_max = max(per_rank_ms)
     ms_per_step = ms_max / args.steps
     value = world * algo_bytes / (ms_per_step * 1e-3) / 1e9
     achieved = algo_bytes / (ms / args.steps * 1e-3) / 1e9  # this rank's kernel, one launch per step
 
-    # ---- end to end through the public C ABI with host buffers ----
+    # ---- end to end through the public C ABI with host buffers (every rank; summed) ----
     e2e = run_e2e(torch, voxq, dev, stream, sets[0], args, algo_bytes)
-    e2e_abi = run_e2e_tensor_abi(torch, voxq, dev, args, algo_bytes, rank) if args.tensor_abi else None
+    if dist is not None:
+        t = torch.zeros(world, device=dev)
+        t[rank] = e2e["ms_per_step"]
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        e2e_ms = [float(v) for v in t.tolist()]
+        e2e["per_rank_ms_per_step"] = [round(v, 5) for v in e2e_ms]
+        e2e["ms_per_step"] = round(max(e2e_ms), 5)
+        e2e["value"] = round(world * algo_bytes / (max(e2e_ms) * 1e-3) / 1e9, 1)
+        e2e["aggregate"] = "all ranks' bytes over the slowest rank's time"
+    e2e_abi = run_e2e_tensor_abi(torch, voxq, dev, args, algo_bytes, rank) if (args.tensor_abi and rank == 0) else None
 
+    configs = {}
+    if world > 1:
+        configs["c3_sharded"] = measure_sharded_c3(torch, voxq, dist, dev, stream, rank, world, args.steps,
+                                                    args.warmup)
     cpu = None
-    if rank == 0 and world == 1 and args.cpu_seconds > 0:
-        cpu = cpu_baseline(args.cpu_seconds, threads=1)
+    if rank == 0 and world == 1:
+        if args.configs:
+            configs["c1"] = measure_c1(torch, voxq, dev, stream, args.steps, args.warmup)
+            configs["c2_chain"] = measure_c2_chain(torch, voxq, dev, stream, qtype, max(20, args.steps // 20),
+                                                   args.warmup)
+            configs["c3"] = measure_c3(torch, voxq, dev, stream, args.steps, args.warmup, eager=False)
+            if args.tensor_abi:
+                shapes = [(M, N, 1024) for N in C3_N for M in C3_M]
+                configs["tensor_abi_per_call"] = {
+                    "what": "wall-clock us per tensor_matmul_nt_cuda call, host a/out, quantized device weights",
+                    "q4_c2_shapes": measure_abi_calls(torch, voxq, "q4", [(1, N, K) for (_, N, K, _) in C2_LAYER[:5]]
+                                                      + [(1, H, F)], 200),
+                    "q8_c3": measure_abi_calls(torch, voxq, "q8", shapes, 40),
+                }
+            configs["reference_gpu"] = measure_ref_gpu(args)
+        if args.cpu_seconds > 0:
+            cpu = cpu_baseline(args.cpu_seconds, threads=1)
 
     # the single-row launch runs the tensor-path GEMV unless VOXQ_GEMV_MMA=0
     mma = os.environ.get("VOXQ_GEMV_MMA", "1")[:1] != "0"
@@ -212,15 +254,21 @@ def run_ours(args, torch, dist, rank, world, local_rank):
             "dtype": "q4 weights, fp32 activations/accumulate",
             "data": "synthetic: weights 0.02*N(0,1) quantized on device to Q4, activations N(0,1)",
             "config": {
-                "workload": "BASELINE config 2: 24-layer batch-1 decode step, Q/K/V/O/gate/up/down GEMVs, Q4, one grouped launch",
+                "workload": "BASELINE config 2: 24-layer batch-1 decode step, Q/K/V/O/gate/up/down GEMVs, Q4, "
+                            "independent inputs, one grouped launch (the dependent chain is configs.c2_chain)",
                 "gemvs_per_step": n_items, "hidden": H, "ffn": F, "kv_dim": KV, "layers": LAYERS,
                 "weight_bytes_per_step": wbytes, "algorithmic_bytes_per_step": algo_bytes,
                 "l2": "inputs larger than L2: two 224 MB weight sets alternated between steps",
                 "parallelism": f"replicas x{world} (batch-1 GEMV does not shard)",
             },
+            "per_rank_ms": [round(v, 4) for v in per_rank_ms],
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
-                         "traffic": traffic, "kernel": kernel},
+                         "traffic": traffic,
+                         "traffic_source": "profiles/traffic.json: dram__bytes_read.sum + dram__bytes_write.sum "
+                                           "of one launch of this kernel on this workload from an ncu capture "
+                                           "(copied, not measured in this run)" if traffic else None,
+                         "kernel": kernel},
             "e2e": e2e,
             # per step: the tensor-path GEMV splits its activations itself (one launch);
             # the dp4a kernel needs the limb prepass before it (two)
@@ -231,6 +279,8 @@ def run_ours(args, torch, dist, rank, world, local_rank):
             line["e2e_tensor_abi"] = e2e_abi
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if configs:
+            line["configs"] = configs
         print(json.dumps(line), flush=True)
 
 
@@ -411,29 +461,25 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def run_c1(args, torch):
+def measure_c1(torch, voxq, dev, st, steps, warmup):
     """one Q8 GEMV, W [4096, 1024] = 0.02 N(0,1) quantized on device, x [1, 1024]
     N(0,1), y [1, 4096].  The weight fits in L2, so 64 weight copies (> 335 MB) are rotated and the
     calls are replayed from a CUDA graph (device time per call; host launch cost excluded)."""
-    import voxq
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
     hbm, bf16, bf16s, peak_kind = peaks()
-    st = torch.cuda.Stream(dev)
     N, K, copies = 4096, 1024, 64
     g = torch.Generator(device=dev).manual_seed(1)
     ws = [voxq.QWeight.from_float(torch.randn(N, K, device=dev, generator=g) * 0.02, voxq.Q8) for _ in range(copies)]
     x = torch.randn(1, K, device=dev, generator=g)
     y = torch.empty(1, N, device=dev)
     with torch.cuda.stream(st):
-        for i in range(max(args.warmup, 3)):
+        for i in range(max(warmup, 3)):
             voxq.matmul_nt_q(x, ws[i % copies], out=y, stream=st)
     torch.cuda.synchronize(dev)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=st):
         for i in range(copies):
             voxq.matmul_nt_q(x, ws[i], out=y, stream=st)
-    loops = max(1, args.steps // copies)
+    loops = max(2, steps // copies)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(st):
@@ -443,45 +489,58 @@ def run_c1(args, torch):
             graph.replay()
         e1.record(st)
     torch.cuda.synchronize(dev)
+    del graph
     calls = loops * copies
     ms = e0.elapsed_time(e1) / calls
     byts = N * K * 5 // 4 + 4 * K + 4 * N  # 5,263,360 B
     gbs = byts / (ms * 1e-3) / 1e9
-    print(json.dumps({"metric": "c1_q8_gemv_hbm_GBps", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
-                      "steps": calls, "warmup": max(args.warmup, 3), "us_per_call": round(ms * 1e3, 3),
-                      "higher_is_better": True, "dtype": "q8 weights, fp32 activations/accumulate",
-                      "data": "synthetic: 0.02*N(0,1) weights quantized on device to Q8, N(0,1) activation",
-                      "config": {"workload": "BASELINE config 1: Q8 GEMV N=4096 K=1024",
-                                 "algorithmic_bytes_per_call": byts, "weight_copies": copies,
-                                 "l2": "64 rotated weight copies (335 MB > L2)"},
-                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
-                                   "frac": round(gbs / hbm, 4), "peak_kind": peak_kind},
-                      "gpu_launches": (1 if os.environ.get("VOXQ_GEMV_MMA", "1")[:1] != "0" else 2) * calls,
-                      "device_error": voxq.lib().voxq_device_error(1)}), flush=True)
+    mma = os.environ.get("VOXQ_GEMV_MMA", "1")[:1] != "0"
+    return {"metric": "c1_q8_gemv_hbm_GBps", "value": round(gbs, 1), "unit": "GB/s", "us_per_call": round(ms * 1e3, 3),
+            "calls": calls, "workload": "BASELINE config 1: Q8 GEMV N=4096 K=1024, CUDA-graph replay",
+            "algorithmic_bytes_per_call": byts, "l2": "64 rotated weight copies (335 MB > L2)",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs / hbm, 4), "peak_kind": peak_kind},
+            "gpu_launches": (1 if mma else 2) * calls, "device_error": voxq.lib().voxq_device_error(1)}
 
 
-def run_c3(args, torch):
-    """BASELINE config 3 sweep (one JSON line per shape): K = 1024, N in {1024, 4096},
-    M in {16, 64, 256, 2048}, Q8 and Q4, one voxq_matmul_nt_q call per step.
+def run_c1(args, torch):
+    import voxq
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    print(json.dumps(measure_c1(torch, voxq, dev, torch.cuda.Stream(dev), args.steps, args.warmup)), flush=True)
+
+
+C3_M = (16, 64, 256, 2048)
+C3_N = (1024, 4096)
+
+
+def c3_roof(M, N, K, qt_q8, ms):
+    hbm, bf16, bf16s, peak_kind = peaks()
+    wbytes = int(N * K * (1.25 if qt_q8 else 0.625))
+    flops = 2.0 * M * N * K
+    byts = wbytes + 4 * M * K + 4 * M * N
+    tf = flops / (ms * 1e-3) / 1e12
+    gbs = byts / (ms * 1e-3) / 1e9
+    bound = "tensor" if flops / byts > bf16 * 1e12 / (hbm * 1e9) else "hbm"
+    frac = tf / bf16 if bound == "tensor" else gbs / hbm
+    return {"TFLOPs": round(tf, 1), "GBps": round(gbs, 1), "bound": bound, "frac": round(frac, 4),
+            "peak_kind": peak_kind, "algorithmic_bytes": byts}
+
+
+def measure_c3(torch, voxq, dev, st, steps, warmup, only=None, eager=True):
+    """BASELINE config 3 sweep: K = 1024, N in {1024, 4096}, M in {16, 64, 256, 2048}, Q8 and Q4,
+    one voxq_matmul_nt_q call per step.
 
     `us` is device time per call: the calls (prepass, GEMM and any split-K reduction
     kernel each) are captured in a CUDA graph and replayed, so host launch cost is
     excluded; `us_eager` is the same loop launched from Python call by call.  Weight
-    copies are rotated so the weights of consecutive calls never share L2 (> 126 MB
-    in total)."""
-    import voxq
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    hbm, bf16, bf16s, peak_kind = peaks()
-    st = torch.cuda.Stream(dev)
+    copies are rotated so the weights of consecutive calls never share L2 (> 300 MB
+    in total).  Returns one dict per shape."""
     K = 1024
     g = torch.Generator(device=dev).manual_seed(3)
-    only = None
-    if args.shape:  # "M,N,q8|q4": one shape (profiling)
-        m_, n_, q_ = args.shape.split(",")
-        only = (int(m_), int(n_), voxq.Q8 if q_.lower() == "q8" else voxq.Q4)
+    rows = []
     for qt in (voxq.Q8, voxq.Q4):
-        for N in (1024, 4096):
+        for N in C3_N:
             if only and (qt != only[2] or N != only[1]):
                 continue
             wbytes = int(N * K * (1.25 if qt == voxq.Q8 else 0.625))
@@ -489,14 +548,14 @@ def run_c3(args, torch):
             copies = 4 if only else max(2, int(300e6 // wbytes) + 1)
             ws = [voxq.QWeight.from_float(torch.randn(N, K, device=dev, generator=g) * 0.02, qt)
                   for _ in range(copies)]
-            for M in (16, 64, 256, 2048):
+            for M in C3_M:
                 if only and M != only[0]:
                     continue
                 a = torch.randn(M, K, device=dev, generator=g)
                 out = torch.empty(M, N, device=dev)
                 reps = max(copies, 64)
                 with torch.cuda.stream(st):
-                    for i in range(max(args.warmup, 3)):
+                    for i in range(max(warmup, 3)):
                         voxq.matmul_nt_q(a, ws[i % copies], out=out, stream=st)
                 torch.cuda.synchronize(dev)
                 graph = torch.cuda.CUDAGraph()
@@ -508,7 +567,7 @@ def run_c3(args, torch):
                 torch.cuda.synchronize(dev)
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
-                loops = max(1, args.steps // reps)
+                loops = max(2, steps // reps)
                 with torch.cuda.stream(st):  # replay() launches on the current stream
                     e0.record(st)
                     for _ in range(loops):
@@ -517,28 +576,320 @@ def run_c3(args, torch):
                 torch.cuda.synchronize(dev)
                 ms = e0.elapsed_time(e1) / (loops * reps)
                 del graph
-                with torch.cuda.stream(st):
-                    e0.record(st)
-                    for i in range(reps):
-                        voxq.matmul_nt_q(a, ws[i % copies], out=out, stream=st)
-                    e1.record(st)
-                torch.cuda.synchronize(dev)
-                ms_eager = e0.elapsed_time(e1) / reps
-                err = voxq.lib().voxq_device_error(1)
-                flops = 2.0 * M * N * K
-                byts = wbytes + 4 * M * K + 4 * M * N
-                tf = flops / (ms * 1e-3) / 1e12
-                gbs = byts / (ms * 1e-3) / 1e9
-                ai = flops / byts
-                bound = "tensor" if ai > bf16 * 1e12 / (hbm * 1e9) else "hbm"
-                frac = tf / bf16 if bound == "tensor" else gbs / hbm
-                print(json.dumps({"config": "c3", "qtype": "q8" if qt == voxq.Q8 else "q4", "M": M, "N": N, "K": K,
-                                  "us": round(ms * 1e3, 2), "us_eager": round(ms_eager * 1e3, 2),
-                                  "TFLOPs": round(tf, 1), "GBps": round(gbs, 1), "bound": bound,
-                                  "frac": round(frac, 4), "peak_kind": peak_kind,
-                                  "path": "gemv" if M <= 8 else "tcgen05 gemm", "weight_copies": copies,
-                                  "device_error": err}), flush=True)
+                row = {"qtype": "q8" if qt == voxq.Q8 else "q4", "M": M, "N": N, "K": K, "us": round(ms * 1e3, 2)}
+                if eager:
+                    with torch.cuda.stream(st):
+                        e0.record(st)
+                        for i in range(reps):
+                            voxq.matmul_nt_q(a, ws[i % copies], out=out, stream=st)
+                        e1.record(st)
+                    torch.cuda.synchronize(dev)
+                    row["us_eager"] = round(e0.elapsed_time(e1) / reps * 1e3, 2)
+                row.update(c3_roof(M, N, K, qt == voxq.Q8, ms))
+                row.update({"path": "gemv" if M <= 8 else "tcgen05 gemm", "weight_copies": copies,
+                            "device_error": voxq.lib().voxq_device_error(1)})
+                rows.append(row)
             del ws
+    return rows
+
+
+def run_c3(args, torch):
+    import voxq
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    only = None
+    if args.shape:  # "M,N,q8|q4": one shape (profiling)
+        m_, n_, q_ = args.shape.split(",")
+        only = (int(m_), int(n_), voxq.Q8 if q_.lower() == "q8" else voxq.Q4)
+    for row in measure_c3(torch, voxq, dev, torch.cuda.Stream(dev), args.steps, args.warmup, only):
+        row["config"] = "c3"
+        print(json.dumps(row), flush=True)
+
+
+def measure_c2_chain(torch, voxq, dev, st, qtype, steps, warmup, seed=77):
+    """Config 2 as a dependent decode step: per layer, Q/K/V from the layer input
+    (one grouped launch), O from Q (+ the layer input as residual), gate/up from
+    O with the fused SwiGLU epilogue, down from that (+ O as residual); the down
+    output is the next layer's input.  Attention and the norms are not on the
+    matmul path and are left out, so O reads Q directly.  Each step is captured
+    once in a CUDA graph (one per weight set; two sets alternate so every step
+    streams its 224 MB of weights from HBM) and replayed."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    graphs, launches = [], 0
+    keep = []
+    mma = os.environ.get("VOXQ_GEMV_MMA", "1")[:1] != "0"
+    for copy in range(2):
+        W = []
+        for layer in range(LAYERS):
+            W.append({name: voxq.QWeight.from_float(torch.randn(N, K, device=dev, generator=g) * 0.02, qtype)
+                      for (name, N, K, _) in C2_LAYER})
+        xs = [torch.randn(1, H, device=dev, generator=g)] + [torch.empty(1, H, device=dev) for _ in range(LAYERS)]
+        qs = [torch.empty(1, H, device=dev) for _ in range(LAYERS)]
+        kvs = [torch.empty(1, KV, device=dev) for _ in range(2 * LAYERS)]
+        os_ = [torch.empty(1, H, device=dev) for _ in range(LAYERS)]
+        hs = [torch.empty(1, F, device=dev) for _ in range(LAYERS)]
+        qkv = [voxq.make_gemv_items([dict(w=W[l]["q"], a=xs[l], out=qs[l]), dict(w=W[l]["k"], a=xs[l], out=kvs[2 * l]),
+                                     dict(w=W[l]["v"], a=xs[l], out=kvs[2 * l + 1])]) for l in range(LAYERS)]
+
+        def step(W=W, xs=xs, qs=qs, os_=os_, hs=hs, qkv=qkv):
+            for l in range(LAYERS):
+                voxq.gemv_batch(qkv[l], stream=st)
+                voxq.matmul_nt_q(qs[l], W[l]["o"], out=os_[l], residual=xs[l], stream=st)
+                voxq.matmul_nt_q(os_[l], W[l]["gate"], out=hs[l], up=W[l]["up"], stream=st)
+                voxq.matmul_nt_q(hs[l], W[l]["down"], out=xs[l + 1], residual=os_[l], stream=st)
+        with torch.cuda.stream(st):
+            for _ in range(max(warmup, 3)):
+                step()
+        torch.cuda.synchronize(dev)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=st):
+            step()
+        graphs.append(gr)
+        keep.append((W, xs, qs, kvs, os_, hs, qkv, step))
+    # QKV, O, down: one launch each on the tensor-path GEMV; gate/up with SwiGLU: limb prepass + GEMV
+    launches = LAYERS * ((3 if mma else 6) + 2)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        for i in range(4):
+            graphs[i & 1].replay()
+        torch.cuda.synchronize(dev)
+        e0.record(st)
+        for i in range(steps):
+            graphs[i & 1].replay()
+        e1.record(st)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    # the same chain launched call by call from Python (host launch cost included)
+    k_eager = max(3, min(steps, 50))
+    with torch.cuda.stream(st):
+        e0.record(st)
+        for i in range(k_eager):
+            keep[i & 1][-1]()
+        e1.record(st)
+    torch.cuda.synchronize(dev)
+    ms_eager = e0.elapsed_time(e1) / k_eager
+    del graphs
+    hbm, _, _, peak_kind = peaks()
+    algo_bytes, _ = c2_bytes_per_step(qtype)
+    gbs = algo_bytes / (ms * 1e-3) / 1e9
+    return {"metric": "c2_q4_decode_chain_hbm_GBps", "value": round(gbs, 1), "unit": "GB/s",
+            "ms_per_step": round(ms, 5), "ms_per_step_eager": round(ms_eager, 4),
+            "value_eager": round(algo_bytes / (ms_eager * 1e-3) / 1e9, 1),
+            "workload": "BASELINE config 2, dependent: 24 layers x (QKV grouped -> O(+res) -> gate/up SwiGLU -> "
+                        "down(+res)), each input the previous output; CUDA-graph replay (value) and Python "
+                        "launches (value_eager)",
+            "launches_per_step": launches, "algorithmic_bytes_per_step": algo_bytes,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs / hbm, 4), "peak_kind": peak_kind},
+            "device_error": voxq.lib().voxq_device_error(1)}
+
+
+def measure_abi_calls(torch, voxq, qname, shapes, reps):
+    """Per-call cost of tensor_matmul_nt_cuda (the reference ABI the unchanged
+    engine calls) with host activations and outputs, weights uploaded and
+    quantized by tensor_to_cuda under VOXCPM_QUANT=qname.  Wall clock per call."""
+    L = voxq.lib()
+    os.environ["VOXCPM_QUANT"] = qname
+    L.tensor_cuda_shutdown()
+    if L.tensor_cuda_init() != 0:
+        return [{"unavailable": "tensor_cuda_init failed"}]
+    g = torch.Generator().manual_seed(5)
+    rows = []
+    try:
+        for (M, N, K) in shapes:
+            w = voxq.host_tensor((torch.randn(N, K, generator=g) * 0.02).numpy())
+            a = voxq.host_tensor(torch.randn(M, K, generator=g).numpy())
+            o = voxq.host_tensor(np.zeros((M, N), np.float32))
+            try:
+                voxq.check(L.tensor_to_cuda(w), "tensor_to_cuda")
+                for _ in range(3):
+                    voxq.check(L.tensor_matmul_nt_cuda(a, w, o), "tensor_matmul_nt_cuda")
+                k = max(3, reps if M <= 256 else reps // 4)
+                t0 = time.perf_counter()
+                for _ in range(k):
+                    L.tensor_matmul_nt_cuda(a, w, o)
+                us = (time.perf_counter() - t0) * 1e6 / k
+                rows.append({"M": M, "N": N, "K": K, "us": round(us, 2)})
+            finally:
+                for t in (w, a, o):
+                    voxq.free_tensor(t)
+    finally:
+        L.tensor_cuda_shutdown()
+        os.environ.pop("VOXCPM_QUANT", None)
+    return rows
+
+
+REF_GPU_LIB = os.path.join(REPO, "oracle", "_ref", "libref_tensor_cuda.so")
+
+
+def ref_gpu_worker(args):
+    """Runs in its own process (the reference library exports the same tensor_*
+    symbols as libvoxq): the reference's GPU path, src/tensor_cuda.cu + src/tensor.c
+    built unchanged for sm_100.  tensor_matmul_nt -> tensor_matmul_nt_cuda ->
+    cuBLAS FP32 SGEMM on device fp32 weights (the reference has no quantized GPU
+    path; Q4/Q8 files are dequantized to fp32 at load), per-call cudaMalloc,
+    copies and cudaDeviceSynchronize.  Prints one JSON object."""
+    sys.path.insert(0, REPO)
+    from oracle import oracle as O
+    L = C.CDLL(REF_GPU_LIB)
+    TP = C.POINTER(O.RefTensor)
+    L.tensor_create.argtypes = [C.c_int, C.POINTER(C.c_int)]
+    L.tensor_create.restype = TP
+    L.tensor_free.argtypes = [TP]
+    for f in ("tensor_to_cuda", "tensor_matmul_nt"):
+        getattr(L, f).restype = C.c_int
+    L.tensor_to_cuda.argtypes = [TP]
+    L.tensor_matmul_nt.argtypes = [TP, TP, TP]
+    L.tensor_cuda_init.restype = C.c_int
+    if L.tensor_cuda_init() != 0:
+        print(json.dumps({"unavailable": "reference tensor_cuda_init failed"}))
+        return
+    rng = np.random.default_rng(17)
+
+    def make(shape, scale=1.0):
+        t = L.tensor_create(len(shape), (C.c_int * len(shape))(*shape))
+        n = int(np.prod(shape))
+        buf = (C.c_float * n).from_address(C.cast(t.contents.data, C.c_void_p).value)
+        np.frombuffer(buf, dtype=np.float32)[:] = rng.standard_normal(n, dtype=np.float32) * np.float32(scale)
+        return t
+
+    out = {}
+    # config 2: 168 synchronous calls per step, host activations and outputs
+    ws, ins, outs = [], [], []
+    for layer in range(LAYERS):
+        for (_, N, K, _) in C2_LAYER:
+            w = make((N, K), 0.02)
+            if L.tensor_to_cuda(w) != 0:
+                print(json.dumps({"unavailable": "reference tensor_to_cuda failed"}))
+                return
+            ws.append(w)
+            ins.append(make((1, K)))
+            outs.append(make((1, N)))
+
+    def c2_step():
+        for w, a, o in zip(ws, ins, outs):
+            if L.tensor_matmul_nt(a, w, o) != 0:
+                raise RuntimeError("reference tensor_matmul_nt failed")
+    for _ in range(3):
+        c2_step()
+    k = max(3, min(args.steps, 20))
+    t0 = time.perf_counter()
+    for _ in range(k):
+        c2_step()
+    ms = (time.perf_counter() - t0) * 1e3 / k
+    algo_bytes, _ = c2_bytes_per_step(2)
+    out["c2"] = {"ms_per_step": round(ms, 3), "value": round(algo_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                 "us_per_call": round(ms * 1e3 / len(ws), 2),
+                 "path": "168 x tensor_matmul_nt (reference, VOXCPM_CUDA): host a/out, fp32 device weights, cuBLAS"}
+    for t in ws + ins + outs:
+        L.tensor_free(t)
+    # config 3: per shape, host a/out (engine path) and device a/out (kernel + the call's sync)
+    rows = []
+    K = 1024
+    for N in C3_N:
+        w = make((N, K), 0.02)
+        L.tensor_to_cuda(w)
+        for M in C3_M:
+            a, o = make((M, K)), make((M, N))
+            for _ in range(2):
+                L.tensor_matmul_nt(a, w, o)
+            reps = 20 if M < 2048 else 6
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                L.tensor_matmul_nt(a, w, o)
+            us_host = (time.perf_counter() - t0) * 1e6 / reps
+            L.tensor_to_cuda(a)
+            L.tensor_to_cuda(o)
+            for _ in range(2):
+                L.tensor_matmul_nt(a, w, o)
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                L.tensor_matmul_nt(a, w, o)
+            us_dev = (time.perf_counter() - t0) * 1e6 / reps
+            rows.append({"M": M, "N": N, "K": K, "us_host_io": round(us_host, 1), "us_device_io": round(us_dev, 1),
+                         "TFLOPs_device_io": round(2.0 * M * N * K / (us_dev * 1e-6) / 1e12, 2)})
+            L.tensor_free(a)
+            L.tensor_free(o)
+        L.tensor_free(w)
+    out["c3"] = rows
+    print(json.dumps(out), flush=True)
+
+
+def measure_ref_gpu(args):
+    """The reference's GPU bar, timed in a child process (see ref_gpu_worker)."""
+    if not os.path.exists(REF_GPU_LIB):
+        return {"unavailable": "oracle/_ref/libref_tensor_cuda.so not built (needs the reference checkout)"}
+    try:
+        r = subprocess.run([sys.executable, os.path.abspath(__file__), "--ref-gpu-worker", "--steps", str(args.steps)],
+                           capture_output=True, text=True, timeout=600)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "reference GPU worker timed out"}
+    for line in reversed(r.stdout.strip().splitlines()):
+        if line.startswith("{"):
+            d = json.loads(line)
+            d["build"] = "src/tensor.c (-DVOXCPM_CUDA) + src/tensor_cuda.cu unchanged, nvcc sm_100, cuBLAS"
+            return d
+    return {"unavailable": f"reference GPU worker exited {r.returncode}: {r.stderr.strip()[-300:]}"}
+
+
+def measure_sharded_c3(torch, voxq, dist, dev, st, rank, world, steps, warmup):
+    """Config-3 GEMM column shards (no collective): rank r owns weight rows
+    [r*N/G, (r+1)*N/G), quantized on its own GPU, and writes its column slice of
+    out[M, N] from the full activation block.  Weak: N = 4096 per rank (the
+    weight grows with the ranks); strong: N = 4096 in total.  Each rank's device
+    time per call (CUDA-graph replay, rotated weights) is gathered; the
+    aggregate TFLOP/s is all ranks' flops over the slowest rank's time."""
+    M, K = 2048, 1024
+    res = {}
+    for kind, n_total in (("weak", 4096 * world), ("strong", 4096)):
+        n_loc = n_total // world
+        g = torch.Generator(device=dev).manual_seed(1000 + rank)
+        copies = 8
+        ws = [voxq.QWeight.from_float(torch.randn(n_loc, K, device=dev, generator=g) * 0.02, voxq.Q8)
+              for _ in range(copies)]
+        a = torch.randn(M, K, device=dev, generator=torch.Generator(device=dev).manual_seed(7))
+        out = torch.empty(M, n_loc, device=dev)
+        with torch.cuda.stream(st):
+            for i in range(max(warmup, 3)):
+                voxq.matmul_nt_q(a, ws[i % copies], out=out, stream=st)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        reps = 32
+        with torch.cuda.graph(graph, stream=st):
+            for i in range(reps):
+                voxq.matmul_nt_q(a, ws[i % copies], out=out, stream=st)
+        loops = max(2, steps // reps)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        with torch.cuda.stream(st):
+            e0.record(st)
+            for _ in range(loops):
+                graph.replay()
+            e1.record(st)
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) / (loops * reps) * 1e3
+        del graph
+        per_rank = [us]
+        if dist is not None:
+            t = torch.zeros(world, device=dev)
+            t[rank] = us
+            dist.all_reduce(t, op=dist.ReduceOp.SUM)
+            per_rank = [round(float(v), 2) for v in t.tolist()]
+        us_max = max(per_rank)
+        flops = 2.0 * M * n_total * K
+        res[kind] = {"M": M, "N_total": n_total, "N_per_rank": n_loc, "K": K, "qtype": "q8",
+                     "us_max": round(us_max, 2), "TFLOPs": round(flops / (us_max * 1e-6) / 1e12, 1),
+                     "per_rank_us": [round(v, 2) for v in per_rank],
+                     "device_error": voxq.lib().voxq_device_error(1)}
+        del ws
+    return res
 
 
 def main():
@@ -553,8 +904,14 @@ def main():
     ap.add_argument("--shape", default="", help="c3 only: one shape 'M,N,q8|q4'")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3"],
                     help="c2: the headline decode step (default); c1: one Q8 GEMV; c3: GEMM sweep, one line per shape")
+    ap.add_argument("--no-configs", dest="configs", action="store_false",
+                    help="c2 line without the configs object (C1, C3, chain, reference GPU)")
+    ap.add_argument("--ref-gpu-worker", action="store_true", help=argparse.SUPPRESS)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.ref_gpu_worker:
+        ref_gpu_worker(args)
+        return
     if args.config in ("c1", "c3"):
         import torch
         (run_c1 if args.config == "c1" else run_c3)(args, torch)

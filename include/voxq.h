@@ -130,8 +130,10 @@ VOXQ_API VoxCPMError voxq_set_device(int device);
 /* Device-side status of the current device's kernels: 0, or the code of the
  * first bounded wait that gave up (1 full-stage, 2 empty-stage, 3 MMA
  * completion, 4 tensor-memory allocation).  A kernel that gives up returns
- * early instead of hanging; its outputs are then undefined.  clear != 0 resets
- * the word.  Returns -1 if the word cannot be read. */
+ * early instead of hanging; its outputs are then undefined.  Covers the
+ * library's kernels and those of voxq_matmul_nt_q_noalloc (the library's
+ * word is reported first).  clear != 0 resets both words.  Returns -1 if a
+ * word cannot be read. */
 VOXQ_API int voxq_device_error(int clear);
 
 /* Failure-detection self-test (no counterpart in the reference): launches one
@@ -218,17 +220,28 @@ VOXQ_API VoxCPMError voxq_matmul_nt_q(const float* d_a, int M, int64_t lda, cons
  * allocate: engines that reserve their whole device-memory budget up front, or
  * hosts that forbid device allocation after set-up because cudaMalloc /
  * cudaFree can synchronise the device and stall a real-time audio stream.
- * Its scratch is a fixed array of VOXQ_NOALLOC_SCRATCH_BYTES inside the
- * library's own device image (every GPU that loads the library holds it until
- * exit), which covers every shape the GEMV accepts (K <= 16384 for Q8, 32768
- * for Q4).  Larger scratch needs -> VOXCPM_ERR_OOM; M > 8 ->
+ * Its scratch is a fixed array of VOXQ_NOALLOC_SCRATCH_BYTES (896 KiB) inside
+ * the library's own device image (every GPU that loads the library holds it
+ * until exit).  The activation limbs it holds take M * 3.5 * K bytes for Q4 and
+ * M * 4 * K bytes for Q8, so it covers every shape the GEMV accepts: M <= 8,
+ * K <= 32768 for Q4 and K <= 16384 for Q8 (half those K with the SwiGLU `up`
+ * weight).  Larger K -> VOXCPM_ERR_UNSUPPORTED (the GEMV's own limit); a
+ * scratch need above the array -> VOXCPM_ERR_OOM; M > 8 ->
  * VOXCPM_ERR_UNSUPPORTED.  The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress) and clears its error word, so make
- * that first call before any stream capture.  All calls share the one array:
- * calls that overlap on the GPU (other streams, other host threads) race. */
-#define VOXQ_NOALLOC_SCRATCH_BYTES (512 * 1024)
+ * device address (cudaGetSymbolAddress) and clears its error word on `stream`,
+ * waiting for that stream, so make that first call before any stream capture.
+ * All calls share the one array and keep no state in it between calls: calls
+ * that overlap on the GPU (other streams, other host threads) race. */
+#define VOXQ_NOALLOC_SCRATCH_BYTES (896 * 1024)
 VOXQ_API VoxCPMError voxq_matmul_nt_q_noalloc(const float* d_a, int M, int64_t lda, const voxq_qweight* w,
                                               float* d_out, int64_t ldo, const voxq_epilogue* epi, void* stream);
+
+/* Device-side status of voxq_matmul_nt_q_noalloc's kernels on the current
+ * device, read without allocating: 0, or the code of the first bounded wait
+ * that gave up (same codes as voxq_device_error, which reports this word too).
+ * clear != 0 resets it.  Returns -1 if the word cannot be read.  No
+ * counterpart in the reference. */
+VOXQ_API int voxq_noalloc_device_error(int clear);
 
 /* Dense fp32 / fp16 weights (the reference's unquantized path,
  * src/tensor_cuda.cu:192-333), full fp32 arithmetic. */

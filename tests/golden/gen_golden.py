@@ -1,9 +1,10 @@
 #!/usr/bin/env python3
 """Regenerates the golden fixtures in this folder from the reference itself.
 
-Run in a checkout that has the reference at REF (default /root/reference):
+Run where the reference checkout is available (its path from --ref, else the
+VOXCPM_REF environment variable, else BASELINE.json's "reference_path"):
 
-    python tests/golden/gen_golden.py [--ref /root/reference]
+    python tests/golden/gen_golden.py [--ref <reference checkout>]
 
 It writes:
   ref_quant/            output of the reference's ``scripts/gen_test_data.py
@@ -41,6 +42,17 @@ sys.path.insert(0, HERE)
 sys.path.insert(0, REPO)
 
 import cases  # noqa: E402
+
+
+def default_ref():
+    """The reference checkout: $VOXCPM_REF, else BASELINE.json's reference_path."""
+    if os.environ.get("VOXCPM_REF"):
+        return os.environ["VOXCPM_REF"]
+    try:
+        with open(os.path.join(os.path.dirname(os.path.dirname(HERE)), "BASELINE.json")) as f:
+            return json.load(f).get("reference_path")
+    except (OSError, ValueError):
+        return None
 
 
 def load_quantize(ref: str):
@@ -107,7 +119,8 @@ def sha(b) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=default_ref(), required=default_ref() is None,
+                    help="reference checkout (default: $VOXCPM_REF or BASELINE.json reference_path)")
     args = ap.parse_args()
     warnings.simplefilter("ignore")
     Q = load_quantize(args.ref)

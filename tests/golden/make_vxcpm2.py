@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Regenerates the VXCPM2 container fixtures in this folder.
 
-    python tests/golden/make_vxcpm2.py [--ref /root/reference]
+    python tests/golden/make_vxcpm2.py [--ref <reference checkout>]
 
 vxcpm2_f32.bin is written here from seeded tensors in the container layout
 that the reference's quantizer reads (scripts/quantize.py:119-162: 256-byte
@@ -20,6 +20,7 @@ import contextlib
 import hashlib
 import importlib.util
 import io
+import json
 import os
 import struct
 import zlib
@@ -43,6 +44,17 @@ HEADER = dict(version=2, n_layers=2, n_layers_enc=1, n_ralm_layers=1, n_dit_laye
               audio_vae_dim=64, rope_theta=10000.0)
 HEADER_ORDER = ["version", "n_layers", "n_layers_enc", "n_ralm_layers", "n_dit_layers", "d_model", "d_ff", "n_heads",
                 "n_kv_heads", "head_dim", "max_seq_len", "vocab_size", "quant", "sample_rate", "audio_vae_dim"]
+
+
+def default_ref():
+    """The reference checkout: $VOXCPM_REF, else BASELINE.json's reference_path."""
+    if os.environ.get("VOXCPM_REF"):
+        return os.environ["VOXCPM_REF"]
+    try:
+        with open(os.path.join(os.path.dirname(os.path.dirname(HERE)), "BASELINE.json")) as f:
+            return json.load(f).get("reference_path")
+    except (OSError, ValueError):
+        return None
 
 
 def tensor_values(i: int) -> np.ndarray:
@@ -83,7 +95,8 @@ def write_f32(path: str) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=default_ref(), required=default_ref() is None,
+                    help="reference checkout (default: $VOXCPM_REF or BASELINE.json reference_path)")
     args = ap.parse_args()
     spec = importlib.util.spec_from_file_location("ref_quantize", os.path.join(args.ref, "scripts", "quantize.py"))
     q = importlib.util.module_from_spec(spec)

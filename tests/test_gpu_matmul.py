@@ -236,6 +236,36 @@ def test_gemm_matches_tensor_c(qt, M, N):
     assert_matmul_close(y, y_ref, sc, TOL_GEMM, f"gemm M{M} N{N}")
 
 
+# Rows of the M = 2048 outputs checked against the CPU checker: eight rows in
+# each 256-row activation tile (its first and last rows, both sides of the
+# 64- and 128-row boundaries), 64 in all.
+C3_ROWS_2048 = np.array([t * 256 + r for t in range(8) for r in (0, 1, 63, 64, 127, 128, 200, 255)])
+
+
+@pytest.mark.parametrize("qt", [voxq.Q8, voxq.Q4], ids=["q8", "q4"])
+@pytest.mark.parametrize("M", [16, 64, 256, 2048])
+@pytest.mark.parametrize("N", [1024, 4096])
+def test_gemm_c3_sweep_vs_tensor_c(qt, M, N):
+    """Every config-3 case (K = 1024), each of which takes its own launch plan
+    (tile width, split-K factor, one or two weight sub-tiles per tile), against
+    tensor_matmul_nt (src/tensor.c:617-678) on the dequantized weight."""
+    K = 1024
+    qw, wdeq = make_weight(N, K, qt, seed=3000 + 7 * M + N)
+    a = O.rand_normal(4000 + M + N, M * K).reshape(M, K)
+    y = voxq.matmul_nt_q(torch.from_numpy(a).cuda(), qw).cpu().numpy()
+    rows = np.arange(M) if M <= 256 else C3_ROWS_2048
+    y_ref, sc = ref(a[rows], wdeq)
+    assert_matmul_close(y[rows], y_ref, sc, TOL_GEMM, f"c3 M{M} N{N} q{qt}")
+    if M == 2048:
+        # all rows against an fp64 product of the same operands
+        yd = torch.from_numpy(y).double()
+        wd = torch.from_numpy(wdeq).double()
+        ad = torch.from_numpy(a).double()
+        y64 = ad @ wd.T
+        sc64 = (ad.abs() @ wd.abs().T) / np.sqrt(K)
+        assert bool(((yd - y64).abs() <= TOL_GEMM * torch.maximum(y64.abs(), sc64)).all())
+
+
 def test_gemm_c3_largest_against_fp64():
     """C3's largest shape (M=2048, N=4096, K=1024) on device data, fp64 torch check."""
     M, N, K = 2048, 4096, 1024

@@ -1188,10 +1188,12 @@ static VoxCPMError launch_items(const voxq_gemv_item* const* sel, int n, cudaStr
     return dispatch<MAXI>(p, qt, mt, swi, f.w.q8_signed != 0, use_mma, st);
 }
 
+// Limb workspace of the items: the tensor-path kernel's items compute their
+// limbs in shared memory and need none.
 size_t gemv_workspace_bytes(const voxq_gemv_item* items, int count) {
     size_t total = 0;
     for (int i = 0; i < count; i++)
-        if (items[i].w.K > 0 && items[i].M > 0)
+        if (items[i].w.K > 0 && items[i].M > 0 && !mma_item(items[i]))
             total += (limb_bytes(items[i].M, items[i].w.K, items[i].w.qtype) + 255) & ~(size_t)255;
     return total;
 }
@@ -1225,7 +1227,7 @@ VoxCPMError gemv_launch_ws(const voxq_gemv_item* items, int count, cudaStream_t 
         // each variant group gets its own part of the workspace
         size_t need = 0;
         for (int k = 0; k < n; k++)
-            if (sel[k]->w.K > 0 && sel[k]->M > 0)
+            if (sel[k]->w.K > 0 && sel[k]->M > 0 && !mma_item(*sel[k]))
                 need += (limb_bytes(sel[k]->M, sel[k]->w.K, sel[k]->w.qtype) + 255) & ~(size_t)255;
         uint8_t* part = static_cast<uint8_t*>(ws) + used;
         VoxCPMError e = (n == 1) ? launch_items<1>(sel, n, st, part, ws_bytes - used, err)

@@ -42,6 +42,10 @@ VoxCPMError widen_fp16(const uint16_t* src, float* dst, size_t n, cudaStream_t s
 // Per-device device-side error word (allocated on first use, zeroed).
 int* device_error_word();
 
+// Error word of voxq_matmul_nt_q_noalloc on the current device (a static
+// device variable; reading it allocates nothing).  -1 if it cannot be read.
+int noalloc_error(bool clear);
+
 // Per-device workspace arena (voxq_runtime.cu): grows on demand, never
 // shrinks, ordered on the stream that uses it.
 void* workspace(size_t bytes);

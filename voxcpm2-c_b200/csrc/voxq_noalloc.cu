@@ -11,12 +11,18 @@
 // library image itself carries in device memory.
 //
 // The scratch is a file-scope static __device__ array of
-// VOXQ_NOALLOC_SCRATCH_BYTES bytes (512 KiB, enough for every GEMV shape the
-// kernel accepts: M <= 8 rows, K <= 16384 for Q8 / 32768 for Q4).  Every GPU
-// that loads the library holds it until the process exits.  Host code cannot
-// hand the array's name to a kernel (on the host it is only a stand-in, not a
-// device address), so the device address is looked up with
+// VOXQ_NOALLOC_SCRATCH_BYTES bytes (896 KiB).  The activation limbs take
+// M * 7 * K / 2 bytes for Q4 and M * 4 * K bytes for Q8, so the array covers
+// every GEMV shape the kernel accepts: M <= 8 rows, K <= 32768 for Q4
+// (917,504 bytes at the limit) and K <= 16384 for Q8 (524,288 bytes).  Every
+// GPU that loads the library holds it until the process exits.  Host code
+// cannot hand the array's name to a kernel (on the host it is only a
+// stand-in, not a device address), so the device address is looked up with
 // cudaGetSymbolAddress once per device, on that device's first call.
+//
+// Kernels launched here record a bounded wait that gave up in this file's own
+// error word, g_noalloc_error.  voxq_noalloc_device_error reads it without
+// allocating anything; voxq_device_error reports it too.
 #include <mutex>
 
 #include "voxq_common.cuh"
@@ -38,8 +44,10 @@ NoallocDev g_na[kMaxDevices];
 std::mutex g_na_mu;
 
 // Resolves (once per device, with that device current) the device addresses
-// of the static scratch array and error word, and clears the error word.
-VoxCPMError noalloc_setup(int dev, NoallocDev** out) {
+// of the static scratch array and error word, and clears the error word on the
+// caller's stream (waiting for it, so the clear is done before any launch on
+// any stream).
+VoxCPMError noalloc_setup(int dev, cudaStream_t st, NoallocDev** out) {
     std::lock_guard<std::mutex> lk(g_na_mu);
     NoallocDev& d = g_na[dev];
     if (!d.ready) {
@@ -57,8 +65,13 @@ VoxCPMError noalloc_setup(int dev, NoallocDev** out) {
                     cudaGetErrorString(e));
             return VOXCPM_ERR_INTERNAL;
         }
-        e = cudaMemset(q, 0, sizeof(int));
-        if (e != cudaSuccess) return VOXCPM_ERR_INTERNAL;
+        e = cudaMemsetAsync(q, 0, sizeof(int), st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) {
+            fprintf(stderr, "[voxq] noalloc: clearing the error word failed on device %d: %s\n", dev,
+                    cudaGetErrorString(e));
+            return VOXCPM_ERR_INTERNAL;
+        }
         d.scratch = p;
         d.err = static_cast<int*>(q);
         d.ready = true;
@@ -67,6 +80,22 @@ VoxCPMError noalloc_setup(int dev, NoallocDev** out) {
     return VOXCPM_SUCCESS;
 }
 }  // namespace
+
+int noalloc_error(bool clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_noalloc_error, sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    if (clear && v) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbol(g_noalloc_error, &zero, sizeof(int)) != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+    }
+    return v;
+}
 
 }  // namespace voxq
 
@@ -105,13 +134,15 @@ extern "C" VoxCPMError voxq_matmul_nt_q_noalloc(const float* d_a, int M, int64_t
     const size_t need = gemv_workspace_bytes(&it, 1);
     if (need > VOXQ_NOALLOC_SCRATCH_BYTES) {
         fprintf(stderr, "[voxq] voxq_matmul_nt_q_noalloc: needs %zu scratch bytes, the fixed array holds %d\n", need,
-                VOXQ_NOALLOC_SCRATCH_BYTES);
+                (int)VOXQ_NOALLOC_SCRATCH_BYTES);
         return VOXCPM_ERR_OOM;
     }
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return VOXCPM_ERR_CUDA_NOT_FOUND;
     NoallocDev* d = nullptr;
-    e = noalloc_setup(dev, &d);
+    e = noalloc_setup(dev, (cudaStream_t)stream, &d);
     if (e) return e;
     return gemv_launch_ws(&it, 1, (cudaStream_t)stream, d->scratch, VOXQ_NOALLOC_SCRATCH_BYTES, d->err);
 }
+
+extern "C" int voxq_noalloc_device_error(int clear) { return noalloc_error(clear != 0); }

@@ -174,8 +174,10 @@ extern "C" int voxq_device_error(int clear) {
     if (!e) return -1;
     int v = 0;
     if (cudaMemcpy(&v, e, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
-    if (clear && v) cudaMemset(e, 0, sizeof(int));
-    return v;
+    if (clear && v && cudaMemset(e, 0, sizeof(int)) != cudaSuccess) return -1;
+    const int na = noalloc_error(clear != 0);
+    if (na < 0) return -1;
+    return v ? v : na;
 }
 
 extern "C" VoxCPMError voxq_set_device(int device) {
@@ -297,29 +299,51 @@ extern "C" VoxCPMError tensor_to_cuda(Tensor* t) {
     if (quantize) {
         const int N = t->shape[0], K = t->shape[1], qt = s->quant;
         const size_t n = (size_t)N * K;
+        const size_t cb = voxq_codes_bytes(N, K, qt), sb = voxq_scales_bytes(N, K, qt);
+        // every temporary is released on every exit; `base` is kept only on success
         float* d_f32 = nullptr;
-        VOXQ_CUDA_TRY(cudaMalloc(&d_f32, n * sizeof(float)));
+        uint16_t* d_h = nullptr;
+        void* base = nullptr;
+        auto fail = [&](VoxCPMError e, cudaError_t ce, const char* what) {
+            if (ce != cudaSuccess)
+                fprintf(stderr, "[voxq] tensor_to_cuda: %s failed: %s\n", what, cudaGetErrorString(ce));
+            cudaStreamSynchronize(s->stream);
+            cudaGetLastError();
+            if (d_h) cudaFree(d_h);
+            if (d_f32) cudaFree(d_f32);
+            if (base) cudaFree(base);
+            return e;
+        };
+        cudaError_t ce;
+        if ((ce = cudaMalloc(&d_f32, n * sizeof(float))) != cudaSuccess) {
+            d_f32 = nullptr;
+            return fail(VOXCPM_ERR_OOM, ce, "cudaMalloc");
+        }
+        if ((ce = cudaMalloc(&base, align256(cb) + sb)) != cudaSuccess) {
+            base = nullptr;
+            return fail(VOXCPM_ERR_OOM, ce, "cudaMalloc");
+        }
         if (t->is_fp16) {
-            uint16_t* d_h = nullptr;
-            VOXQ_CUDA_TRY(cudaMalloc(&d_h, n * 2));
-            VOXQ_CUDA_TRY(cudaMemcpy(d_h, t->data_fp16, n * 2, cudaMemcpyHostToDevice));
+            if ((ce = cudaMalloc(&d_h, n * 2)) != cudaSuccess) {
+                d_h = nullptr;
+                return fail(VOXCPM_ERR_OOM, ce, "cudaMalloc");
+            }
+            if ((ce = cudaMemcpy(d_h, t->data_fp16, n * 2, cudaMemcpyHostToDevice)) != cudaSuccess)
+                return fail(VOXCPM_ERR_INTERNAL, ce, "cudaMemcpy");
             // exact widening, then the quantizer sees the same floats quantize.py would
             VoxCPMError e = widen_fp16(d_h, d_f32, n, s->stream);
-            if (e) return e;
-            VOXQ_CUDA_TRY(cudaStreamSynchronize(s->stream));
-            VOXQ_CUDA_TRY(cudaFree(d_h));
-        } else {
-            VOXQ_CUDA_TRY(cudaMemcpy(d_f32, t->data, n * sizeof(float), cudaMemcpyHostToDevice));
+            if (e) return fail(e, cudaSuccess, "");
+        } else if ((ce = cudaMemcpy(d_f32, t->data, n * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess) {
+            return fail(VOXCPM_ERR_INTERNAL, ce, "cudaMemcpy");
         }
-        const size_t cb = voxq_codes_bytes(N, K, qt), sb = voxq_scales_bytes(N, K, qt);
-        void* base = nullptr;
-        VOXQ_CUDA_TRY(cudaMalloc(&base, align256(cb) + sb));
         uint8_t* codes = (uint8_t*)base;
         void* scales = (uint8_t*)base + align256(cb);
         VoxCPMError e = voxq_quantize_weight(d_f32, N, K, qt, codes, scales, nullptr, s->stream);
-        if (e) return e;
-        VOXQ_CUDA_TRY(cudaStreamSynchronize(s->stream));
-        VOXQ_CUDA_TRY(cudaFree(d_f32));
+        if (e) return fail(e, cudaSuccess, "");
+        if ((ce = cudaStreamSynchronize(s->stream)) != cudaSuccess)
+            return fail(VOXCPM_ERR_INTERNAL, ce, "cudaStreamSynchronize");
+        if (d_h) cudaFree(d_h);
+        cudaFree(d_f32);
         {
             std::lock_guard<std::mutex> lk(g_mu);
             g_qtab[base] = QRec{base, codes, scales, N, K, qt, t->is_fp16};

@@ -30,7 +30,7 @@ ERRORS = {
     -6: "VOXCPM_ERR_OOM", -7: "VOXCPM_ERR_GPU", -8: "VOXCPM_ERR_INTERNAL", -9: "VOXCPM_ERR_UNSUPPORTED",
     -10: "VOXCPM_ERR_TIMEOUT", -11: "VOXCPM_ERR_CUDA_NOT_FOUND",
 }
-SHAPE_MISMATCH, INTERNAL, UNSUPPORTED, CUDA_NOT_FOUND = -5, -8, -9, -11
+SHAPE_MISMATCH, OOM, INTERNAL, UNSUPPORTED, CUDA_NOT_FOUND = -5, -6, -8, -9, -11
 
 
 class VoxqError(RuntimeError):
@@ -113,6 +113,7 @@ SIGNATURES = {
     "voxq_unpack_blocks": ([_vp, _vp, _i, _i, _i, _vp, _vp], _i),
     "voxq_matmul_nt_q": ([_vp, _i, _i64, C.POINTER(QWeightDesc), _vp, _i64, C.POINTER(Epilogue), _vp], _i),
     "voxq_matmul_nt_q_noalloc": ([_vp, _i, _i64, C.POINTER(QWeightDesc), _vp, _i64, C.POINTER(Epilogue), _vp], _i),
+    "voxq_noalloc_device_error": ([_i], _i),
     "voxq_matmul_nt_dense": ([_vp, _i, _i64, _vp, _i, _i, _i, _vp, _i64, _vp], _i),
     "voxq_gemv_batch": ([C.POINTER(GemvItem), _i, _vp], _i),
     "voxq_vxcpm2_open": ([C.c_char_p, C.POINTER(_vp)], _i),
