@@ -222,10 +222,14 @@ def run_ours(args, torch, dist, rank, world, local_rank):
                 configs["tensor_abi_per_call"] = {
                     "what": "wall-clock us per tensor_matmul_nt_cuda call, host a/out, quantized device weights",
                     "q4_c2_shapes": measure_abi_calls(torch, voxq, "q4", [(1, N, K) for (_, N, K, _) in C2_LAYER[:5]]
-                                                      + [(1, H, F)], 200),
+                                                      + [(1, H, F)], 200, breakdown=True),
                     "q8_c3": measure_abi_calls(torch, voxq, "q8", shapes, 40),
                 }
             configs["reference_gpu"] = measure_ref_gpu(args)
+            try:
+                configs["c4"] = measure_c4(args.c4_patches)
+            except Exception as e:  # the engine run is reported, never fatal to the headline line
+                configs["c4"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
         if args.cpu_seconds > 0:
             cpu = cpu_baseline(args.cpu_seconds, threads=1)
 
@@ -685,10 +689,25 @@ def measure_c2_chain(torch, voxq, dev, st, qtype, steps, warmup, seed=77):
             "device_error": voxq.lib().voxq_device_error(1)}
 
 
-def measure_abi_calls(torch, voxq, qname, shapes, reps):
+def _device_tensor(voxq, t):
+    """A reference Tensor that borrows a CUDA torch tensor (is_cuda, not owned)."""
+    T = voxq.Tensor()
+    shp = (C.c_int * t.dim())(*t.shape)
+    T.data = C.cast(C.c_void_p(t.data_ptr()), C.POINTER(C.c_float))
+    T.shape = C.cast(shp, C.POINTER(C.c_int))
+    T.ndim = t.dim()
+    T.size = t.numel()
+    T.is_cuda = True
+    return T, shp
+
+
+def measure_abi_calls(torch, voxq, qname, shapes, reps, breakdown=False):
     """Per-call cost of tensor_matmul_nt_cuda (the reference ABI the unchanged
     engine calls) with host activations and outputs, weights uploaded and
-    quantized by tensor_to_cuda under VOXCPM_QUANT=qname.  Wall clock per call."""
+    quantized by tensor_to_cuda under VOXCPM_QUANT=qname.  Wall clock per call.
+    With `breakdown`, the same call also with a device activation (no staging
+    or host->device copy), with a device output (no output path or wait), and
+    with both on the device (launch only; one device synchronisation per loop)."""
     L = voxq.lib()
     os.environ["VOXCPM_QUANT"] = qname
     L.tensor_cuda_shutdown()
@@ -696,21 +715,35 @@ def measure_abi_calls(torch, voxq, qname, shapes, reps):
         return [{"unavailable": "tensor_cuda_init failed"}]
     g = torch.Generator().manual_seed(5)
     rows = []
+
+    def timed(a, w, o, k, sync=False):
+        for _ in range(3):
+            voxq.check(L.tensor_matmul_nt_cuda(a, w, o), "tensor_matmul_nt_cuda")
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(k):
+            L.tensor_matmul_nt_cuda(a, w, o)
+        if sync:
+            torch.cuda.synchronize()
+        return round((time.perf_counter() - t0) * 1e6 / k, 2)
     try:
         for (M, N, K) in shapes:
             w = voxq.host_tensor((torch.randn(N, K, generator=g) * 0.02).numpy())
-            a = voxq.host_tensor(torch.randn(M, K, generator=g).numpy())
+            a_np = torch.randn(M, K, generator=g).numpy()
+            a = voxq.host_tensor(a_np)
             o = voxq.host_tensor(np.zeros((M, N), np.float32))
             try:
                 voxq.check(L.tensor_to_cuda(w), "tensor_to_cuda")
-                for _ in range(3):
-                    voxq.check(L.tensor_matmul_nt_cuda(a, w, o), "tensor_matmul_nt_cuda")
                 k = max(3, reps if M <= 256 else reps // 4)
-                t0 = time.perf_counter()
-                for _ in range(k):
-                    L.tensor_matmul_nt_cuda(a, w, o)
-                us = (time.perf_counter() - t0) * 1e6 / k
-                rows.append({"M": M, "N": N, "K": K, "us": round(us, 2)})
+                row = {"M": M, "N": N, "K": K, "us": timed(a, w, o, k)}
+                if breakdown:
+                    ad = torch.from_numpy(a_np).cuda()
+                    od = torch.empty(M, N, device="cuda")
+                    (ta, s1), (to, s2) = _device_tensor(voxq, ad), _device_tensor(voxq, od)
+                    row["us_device_a"] = timed(C.byref(ta), w, o, k)
+                    row["us_device_out"] = timed(a, w, C.byref(to), k, sync=True)
+                    row["us_device_both"] = timed(C.byref(ta), w, C.byref(to), k, sync=True)
+                rows.append(row)
             finally:
                 for t in (w, a, o):
                     voxq.free_tensor(t)
@@ -833,6 +866,74 @@ def measure_ref_gpu(args):
     return {"unavailable": f"reference GPU worker exited {r.returncode}: {r.stderr.strip()[-300:]}"}
 
 
+ENGINE_BUILD = os.path.join(REPO, "voxcpm2-c_b200", "engine", "_build")
+ENGINE_GOLDEN = os.path.join(REPO, "tests", "golden", "engine_c4_q8.json")
+
+
+def _engine_run(exe, model, patches, env_extra, extra_args=()):
+    env = dict(os.environ, **env_extra)
+    r = subprocess.run([os.path.join(ENGINE_BUILD, exe), "--model", model, "--patches", str(patches),
+                        "--tokens", "64", "--token-seed", "1", *extra_args], env=env, capture_output=True,
+                       text=True, timeout=3600)
+    if r.returncode != 0:
+        return {"unavailable": f"{exe} exited {r.returncode}: {r.stderr.strip()[-300:]}"}
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    d["per_patch_s"] = {k: round(v["s"] / patches, 5) for k, v in d["stages"].items()}
+    return d
+
+
+def measure_c4(patches=4, workdir=None, cpu_patches=0):
+    """one utterance through the unchanged reference engine
+    (src/*.c compiled as they are) on the seeded random-init model: 64 token
+    ids, `patches` patches (4 frames each), 10 Euler steps, CFG 2.0.  Three
+    builds of the same engine: with libvoxq (VOXCPM_CUDA, VOXCPM_QUANT=q8),
+    with the reference's own src/tensor_cuda.cu (cuBLAS FP32 on the stored
+    fp16 weights), and, when cpu_patches > 0, without VOXCPM_CUDA (the CPU
+    path, one host thread).  RTF = wall time of voxcpm_generate / audio
+    seconds; per-stage times from the harness (voxq_engine_run.c)."""
+    import shutil
+    import tempfile
+    for exe in ("make_model", "voxq_engine_run_gpu"):
+        if not os.path.exists(os.path.join(ENGINE_BUILD, exe)):
+            return {"unavailable": f"{exe} not built (make -C voxcpm2-c_b200/engine REF=<reference checkout>)"}
+    base = workdir or os.environ.get("VOXQ_MODEL_DIR") or tempfile.gettempdir()
+    if shutil.disk_usage(base).free < 12e9:
+        return {"unavailable": f"less than 12 GB free in {base} for the 5 GB model"}
+    work = tempfile.mkdtemp(prefix="voxq_c4_", dir=base)
+    try:
+        t0 = time.perf_counter()
+        gen = json.loads(subprocess.run([os.path.join(ENGINE_BUILD, "make_model"), os.path.join(work, "rand"),
+                                         "--seed", "1"], check=True, capture_output=True,
+                                        text=True).stdout.strip().splitlines()[-1])
+        gen_s = time.perf_counter() - t0
+        model = os.path.join(work, "rand.vxcpm")
+        out = {"workload": f"BASELINE config 4 slice: unchanged engine, 64 token ids, {patches} patches, "
+                           "10 Euler steps, CFG 2.0, random-init model (Q8-exact projection weights)",
+               "model_gen_s": round(gen_s, 1), "model_bytes": gen["model_bytes"] + gen["audiovae_bytes"]}
+        out["ours"] = _engine_run("voxq_engine_run_gpu", model, patches, {"VOXCPM_QUANT": "q8"}, ["--gpu"])
+        if os.path.exists(os.path.join(ENGINE_BUILD, "voxq_engine_run_refgpu")):
+            out["reference_gpu"] = _engine_run("voxq_engine_run_refgpu", model, patches, {}, ["--gpu"])
+        if cpu_patches > 0:
+            out["reference_cpu"] = _engine_run("voxq_engine_run_cpu", model, cpu_patches, {})
+        elif os.path.exists(ENGINE_GOLDEN):
+            g = json.load(open(ENGINE_GOLDEN))
+            c = g["cpu_run"]
+            c["per_patch_s"] = {k: round(v["s"] / c["patches"], 5) for k, v in c["stages"].items()}
+            c["measured_on"] = f"the build host ({g.get('cpu', '?')}), not this GPU host"
+            out["reference_cpu"] = c
+        return out
+    finally:
+        shutil.rmtree(work, ignore_errors=True)
+
+
+def run_c4(args):
+    d = measure_c4(args.c4_patches, cpu_patches=args.c4_cpu_patches)
+    ours = d.get("ours", {})
+    line = {"metric": "c4_rtf", "value": ours.get("rtf"), "unit": "s/s", "higher_is_better": False,
+            "n_gpus": 1, "config": {"workload": d.get("workload")}, "c4": d}
+    print(json.dumps(line), flush=True)
+
+
 def measure_sharded_c3(torch, voxq, dist, dev, st, rank, world, steps, warmup):
     """Config-3 GEMM column shards (no collective): rank r owns weight rows
     [r*N/G, (r+1)*N/G), quantized on its own GPU, and writes its column slice of
@@ -902,8 +1003,11 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-tensor-abi", dest="tensor_abi", action="store_false")
     ap.add_argument("--shape", default="", help="c3 only: one shape 'M,N,q8|q4'")
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3"],
-                    help="c2: the headline decode step (default); c1: one Q8 GEMV; c3: GEMM sweep, one line per shape")
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4"],
+                    help="c2: the headline decode step (default); c1: one Q8 GEMV; c3: GEMM sweep, one line per "
+                         "shape; c4: the unchanged engine's RTF")
+    ap.add_argument("--c4-patches", type=int, default=4)
+    ap.add_argument("--c4-cpu-patches", type=int, default=0, help="c4: also time the CPU engine on this many patches")
     ap.add_argument("--no-configs", dest="configs", action="store_false",
                     help="c2 line without the configs object (C1, C3, chain, reference GPU)")
     ap.add_argument("--ref-gpu-worker", action="store_true", help=argparse.SUPPRESS)
@@ -915,6 +1019,9 @@ def main():
     if args.config in ("c1", "c3"):
         import torch
         (run_c1 if args.config == "c1" else run_c3)(args, torch)
+        return
+    if args.config == "c4":
+        run_c4(args)
         return
 
     rank = int(os.environ.get("RANK", "0"))

@@ -15,6 +15,7 @@
 
 #include <mutex>
 #include <unordered_map>
+#include <vector>
 
 #include "voxq_common.cuh"
 #include "voxq_internal.h"
@@ -44,6 +45,7 @@ struct DevState {
     size_t h_in_bytes = 0;
     void* h_out = nullptr;
     size_t h_out_bytes = 0;
+    std::vector<void*> retired;  // outgrown workspace buffers, freed at shutdown
 };
 
 static DevState g_dev[kMaxDev];
@@ -79,23 +81,25 @@ bool pdl_enabled() {
     return v == 1;
 }
 
+// Grows slot k to at least `bytes`.  The old buffer may still be read by work
+// queued on any stream, so it is not freed here (that would need a device-wide
+// synchronisation in the middle of a call): it is retired and freed at
+// tensor_cuda_shutdown.  Growth is geometric, so the retired buffers total less
+// than the live one.
 static void* slot_get(DevState& s, int k, size_t bytes) {
     if (bytes == 0) bytes = 256;
     if (s.slot_bytes[k] >= bytes) return s.slot[k];
     size_t want = 1 << 20;
     while (want < bytes) want <<= 1;
-    if (s.slot[k]) {
-        cudaDeviceSynchronize();  // the old buffer may still be read by queued work
-        cudaFree(s.slot[k]);
-        s.slot[k] = nullptr;
-        s.slot_bytes[k] = 0;
-    }
-    if (cudaMalloc(&s.slot[k], want) != cudaSuccess) {
-        s.slot[k] = nullptr;
+    void* p = nullptr;
+    if (cudaMalloc(&p, want) != cudaSuccess) {
+        cudaGetLastError();
         return nullptr;
     }
+    if (s.slot[k]) s.retired.push_back(s.slot[k]);
+    s.slot[k] = p;
     s.slot_bytes[k] = want;
-    return s.slot[k];
+    return p;
 }
 
 int* device_error_word() {
@@ -266,11 +270,14 @@ extern "C" void tensor_cuda_shutdown(void) {
     DevState* s = state();
     if (!s || !s->init) return;
     cudaStreamSynchronize(s->stream);
+    cudaDeviceSynchronize();  // the workspaces may also serve voxq_* calls on other streams
     for (int k = 0; k < kSlots; k++) {
         if (s->slot[k]) cudaFree(s->slot[k]);
         s->slot[k] = nullptr;
         s->slot_bytes[k] = 0;
     }
+    for (void* p : s->retired) cudaFree(p);
+    s->retired.clear();
     if (s->h_in) cudaFreeHost(s->h_in);
     if (s->h_out) cudaFreeHost(s->h_out);
     s->h_in = s->h_out = nullptr;
@@ -483,15 +490,22 @@ extern "C" VoxCPMError tensor_matmul_nt_cuda(const Tensor* a, const Tensor* b, T
         VOXQ_CUDA_TRY(cudaMemcpyAsync(da, s->h_in, a_bytes, cudaMemcpyHostToDevice, st));
         d_a = da;
     }
-    // output
+    // output.  A host `out` of the quantized GEMV (M <= 8) is written by the
+    // kernel straight into the mapped pinned staging buffer (its epilogue uses
+    // plain stores), which saves the device -> host copy and its API call;
+    // every other host output goes through a device slot and one copy.
     const size_t o_bytes = (size_t)M * N * sizeof(float);
     float* d_o = out->data;
-    if (!out->is_cuda) {
+    auto qit = b->is_cuda && b->data ? g_qtab.find(b->data) : g_qtab.end();
+    const bool direct_out = !out->is_cuda && qit != g_qtab.end() && M <= 8;
+    if (direct_out) {
+        if (!pinned_get(&s->h_out, &s->h_out_bytes, o_bytes)) return VOXCPM_ERR_OOM;
+        d_o = (float*)s->h_out;
+    } else if (!out->is_cuda) {
         d_o = (float*)slot_get(*s, 1, o_bytes);
         if (!d_o) return VOXCPM_ERR_OOM;
     }
     // weight
-    auto qit = b->is_cuda && b->data ? g_qtab.find(b->data) : g_qtab.end();
     VoxCPMError e;
     if (qit != g_qtab.end()) {
         const QRec& q = qit->second;
@@ -518,7 +532,10 @@ extern "C" VoxCPMError tensor_matmul_nt_cuda(const Tensor* a, const Tensor* b, T
         e = dense_launch(d_a, M, K, d_w, b->is_fp16 ? 1 : 0, N, K, d_o, N, st);
     }
     if (e) return e;
-    if (!out->is_cuda) {
+    if (direct_out) {
+        VOXQ_CUDA_TRY(cudaStreamSynchronize(st));
+        memcpy(out->data, s->h_out, o_bytes);
+    } else if (!out->is_cuda) {
         lk.lock();
         if (!pinned_get(&s->h_out, &s->h_out_bytes, o_bytes)) return VOXCPM_ERR_OOM;
         VOXQ_CUDA_TRY(cudaMemcpyAsync(s->h_out, d_o, o_bytes, cudaMemcpyDeviceToHost, st));

@@ -1,0 +1,269 @@
+/*
+ * voxq_engine_run.c -- runs the unchanged voxcpm2-c engine (src/model.c
+ * voxcpm_create -> [voxcpm_to_cuda] -> voxcpm_generate, the flow of
+ * examples/tts_minimal.c and src/main.c) on a model file and reports what a
+ * synthesis run needs to be checked and measured: the latent of every patch,
+ * the time spent per stage and the real-time factor.
+ *
+ *   voxq_engine_run --model M.vxcpm [--patches N] [--tokens T] [--token-seed S]
+ *                   [--gpu] [--latents OUT.f32] [--ralm-max-seq L]
+ *   prints one JSON line.
+ *
+ * The engine's sources are compiled as they are.  The run is observed at the
+ * engine's own function boundaries, which the linker redirects here
+ * (-Wl,--wrap=NAME sends model.c's calls of NAME, defined in another object,
+ * to __wrap_NAME; each wrapper calls __real_NAME):
+ *   loc_dit_sample     copies each patch's latent [1, 64, 4] (the sampler's
+ *                      output, src/loc_dit.c:437) and times the stage;
+ *   tslm_forward, ralm_forward, loc_enc_forward, audio_vae_decode,
+ *   tensor_matmul_nt   time per stage (tensor_matmul_nt: every projection of
+ *                      every stage; in a VOXCPM_CUDA build it is the call
+ *                      into tensor_matmul_nt_cuda, src/tensor.c:629-640);
+ *   tokenizer_create_from_weights, tokenizer_encode
+ *                      the input: no tokenizer ships with a random-init
+ *                      model, so the run's text is T token ids drawn
+ *                      uniformly from the 73448-entry vocabulary with a
+ *                      seeded xorshift64 (a vocabulary of placeholder
+ *                      strings is built with tokenizer_create_bpe so the
+ *                      engine holds a real tokenizer object);
+ *   ralm_setup_cache   with --ralm-max-seq L, sets the RALM cache length to
+ *                      L before the cache is allocated.  voxcpm_generate fixes
+ *                      it at 2048 positions (src/model.c:709), which holds
+ *                      63 patches of a 64-token text; longer runs need more.
+ *                      Without the flag the engine's value stands.
+ */
+#define _POSIX_C_SOURCE 200809L
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+
+#include "model.h"
+#include "tensor.h"
+#include "tokenizer.h"
+#include "voxcpm.h"
+
+static double now(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec + ts.tv_nsec * 1e-9;
+}
+
+/* ---- run options and observations ---- */
+static int g_tokens = 64;
+static uint64_t g_token_seed = 1;
+static int g_ralm_max_seq = 0;
+static float* g_latents = NULL;
+static int g_latent_cap = 0, g_latent_n = 0;
+
+enum { ST_TSLM, ST_RALM, ST_DIT, ST_LOCENC, ST_VAE, ST_MATMUL, ST_N };
+static const char* k_stage[ST_N] = {"tslm_forward", "ralm_forward", "loc_dit_sample", "loc_enc_forward",
+                                   "audio_vae_decode", "tensor_matmul_nt"};
+static double g_stage_s[ST_N];
+static long g_stage_calls[ST_N];
+static int g_in_stage = -1;  /* the outermost stage in progress (matmul time is also split per stage) */
+static double g_matmul_in[ST_N];
+
+#define TIMED(stage, call)                                        \
+    do {                                                          \
+        const int outer = g_in_stage;                             \
+        if (outer < 0) g_in_stage = (stage);                      \
+        const double t0_ = now();                                 \
+        r = (call);                                               \
+        g_stage_s[stage] += now() - t0_;                          \
+        g_stage_calls[stage]++;                                   \
+        g_in_stage = outer;                                       \
+    } while (0)
+
+VoxCPMError __real_tslm_forward(TSLM* tslm, const Tensor* x, const Tensor* freqs_cis, Tensor* out);
+VoxCPMError __wrap_tslm_forward(TSLM* tslm, const Tensor* x, const Tensor* freqs_cis, Tensor* out) {
+    VoxCPMError r;
+    TIMED(ST_TSLM, __real_tslm_forward(tslm, x, freqs_cis, out));
+    return r;
+}
+
+VoxCPMError __real_ralm_forward(RALM* ralm, const Tensor* x, const Tensor* freqs_cis, Tensor* out);
+VoxCPMError __wrap_ralm_forward(RALM* ralm, const Tensor* x, const Tensor* freqs_cis, Tensor* out) {
+    VoxCPMError r;
+    TIMED(ST_RALM, __real_ralm_forward(ralm, x, freqs_cis, out));
+    return r;
+}
+
+VoxCPMError __real_loc_enc_forward(const LocEnc* enc, const Tensor* feats, Tensor* out);
+VoxCPMError __wrap_loc_enc_forward(const LocEnc* enc, const Tensor* feats, Tensor* out) {
+    VoxCPMError r;
+    TIMED(ST_LOCENC, __real_loc_enc_forward(enc, feats, out));
+    return r;
+}
+
+VoxCPMError __real_audio_vae_decode(const AudioVAE* vae, const Tensor* z, Tensor* out);
+VoxCPMError __wrap_audio_vae_decode(const AudioVAE* vae, const Tensor* z, Tensor* out) {
+    VoxCPMError r;
+    TIMED(ST_VAE, __real_audio_vae_decode(vae, z, out));
+    return r;
+}
+
+VoxCPMError __real_tensor_matmul_nt(const Tensor* a, const Tensor* b, Tensor* out);
+VoxCPMError __wrap_tensor_matmul_nt(const Tensor* a, const Tensor* b, Tensor* out) {
+    const double t0 = now();
+    VoxCPMError r = __real_tensor_matmul_nt(a, b, out);
+    const double dt = now() - t0;
+    g_stage_s[ST_MATMUL] += dt;
+    g_stage_calls[ST_MATMUL]++;
+    if (g_in_stage >= 0) g_matmul_in[g_in_stage] += dt;
+    return r;
+}
+
+VoxCPMError __real_loc_dit_sample(const LocDiT* dit, const Tensor* mu, const Tensor* cond, int n_timesteps,
+                                  float cfg_value, Tensor* out);
+VoxCPMError __wrap_loc_dit_sample(const LocDiT* dit, const Tensor* mu, const Tensor* cond, int n_timesteps,
+                                  float cfg_value, Tensor* out) {
+    VoxCPMError r;
+    TIMED(ST_DIT, __real_loc_dit_sample(dit, mu, cond, n_timesteps, cfg_value, out));
+    if (r == VOXCPM_SUCCESS && out && out->data && !out->is_cuda) {
+        const int n = (int)out->size;
+        if (g_latent_n + n > g_latent_cap) {
+            g_latent_cap = 2 * (g_latent_n + n);
+            g_latents = (float*)realloc(g_latents, (size_t)g_latent_cap * sizeof(float));
+            if (!g_latents) return VOXCPM_ERR_OOM;
+        }
+        memcpy(g_latents + g_latent_n, out->data, (size_t)n * sizeof(float));
+        g_latent_n += n;
+    }
+    return r;
+}
+
+VoxCPMError __real_ralm_setup_cache(RALM* ralm, int batch_size);
+VoxCPMError __wrap_ralm_setup_cache(RALM* ralm, int batch_size) {
+    if (ralm && g_ralm_max_seq > 0) ralm->max_seq_len = g_ralm_max_seq;
+    return __real_ralm_setup_cache(ralm, batch_size);
+}
+
+#define VOCAB 73448
+Tokenizer* __real_tokenizer_create_from_weights(const uint8_t* mmap_data, const WeightIndex* idx);
+Tokenizer* __wrap_tokenizer_create_from_weights(const uint8_t* mmap_data, const WeightIndex* idx) {
+    Tokenizer* t = __real_tokenizer_create_from_weights(mmap_data, idx);
+    if (t) return t;
+    static char store[VOCAB][12];
+    static const char* vocab[VOCAB];
+    for (int i = 0; i < VOCAB; i++) {
+        snprintf(store[i], sizeof store[i], "<%d>", i);
+        vocab[i] = store[i];
+    }
+    return tokenizer_create_bpe(vocab, VOCAB, 11);
+}
+
+int __real_tokenizer_encode(const Tokenizer* tok, const char* text, int32_t* out_tokens, int max_tokens);
+int __wrap_tokenizer_encode(const Tokenizer* tok, const char* text, int32_t* out_tokens, int max_tokens) {
+    (void)tok;
+    (void)text;
+    if (!out_tokens) return g_tokens;
+    if (max_tokens < g_tokens) return -VOXCPM_ERR_INTERNAL;
+    uint64_t s = g_token_seed ? g_token_seed : 1;  /* xorshift64 (src/tensor.c:339-345); 0 would stay 0 */
+    for (int i = 0; i < g_tokens; i++) {
+        s ^= s << 13;
+        s ^= s >> 7;
+        s ^= s << 17;
+        out_tokens[i] = (int32_t)(((unsigned __int128)s * VOCAB) >> 64);
+    }
+    return g_tokens;
+}
+
+int main(int argc, char** argv) {
+    const char* model_path = NULL;
+    const char* latents_path = NULL;
+    int patches = 4, gpu = 0;
+    for (int i = 1; i < argc; i++) {
+        const char* a = argv[i];
+        const char* v = i + 1 < argc ? argv[i + 1] : NULL;
+        if (!strcmp(a, "--model") && v) { model_path = v; i++; }
+        else if (!strcmp(a, "--patches") && v) { patches = atoi(v); i++; }
+        else if (!strcmp(a, "--tokens") && v) { g_tokens = atoi(v); i++; }
+        else if (!strcmp(a, "--token-seed") && v) { g_token_seed = strtoull(v, NULL, 10); i++; }
+        else if (!strcmp(a, "--latents") && v) { latents_path = v; i++; }
+        else if (!strcmp(a, "--ralm-max-seq") && v) { g_ralm_max_seq = atoi(v); i++; }
+        else if (!strcmp(a, "--gpu")) gpu = 1;
+        else {
+            fprintf(stderr, "usage: %s --model M.vxcpm [--patches N] [--tokens T] [--token-seed S] [--gpu] "
+                            "[--latents OUT.f32] [--ralm-max-seq L]\n", argv[0]);
+            return 2;
+        }
+    }
+    if (!model_path || patches < 1 || g_tokens < 1) return 2;
+
+    const double t_create = now();
+    VoxCPMModelConfig cfg = voxcpm_model_config_default();
+    cfg.model_path = model_path;
+    cfg.n_threads = 1;
+    cfg.use_gpu = gpu != 0;
+    VoxCPMError err = VOXCPM_SUCCESS;
+    VoxCPMModel* model = voxcpm_create(&cfg, &err);
+    if (!model) {
+        fprintf(stderr, "voxcpm_create failed: %s\n", voxcpm_error_string(err));
+        return 1;
+    }
+    const double create_s = now() - t_create;
+    double upload_s = 0;
+    if (gpu) {
+        const double t0 = now();
+        err = voxcpm_to_cuda(model);
+        upload_s = now() - t0;
+        if (err != VOXCPM_SUCCESS) {
+            fprintf(stderr, "voxcpm_to_cuda failed: %s\n", voxcpm_error_string(err));
+            voxcpm_free(model);
+            return 1;
+        }
+    }
+
+    VoxCPMGenConfig gen = voxcpm_gen_config_default();
+    gen.text = "synthetic token ids";
+    gen.cfg_value = 2.0f;
+    gen.inference_timesteps = 10;
+    gen.max_new_tokens = 4 * patches;
+    VoxCPMAudio audio;
+    memset(&audio, 0, sizeof(audio));
+    memset(g_stage_s, 0, sizeof(g_stage_s));
+    memset(g_stage_calls, 0, sizeof(g_stage_calls));
+    memset(g_matmul_in, 0, sizeof(g_matmul_in));
+    const double t0 = now();
+    err = voxcpm_generate(model, &gen, &audio);
+    const double gen_s = now() - t0;
+    if (err != VOXCPM_SUCCESS) {
+        fprintf(stderr, "voxcpm_generate failed: %s\n", voxcpm_error_string(err));
+        voxcpm_free(model);
+        return 1;
+    }
+    const double audio_s = audio.sample_rate > 0 ? (double)audio.num_samples / audio.sample_rate : 0.0;
+    double asum = 0;
+    for (int i = 0; i < audio.num_samples; i++) asum += audio.samples[i] < 0 ? -audio.samples[i] : audio.samples[i];
+
+    if (latents_path) {
+        FILE* f = fopen(latents_path, "wb");
+        if (!f || fwrite(g_latents, sizeof(float), (size_t)g_latent_n, f) != (size_t)g_latent_n || fclose(f)) {
+            fprintf(stderr, "cannot write %s\n", latents_path);
+            return 1;
+        }
+    }
+    printf("{\"build\": \"%s\", \"patches\": %d, \"tokens\": %d, \"token_seed\": %llu, \"latent_floats\": %d, "
+           "\"samples\": %d, \"sample_rate\": %d, \"audio_s\": %.6f, \"generate_s\": %.4f, \"rtf\": %.5f, "
+           "\"create_s\": %.3f, \"upload_s\": %.3f, \"audio_abs_mean\": %.9g, \"ralm_max_seq\": %d, \"stages\": {",
+#ifdef VOXCPM_CUDA
+           "gpu",
+#else
+           "cpu",
+#endif
+           patches, g_tokens, (unsigned long long)g_token_seed, g_latent_n, audio.num_samples, audio.sample_rate,
+           audio_s, gen_s, audio_s > 0 ? gen_s / audio_s : 0.0, create_s, upload_s,
+           audio.num_samples ? asum / audio.num_samples : 0.0, g_ralm_max_seq);
+    for (int s = 0; s < ST_N; s++) {
+        printf("%s\"%s\": {\"s\": %.5f, \"calls\": %ld", s ? ", " : "", k_stage[s], g_stage_s[s], g_stage_calls[s]);
+        if (s != ST_MATMUL) printf(", \"matmul_s\": %.5f", g_matmul_in[s]);  /* tensor_matmul_nt time inside */
+        printf("}");
+    }
+    printf("}}\n");
+    voxcpm_audio_free(&audio);
+    voxcpm_free(model);
+    free(g_latents);
+    return 0;
+}
