@@ -5,7 +5,9 @@ tests run again in a child process with the switch set:
   feeding the tensor cores) in place of the default two-phase path;
 - VOXQ_GEMM_SPLIT forces the split-K factor: 1 (no split) and the largest the
   K range allows, on the whole config-3 sweep.  Every case must meet the same
-  tolerance against the CPU checker whatever the split."""
+  tolerance against the CPU checker whatever the split;
+- VOXQ_GEMM_CLUSTER=0 sums the K-split partials of batches of up to 256 rows
+  through global memory and a reduction kernel instead of inside a cluster."""
 from __future__ import annotations
 
 import os
@@ -35,3 +37,12 @@ def test_c3_sweep_with_forced_split_in_child_process(split):
                        env=env, cwd=os.path.dirname(HERE), capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
     assert "16 passed" in r.stdout
+
+
+def test_gemm_without_cluster_split_in_child_process():
+    env = dict(os.environ, VOXQ_GEMM_CLUSTER="0")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider",
+                        os.path.join(HERE, "test_gpu_matmul.py"), "-k", "gemm or epilogues"],
+                       env=env, cwd=os.path.dirname(HERE), capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+    assert " passed" in r.stdout

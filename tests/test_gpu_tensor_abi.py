@@ -159,3 +159,23 @@ def test_upload_weight_helper(abi):
     assert L.tensor_cuda_upload_weight(p) == 0 and w.contents.is_cuda
     assert L.tensor_cuda_upload_weight(None) == 0
     voxq.free_tensor(w)
+
+
+@pytest.mark.parametrize("abi", ["q8"], indirect=True)
+def test_fp16_uploads_land_before_quantization(abi):
+    """Many fp16 host weights of the engine's shapes, uploaded back to back by
+    tensor_to_cuda (VOXCPM_QUANT=q8): each must come back from tensor_to_cpu as
+    exactly its Q8 dequantization -- every row, the last ones included (the
+    quantizer must not read the upload before its copy has landed)."""
+    rs = np.random.RandomState(11)
+    shapes = [(2048, 2048), (256, 2048), (256, 2048), (6144, 2048), (2048, 6144), (1024, 64), (64, 1024)] * 3
+    for i, (N, K) in enumerate(shapes):
+        w = (rs.standard_normal((N, K)) * 0.02).astype(np.float16)
+        wt = voxq.host_tensor(w, fp16=True)
+        assert L.tensor_to_cuda(wt) == 0 and wt.contents.is_cuda
+        want = O.dequantize(O.quantize(w.astype(np.float32), voxq.Q8), N * K, voxq.Q8).reshape(N, K)
+        assert L.tensor_to_cpu(wt) == 0
+        back = voxq.host_tensor_view(wt)
+        bad = np.where((back.view(np.uint32) != want.view(np.uint32)).any(1))[0]
+        assert bad.size == 0, f"upload {i} ({N}x{K}): rows {bad[:8].tolist()} differ"
+        voxq.free_tensor(wt)

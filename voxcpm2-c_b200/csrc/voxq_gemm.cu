@@ -200,6 +200,29 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Thread-block cluster helpers: every thread of every CTA of the cluster takes
+// part in a cluster barrier; shared memory of CTA `rank` is read through its
+// shared::cluster address (mapa).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a)
+                 : "memory");
+    return v;
+}
+
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
 struct GemmArgs {
@@ -217,6 +240,7 @@ struct GemmArgs {
     int64_t ldo, ldr, ldg;
     int M, N, K;
     int S, KUs;             // K splits per tile, operand stages per split
+    int cluster;            // S > 1 in one cluster per tile: partials summed in shared memory
     int q8_signed;
     int* err;
 };
@@ -393,6 +417,100 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& g, uint32_t tmem, 
 #undef VOXQ_EPI_FETCH
 }
 
+// Split K inside one thread-block cluster (the fused kernel with g.cluster):
+// the S CTAs of a cluster are the S K-splits of one tile, one unit each, and
+// rank r finishes tile columns (activation rows) [r RB, (r+1) RB), RB = BN / S.
+//   1. the epilogue warps park the raw accumulator in this CTA's shared memory
+//      as P[tile column c][weight row n] (over the operand rings, which the
+//      finished MMAs no longer read);
+//   2. cluster barrier: every P of the cluster is complete;
+//   3. every thread of the CTA pulls, for its items (tile column c of this
+//      rank, 4 consecutive weight rows), the S partials from the S CTAs'
+//      P through distributed shared memory -- a warp reads 512 contiguous
+//      bytes per load, and each thread keeps several items' loads in flight --
+//      sums them in rank order (the order of splitk_reduce_kernel, so the bits
+//      equal the two-kernel split), applies the epilogue and stores the output;
+//   4. cluster barrier: every P stays alive until all ranks have read it.
+// No partial touches global memory and no reduction kernel runs.
+
+template <int BN, int TC>
+__device__ __forceinline__ void cluster_park_partials(const GemmArgs& g, uint32_t tmem, float* P, int e, int q,
+                                                      int lane) {
+    constexpr int CWID = (BN / kEpiParts >= 16) ? BN / kEpiParts : BN;
+    const int cb = (e / 4) * CWID, ce = min(BN, cb + CWID);
+    const uint32_t tacc = tmem + ((uint32_t)(q * 32) << 16);
+    float* pc = P + q * 32 + lane;
+#pragma unroll 1
+    for (int c0 = cb; c0 < ce; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tacc + (uint32_t)c0, v);
+#pragma unroll
+        for (int i = 0; i < 16; i++) pc[(c0 + i) * kBM] = __uint_as_float(v[i]);
+    }
+    tc_fence_before();
+}
+
+// Values step 3 needs, loaded before the barrier so that no global round trip
+// follows it: thread t keeps weight rows n .. n+3 (n = 4 (t % 32), kThreads is a
+// multiple of 32) -- their scale and bias -- and the tile's activation row
+// scales are staged in shared memory (`am`, RB floats).
+struct ReducePrefetch {
+    float rinv[4], bias[4];
+};
+
+template <int BN>
+__device__ __forceinline__ void cluster_reduce_prefetch(const GemmArgs& g, ReducePrefetch& pf, float* am) {
+    const int S = g.S, RB = BN / S, mt = (g.M + BN - 1) / BN;
+    const int t = blockIdx.x / S, me = (int)cluster_rank();
+    const int m0 = (t % mt) * BN + me * RB, n = (t / mt) * kBM + 4 * (threadIdx.x & 31);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        pf.rinv[i] = n + i < g.N ? 1.0f / __ldg(g.rowmul + n + i) : 0.0f;
+        pf.bias[i] = (n + i < g.N && g.bias) ? __ldg(g.bias + n + i) : 0.0f;
+    }
+    if ((int)threadIdx.x < RB) am[threadIdx.x] = m0 + (int)threadIdx.x < g.M ? __ldg(g.ainv + m0 + threadIdx.x) : 0.0f;
+}
+
+template <int BN>
+__device__ __forceinline__ void cluster_reduce_store(const GemmArgs& g, const float* P, const ReducePrefetch& pf,
+                                                     const float* am) {
+    const int S = g.S, RB = BN / S, mt = (g.M + BN - 1) / BN;
+    const int t = blockIdx.x / S, me = (int)cluster_rank();
+    const int m0 = (t % mt) * BN + me * RB, j = threadIdx.x & 31, n = (t / mt) * kBM + 4 * j;
+    constexpr int kRowsPerPass = kThreads / 32;  // tile columns the CTA covers per item index
+    const uint32_t pbase = smem_u32(P) + 16u * (uint32_t)j;
+    uint32_t rbase[8];
+#pragma unroll
+    for (int sp = 0; sp < 8; sp++) rbase[sp] = sp < S ? dsmem_addr(pbase, (uint32_t)sp) : 0u;
+#pragma unroll 1
+    for (int c = me * RB + (int)(threadIdx.x >> 5); c < (me + 1) * RB; c += kRowsPerPass) {
+        // all S partials of the item in flight before the first add
+        const uint32_t off = (uint32_t)(c * kBM) * 4u;
+        float4 x[8];
+#pragma unroll
+        for (int sp = 0; sp < 8; sp++)
+            if (sp < S) x[sp] = ld_dsmem_f4(rbase[sp] + off);
+        float4 acc = x[0];
+#pragma unroll
+        for (int sp = 1; sp < 8; sp++)
+            if (sp < S) {
+                acc.x += x[sp].x;
+                acc.y += x[sp].y;
+                acc.z += x[sp].z;
+                acc.w += x[sp].w;
+            }
+        const int m = m0 - me * RB + c;
+        if (m < g.M) {
+            const float a = am[c - me * RB];
+            const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+            float* o = g.out + (int64_t)m * g.ldo + n;
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                if (n + i < g.N) o[i] = epi_value(g, a4[i], a * pf.rinv[i], pf.bias[i], m, n + i);
+        }
+    }
+}
+
 template <int QT, int BN, bool SIGNED>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmArgs g) {
     constexpr int RK = (QT == VOXQ_Q4) ? 4 : 2;  // operand stages per raw stage
@@ -438,6 +556,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             mbar_init(&acc_empty[i], kEpiWarps);
         }
         mbar_fence_init();
+        // Weights never depend on earlier kernels: the first raw stages of this
+        // CTA's first unit are requested right away, before tensor memory is
+        // allocated and the CTA synchronises (the raw producer skips them).
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&g.tm_codes)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&g.tm_tr)) : "memory");
+        if ((int)blockIdx.x < units) {
+            const int w = blockIdx.x, t = w / S, u0 = (w % S) * KUs, u1 = min(KU, u0 + KUs);
+            const int n0 = (t / mt) * kBM;
+            int c = 0;
+            for (int u = u0; u < u1 && c < kRaw; u += RK, c++) {
+                mbar_arrive_expect_tx(&full_raw[c], kRawStage);
+                uint8_t* rs = raw + c * kRawStage;
+                tma_load_2d(rs, &g.tm_codes, (u / RK) * kRawRow, n0, &full_raw[c]);
+                tma_load_2d(rs + kRawCodes, &g.tm_tr, (u / RK) * kRawTrRow, n0, &full_raw[c]);
+            }
+        }
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
@@ -458,15 +592,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         // Weights never depend on the predecessor kernel, so this warp streams from
         // the start.  It has a ring of its own, so it runs ahead of the tensor core
         // by the full raw ring, independently of the activation ring.
-        if (lane == 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&g.tm_codes)) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&g.tm_tr)) : "memory");
-        }
         Ring rr;
+        int early = 0;  // raw stages thread 0 already requested for the first unit
+        if ((int)blockIdx.x < units) {
+            const int u0 = (blockIdx.x % S) * KUs, u1 = min(KU, u0 + KUs);
+            early = min(kRaw, (u1 - u0 + RK - 1) / RK);
+        }
         for (int w = blockIdx.x; w < units; w += gridDim.x) {
             const int t = w / S, u0 = (w % S) * KUs, u1 = min(KU, u0 + KUs);
             const int n0 = (t / mt) * kBM;
             for (int u = u0; u < u1; u += RK) {  // u0 is a multiple of RK
+                if ((int)rr.c < early) {
+                    rr.c++;
+                    continue;
+                }
                 const int s = rr.slot<kRaw>();
                 if (rr.c >= kRaw) mbar_wait_bounded(&empty_raw[s], rr.phase<kRaw>() ^ 1, VOXQ_DEVERR_WAIT_EMPTY, g.err);
                 if (lane == 0) {
@@ -614,8 +753,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
     } else if (warp < 2 + kDeqWarps + kEpiWarps) {
         // ---------------- epilogue ----------------
-        epilogue_role<BN, TC, 1, 2, kEpiParts>(g, tmem, acc_full, acc_empty, &ainv_s[0][0][0], units, mt, S,
-                                               warp - (2 + kDeqWarps), warp & 3, lane);
+        if (g.cluster) {
+            mbar_wait_sleepy(&acc_full[0], 0, VOXQ_DEVERR_WAIT_MMA, g.err);  // the one unit's accumulator
+            tc_fence_after();
+        } else {
+            epilogue_role<BN, TC, 1, 2, kEpiParts>(g, tmem, acc_full, acc_empty, &ainv_s[0][0][0], units, mt, S,
+                                                   warp - (2 + kDeqWarps), warp & 3, lane);
+        }
+    }
+    if (g.cluster) {
+        // split K inside the cluster (see cluster_park_partials): every thread
+        // of every CTA takes both barriers and reduces
+        float* P = reinterpret_cast<float*>(base);  // over the operand rings
+        float* am_s = &ainv_s[0][0][0];             // the epilogue role's staging, unused in cluster mode
+        if (warp >= 2 + kDeqWarps && warp < 2 + kDeqWarps + kEpiWarps)
+            cluster_park_partials<BN, TC>(g, tmem, P, warp - (2 + kDeqWarps), warp & 3, lane);
+        pdl_wait();  // the prepass's row scales; residual / gate / output of earlier work
+        ReducePrefetch pf;
+        cluster_reduce_prefetch<BN>(g, pf, am_s);
+        cluster_sync_all();
+        pdl_launch_dependents();
+        cluster_reduce_store<BN>(g, P, pf, am_s);
+        cluster_sync_all();
     }
     // dequant / epilogue roles touch global outputs only after the wait below
     tc_fence_before();
@@ -913,6 +1072,7 @@ struct GemmPlan {
     int bn, S, KUs, tiles;
     bool two_phase;  // dequantize the weight once (prep_f16_kernel), then gemm_f16_kernel
     int nt;          // two-phase: 128-row weight sub-tiles per tile (1 or 2)
+    bool cluster;    // fused kernel, the S K-splits of a tile in one cluster (partials in shared memory)
 };
 
 static int env_int(const char* name) {
@@ -920,17 +1080,27 @@ static int env_int(const char* name) {
     return e ? atoi(e) : 0;
 }
 
+static int fused_occupancy(int qt, int bn);
+
 static GemmPlan plan_gemm(int M, int N, int K, int qt) {
     static const int forced_bn = env_int("VOXQ_GEMM_BN"), forced_s = env_int("VOXQ_GEMM_SPLIT");
-    static const int forced_path = env_int("VOXQ_GEMM_TWO_PHASE");  // -1: the fused kernel
+    // VOXQ_GEMM_TWO_PHASE: 1 two-phase at every M, -1 the fused kernel at every M,
+    // unset: fused (cluster split K) for M <= 256, two-phase above
+    static const int forced_path = env_int("VOXQ_GEMM_TWO_PHASE");
+    static const int no_cluster = getenv("VOXQ_GEMM_CLUSTER") && env_int("VOXQ_GEMM_CLUSTER") == 0;
     GemmPlan p;
-    // Dequantizing the weight once per call (about 2.6 B/weight of extra traffic)
-    // and running a plain TMA -> tcgen05 GEMM beats the fused kernel's dequant
-    // pipeline, which repeats the dequant for every activation tile, at every
-    // measured size: config-3 sweep on B200, M = 16 .. 2048, e.g. M = 256,
-    // N = 4096 15.3 vs 17.3 us (Q8) and 15.1 vs 18.0 us (Q4); the one exception,
-    // Q8 M = 64 N = 1024, is 3 % slower.  The fused kernel stays selectable.
-    p.two_phase = forced_path >= 0;
+    p.cluster = false;
+    // Batches above 128 rows: dequantizing the weight once per call (about
+    // 2.6 B/weight of extra traffic) and running a plain TMA -> tcgen05 GEMM
+    // beats the fused kernel's dequant pipeline, which repeats the dequant for
+    // every activation tile.  Batches of up to 128 rows fit one activation tile:
+    // the fused kernel dequantizes each weight byte exactly once and keeps its
+    // K-split partials on chip (cluster), so neither the fp16 weight image nor
+    // split-K partials reach HBM.  Measured on the config-3 shapes (CUDA-graph
+    // replay, B200): M = 16 / 64 are 0.4 - 1.4 us faster than the two-phase
+    // path; at M = 256 the cluster exchange of 128 KB of partials per CTA
+    // (distributed shared memory moves ~20 GB/s per SM) makes it slower.
+    p.two_phase = forced_path > 0 || (forced_path == 0 && M > 128);
     if (forced_bn == 16 || forced_bn == 32 || forced_bn == 64 || forced_bn == 128 || forced_bn == 256) {
         p.bn = forced_bn;
     } else {
@@ -940,6 +1110,25 @@ static GemmPlan plan_gemm(int M, int N, int K, int qt) {
     const int KU = K / kBK, RK = (qt == VOXQ_Q4) ? 4 : 2;
     const int sms = device_sm_count();
     p.nt = 1;
+    if (!p.two_phase && M <= p.bn && !no_cluster) {
+        // one activation tile: cluster split K over up to 8 CTAs per weight tile,
+        // as many as the co-resident CTAs allow
+        p.tiles = (N + kBM - 1) / kBM;
+        const int cap = sms * fused_occupancy(qt, p.bn);
+        const int smax = min(8, KU / RK > 1 ? KU / RK : 1);
+        int s = 1;
+        if (forced_s > 0) {
+            while (2 * s <= min(forced_s, smax)) s *= 2;
+        } else {
+            while (2 * s <= smax && p.tiles * 2 * s <= cap) s *= 2;
+        }
+        int kus = (KU + s - 1) / s;
+        kus = (kus + RK - 1) / RK * RK;
+        p.S = (KU + kus - 1) / kus;
+        p.KUs = kus;
+        p.cluster = p.S > 1 && p.bn >= p.S;
+        if (p.cluster || p.S == 1) return p;
+    }
     if (p.two_phase && p.bn == 256) {
         // 256-row tiles when they still cover most SMs (no split K with them)
         const int tiles2 = ((M + p.bn - 1) / p.bn) * ((N + 2 * kBM - 1) / (2 * kBM));
@@ -975,7 +1164,7 @@ static GemmPlan plan_gemm(int M, int N, int K, int qt) {
 }
 
 static size_t part_bytes(const GemmPlan& p) {
-    return p.S > 1 ? align256((size_t)p.S * p.tiles * p.bn * kBM * 4) : 0;
+    return (p.S > 1 && !p.cluster) ? align256((size_t)p.S * p.tiles * p.bn * kBM * 4) : 0;
 }
 
 static size_t w16_bytes(const GemmPlan& p, int N, int K) {
@@ -992,32 +1181,63 @@ size_t gemm_workspace_bytes(int M, int N, int K, int qtype, bool swiglu) {
 }
 
 template <int QT, int BN, bool SIGNED>
+struct FusedKernel {
+    static constexpr int kB = BN * kBK * 2;
+    static constexpr int smem = 1024 + kOpsA * kA16 + ops_b(BN) * kB + raw_stages(BN) * kRawStage;
+    static constexpr int TC = BN < 32 ? 32 : BN;
+    // co-resident CTAs per SM (shared memory and tensor memory), set once
+    static int occupancy() {
+        static int occ = 1;
+        static std::once_flag once;
+        std::call_once(once, [] {
+            auto kern = gemm_kernel<QT, BN, SIGNED>;
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem);
+            const int tmem_cap = 512 / (2 * TC);  // co-resident CTAs must fit tensor memory
+            if (occ > tmem_cap) occ = tmem_cap;
+            if (occ < 1) occ = 1;
+        });
+        return occ;
+    }
+};
+
+static int fused_occupancy(int qt, int bn) {
+#define VOXQ_OCC(B) \
+    case B: return qt == VOXQ_Q4 ? FusedKernel<VOXQ_Q4, B, false>::occupancy() : FusedKernel<VOXQ_Q8, B, false>::occupancy();
+    switch (bn) {
+        VOXQ_OCC(16)
+        VOXQ_OCC(32)
+        VOXQ_OCC(64)
+        VOXQ_OCC(128)
+        default: return qt == VOXQ_Q4 ? FusedKernel<VOXQ_Q4, 256, false>::occupancy()
+                                      : FusedKernel<VOXQ_Q8, 256, false>::occupancy();
+    }
+#undef VOXQ_OCC
+}
+
+template <int QT, int BN, bool SIGNED>
 static VoxCPMError launch_gemm_t(const GemmArgs& a, cudaStream_t st) {
-    constexpr int kB = BN * kBK * 2;
-    constexpr int smem = 1024 + kOpsA * kA16 + ops_b(BN) * kB + raw_stages(BN) * kRawStage;
-    constexpr int TC = BN < 32 ? 32 : BN;
+    using FK = FusedKernel<QT, BN, SIGNED>;
+    static_assert(kOpsA * kA16 + ops_b(BN) * FK::kB >= BN * kBM * 4, "cluster partials must fit the operand rings");
     auto kern = gemm_kernel<QT, BN, SIGNED>;
-    static int occ = 1;
-    static std::once_flag once;
-    std::call_once(once, [&] {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem);
-        const int tmem_cap = 512 / (2 * TC);  // co-resident CTAs must fit tensor memory
-        if (occ > tmem_cap) occ = tmem_cap;
-        if (occ < 1) occ = 1;
-    });
+    const int occ = FK::occupancy();
     const int units = ((a.M + BN - 1) / BN) * ((a.N + kBM - 1) / kBM) * a.S;
     const int cap = device_sm_count() * occ;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(units < cap ? units : cap);
+    // cluster split K: exactly one unit per CTA, S consecutive CTAs per cluster
+    cfg.gridDim = dim3(a.cluster ? units : (units < cap ? units : cap));
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = FK::smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = a.cluster ? (unsigned)a.S : 1u;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = a.cluster ? 2 : 1;
     VOXQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
     return VOXCPM_SUCCESS;
 }
@@ -1139,13 +1359,14 @@ static VoxCPMError gemm_one(const GemmPlan& pl, const float* ainv, const uint8_t
     ga.K = K;
     ga.S = pl.S;
     ga.KUs = pl.KUs;
+    ga.cluster = pl.cluster ? 1 : 0;
     ga.q8_signed = w->q8_signed;
     ga.err = device_error_word();
     const int bn = pl.bn;
     VoxCPMError e = pl.two_phase ? launch_f16(ga, bn, pl.nt, st)
                     : qt == VOXQ_Q4 ? launch_bn<VOXQ_Q4>(ga, bn, false, st)
                                     : launch_bn<VOXQ_Q8>(ga, bn, w->q8_signed != 0, st);
-    if (e || pl.S == 1) return e;
+    if (e || pl.S == 1 || pl.cluster) return e;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     const int64_t threads = (int64_t)pl.tiles * bn * 32;

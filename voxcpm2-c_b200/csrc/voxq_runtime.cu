@@ -335,12 +335,16 @@ extern "C" VoxCPMError tensor_to_cuda(Tensor* t) {
                 d_h = nullptr;
                 return fail(VOXCPM_ERR_OOM, ce, "cudaMalloc");
             }
-            if ((ce = cudaMemcpy(d_h, t->data_fp16, n * 2, cudaMemcpyHostToDevice)) != cudaSuccess)
+            // on the library stream: the kernels below read d_h there (a synchronous copy
+            // from pageable memory may return before its DMA lands, and the library's
+            // non-blocking stream is not ordered behind the legacy stream)
+            if ((ce = cudaMemcpyAsync(d_h, t->data_fp16, n * 2, cudaMemcpyHostToDevice, s->stream)) != cudaSuccess)
                 return fail(VOXCPM_ERR_INTERNAL, ce, "cudaMemcpy");
             // exact widening, then the quantizer sees the same floats quantize.py would
             VoxCPMError e = widen_fp16(d_h, d_f32, n, s->stream);
             if (e) return fail(e, cudaSuccess, "");
-        } else if ((ce = cudaMemcpy(d_f32, t->data, n * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess) {
+        } else if ((ce = cudaMemcpyAsync(d_f32, t->data, n * sizeof(float), cudaMemcpyHostToDevice, s->stream)) !=
+                   cudaSuccess) {
             return fail(VOXCPM_ERR_INTERNAL, ce, "cudaMemcpy");
         }
         uint8_t* codes = (uint8_t*)base;
@@ -371,7 +375,8 @@ extern "C" VoxCPMError tensor_to_cuda(Tensor* t) {
         const size_t bytes = t->size * sizeof(uint16_t);
         uint16_t* d = nullptr;
         VOXQ_CUDA_TRY(cudaMalloc(&d, bytes));
-        VOXQ_CUDA_TRY(cudaMemcpy(d, t->data_fp16, bytes, cudaMemcpyHostToDevice));
+        VOXQ_CUDA_TRY(cudaMemcpyAsync(d, t->data_fp16, bytes, cudaMemcpyHostToDevice, s->stream));
+        VOXQ_CUDA_TRY(cudaStreamSynchronize(s->stream));  // before the host buffer is freed
         free(t->data_fp16);
         t->data_fp16 = d;
         t->is_cuda = true;
@@ -380,7 +385,8 @@ extern "C" VoxCPMError tensor_to_cuda(Tensor* t) {
     if (!t->data) return VOXCPM_SUCCESS;
     float* d = nullptr;
     VOXQ_CUDA_TRY(cudaMalloc(&d, t->size * sizeof(float)));
-    VOXQ_CUDA_TRY(cudaMemcpy(d, t->data, t->size * sizeof(float), cudaMemcpyHostToDevice));
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(d, t->data, t->size * sizeof(float), cudaMemcpyHostToDevice, s->stream));
+    VOXQ_CUDA_TRY(cudaStreamSynchronize(s->stream));  // before the host buffer is freed
     free(t->data);
     t->data = d;
     t->is_cuda = true;

@@ -104,12 +104,51 @@ VoxCPMError __wrap_audio_vae_decode(const AudioVAE* vae, const Tensor* z, Tensor
     return r;
 }
 
+/* VOXQ_ENGINE_MATMUL_LOG=path: one line per tensor_matmul_nt call (shape,
+ * where the operands live, and sums of the host output), so two builds of the
+ * engine can be compared call by call. */
+static FILE* g_mm_log = NULL;
+static const char* g_dump_calls = NULL;  /* comma-separated call indices */
+static const char* g_dump_dir = NULL;
+static int dump_wanted(long i) {
+    for (const char* p = g_dump_calls; p && *p;) {
+        if (atol(p) == i) return 1;
+        p = strchr(p, ',');
+        if (p) p++;
+    }
+    return 0;
+}
+
 VoxCPMError __real_tensor_matmul_nt(const Tensor* a, const Tensor* b, Tensor* out);
 VoxCPMError __wrap_tensor_matmul_nt(const Tensor* a, const Tensor* b, Tensor* out) {
     const double t0 = now();
     VoxCPMError r = __real_tensor_matmul_nt(a, b, out);
     const double dt = now() - t0;
     g_stage_s[ST_MATMUL] += dt;
+    if (g_mm_log && out && !out->is_cuda && out->data) {
+        double sum = 0, asum = 0;
+        for (size_t i = 0; i < out->size; i++) {
+            sum += out->data[i];
+            asum += out->data[i] < 0 ? -out->data[i] : out->data[i];
+        }
+        fprintf(g_mm_log, "%ld %d %d %d stage=%d a_cuda=%d b_cuda=%d b_fp16=%d r=%d sum=%.9g asum=%.9g v0=%.9g v1=%.9g\n",
+                g_stage_calls[ST_MATMUL], a->shape[0], b->shape[0], a->shape[1], g_in_stage, (int)a->is_cuda,
+                (int)b->is_cuda, (int)b->is_fp16, (int)r, sum, asum, out->size > 0 ? out->data[0] : 0.0,
+                out->size > 1 ? out->data[out->size - 1] : 0.0);
+    }
+    if (g_dump_dir && dump_wanted(g_stage_calls[ST_MATMUL])) {
+        /* VOXQ_ENGINE_DUMP_CALL=i,j,... with VOXQ_ENGINE_DUMP_DIR: the host
+         * activation and output of those calls, as raw float32 */
+        char path[1024];
+        snprintf(path, sizeof path, "%s/call%ld_a.f32", g_dump_dir, g_stage_calls[ST_MATMUL]);
+        FILE* f = fopen(path, "wb");
+        if (f && !a->is_cuda) fwrite(a->data, sizeof(float), a->size, f);
+        if (f) fclose(f);
+        snprintf(path, sizeof path, "%s/call%ld_out.f32", g_dump_dir, g_stage_calls[ST_MATMUL]);
+        f = fopen(path, "wb");
+        if (f && !out->is_cuda) fwrite(out->data, sizeof(float), out->size, f);
+        if (f) fclose(f);
+    }
     g_stage_calls[ST_MATMUL]++;
     if (g_in_stage >= 0) g_matmul_in[g_in_stage] += dt;
     return r;
@@ -191,6 +230,10 @@ int main(int argc, char** argv) {
         }
     }
     if (!model_path || patches < 1 || g_tokens < 1) return 2;
+    const char* mm_log = getenv("VOXQ_ENGINE_MATMUL_LOG");
+    if (mm_log && *mm_log) g_mm_log = fopen(mm_log, "w");
+    g_dump_calls = getenv("VOXQ_ENGINE_DUMP_CALL");
+    g_dump_dir = getenv("VOXQ_ENGINE_DUMP_DIR");
 
     const double t_create = now();
     VoxCPMModelConfig cfg = voxcpm_model_config_default();
@@ -265,5 +308,6 @@ int main(int argc, char** argv) {
     voxcpm_audio_free(&audio);
     voxcpm_free(model);
     free(g_latents);
+    if (g_mm_log) fclose(g_mm_log);
     return 0;
 }
