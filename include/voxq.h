@@ -268,6 +268,46 @@ typedef struct {
 
 VOXQ_API VoxCPMError voxq_gemv_batch(const voxq_gemv_item* items, int count, void* stream);
 
+/* ---- AudioVAE convolutions ---------------------------------------------
+ * The reference decodes audio on the host even in its GPU build: every
+ * AudioVAE weight stays on the CPU (src/model.c:554-556) and the decoder's
+ * 1-D convolutions run in src/nn.c:765-931.  These compute the same two
+ * functions on the device, in fp32, with the engine's own descriptors (the
+ * layouts of Conv1D and Conv1DTranspose, include/nn.h:198-229), so an engine
+ * can route conv1d_forward / conv1d_transpose_forward here:
+ *   conv1d:     out[n,o,t] = b[o] + sum over c in o's group, k of
+ *               w[o][c - group start][k] * x[n][c][t*stride + k - padding]
+ *   transposed: out[n,o,t] = b[o] + sum over c, k, s with s*stride + k - padding = t
+ *               of w[c][o][k] * x[n][c][s]
+ * x [batch, in_channels, time] and out [batch, out_channels, out_time] are
+ * fp32, host or device (a host out is valid on return).  A host weight or
+ * bias is uploaded on its first use and kept, keyed by its pointer, size and a
+ * fingerprint of 64 sampled values (so a buffer freed and reallocated at the
+ * same address is uploaded again), until voxq_conv_cache_clear or
+ * tensor_cuda_shutdown; a cached host weight must not be changed in place
+ * (the AudioVAE's effective weights never are).  Same shape checks and error
+ * codes as nn.c; not initialised -> VOXCPM_ERR_CUDA_NOT_FOUND (the caller then
+ * uses its CPU loop). */
+typedef struct {
+    Tensor* weight;  /* [out_channels, in_channels / groups, kernel_size] */
+    Tensor* bias;    /* [out_channels] or NULL */
+    int in_channels, out_channels, kernel_size, stride, padding, groups;
+} voxq_conv1d_desc;
+typedef struct {
+    Tensor* weight;  /* [in_channels, out_channels, kernel_size] */
+    Tensor* bias;    /* [out_channels] or NULL */
+    int in_channels, out_channels, kernel_size, stride, padding;
+} voxq_conv1d_transpose_desc;
+
+/* src/nn.c:765-834 (conv1d_forward). */
+VOXQ_API VoxCPMError voxq_conv1d_forward(const voxq_conv1d_desc* conv, const Tensor* x, Tensor* out);
+/* src/nn.c:864-931 (conv1d_transpose_forward). */
+VOXQ_API VoxCPMError voxq_conv1d_transpose_forward(const voxq_conv1d_transpose_desc* conv, const Tensor* x,
+                                                   Tensor* out);
+/* Drops the convolutions' cached device copies of host weights (no
+ * counterpart in the reference). */
+VOXQ_API void voxq_conv_cache_clear(void);
+
 /* ---- quantize.py weight containers (VXCPM2) ---------------------------
  * Reads the container written by the reference's quantizer
  * (scripts/quantize.py:110-312): a 256-byte header, the layer-group offset

@@ -47,6 +47,9 @@ def lib():
         L.oracle_matmul_nt.argtypes = [fp, fp, fp, C.c_int, C.c_int, C.c_int]
         L.oracle_matmul_nt_f64.argtypes = [fp, fp, dp, dp, C.c_int, C.c_int, C.c_int]
         L.oracle_rand_normal.argtypes = [C.POINTER(C.c_uint64), fp, C.c_size_t, C.c_float]
+        ip = C.c_int
+        L.oracle_conv1d.argtypes = [fp, fp, fp, fp, fp, ip, ip, ip, ip, ip, ip, ip, ip]
+        L.oracle_conv1d_transpose.argtypes = [fp, fp, fp, fp, fp, ip, ip, ip, ip, ip, ip, ip]
         L.oracle_double_to_half.argtypes = [C.c_double]
         L.oracle_double_to_half.restype = C.c_uint16
         _lib = L
@@ -99,6 +102,37 @@ def matmul_nt_f64(a, w):
     sc = np.zeros((M, N), dtype=np.float64)
     dp = C.POINTER(C.c_double)
     lib().oracle_matmul_nt_f64(ap, wp, out.ctypes.data_as(dp), sc.ctypes.data_as(dp), M, N, K)
+    return out, sc
+
+
+def conv1d(x, w, b, stride: int, pad: int, groups: int):
+    """conv1d_forward (src/nn.c:765-834): x [B, Cin, T], w [Cout, Cin/groups, k].
+    Returns (out, sum of |w x| + |b|) -- the error scale of the parity tests."""
+    x, xp = _f32(x)
+    w, wp = _f32(w)
+    B, Cin, Tin = x.shape
+    Cout, _, Kw = w.shape
+    Tout = (Tin + 2 * pad - Kw) // stride + 1
+    out = np.zeros((B, Cout, Tout), np.float32)
+    sc = np.zeros_like(out)
+    bp = _f32(b)[1] if b is not None else None
+    lib().oracle_conv1d(xp, wp, bp, out.ctypes.data_as(C.POINTER(C.c_float)), sc.ctypes.data_as(C.POINTER(C.c_float)),
+                        B, Cin, Tin, Cout, Kw, stride, pad, groups)
+    return out, sc
+
+
+def conv1d_transpose(x, w, b, stride: int, pad: int):
+    """conv1d_transpose_forward (src/nn.c:864-931): x [B, Cin, T], w [Cin, Cout, k]."""
+    x, xp = _f32(x)
+    w, wp = _f32(w)
+    B, Cin, Tin = x.shape
+    _, Cout, Kw = w.shape
+    Tout = (Tin - 1) * stride - 2 * pad + Kw
+    out = np.zeros((B, Cout, Tout), np.float32)
+    sc = np.zeros_like(out)
+    bp = _f32(b)[1] if b is not None else None
+    lib().oracle_conv1d_transpose(xp, wp, bp, out.ctypes.data_as(C.POINTER(C.c_float)),
+                                  sc.ctypes.data_as(C.POINTER(C.c_float)), B, Cin, Tin, Cout, Kw, stride, pad)
     return out, sc
 
 

@@ -305,3 +305,62 @@ void oracle_rand_normal(uint64_t* seed, float* out, size_t n, float mult) {
     }
     if (i < n) out[i] = 0.0f;
 }
+
+/* ------------------------------------------------------------------ */
+/* AudioVAE convolutions (src/nn.c:765-834 conv1d_forward,             */
+/* src/nn.c:864-931 conv1d_transpose_forward): same loop order, fp32    */
+/* accumulation.  `absout` (may be NULL) receives the same sums of      */
+/* |w x| -- the scale the parity tests measure errors against.          */
+/* ------------------------------------------------------------------ */
+
+void oracle_conv1d(const float* x, const float* w, const float* b, float* out, float* absout, int B, int Cin,
+                   int Tin, int Cout, int Kw, int stride, int pad, int groups) {
+    const int Tout = (Tin + 2 * pad - Kw) / stride + 1;
+    const int ipg = groups > 0 ? Cin / groups : Cin, opg = groups > 0 ? Cout / groups : Cout;
+    for (int n = 0; n < B; n++)
+        for (int o = 0; o < Cout; o++) {
+            const int c0 = (opg > 0 ? o / opg : 0) * ipg;
+            for (int t = 0; t < Tout; t++) {
+                float sum = b ? b[o] : 0.0f, asum = b ? fabsf(b[o]) : 0.0f;
+                for (int c = c0; c < c0 + ipg; c++)
+                    for (int k = 0; k < Kw; k++) {
+                        const int ti = t * stride + k - pad;
+                        if (ti < 0 || ti >= Tin) continue;
+                        const float p = w[((size_t)o * ipg + (size_t)(c - c0)) * Kw + k] *
+                                        x[((size_t)n * Cin + c) * Tin + ti];
+                        sum += p;
+                        asum += fabsf(p);
+                    }
+                out[((size_t)n * Cout + o) * Tout + t] = sum;
+                if (absout) absout[((size_t)n * Cout + o) * Tout + t] = asum;
+            }
+        }
+}
+
+void oracle_conv1d_transpose(const float* x, const float* w, const float* b, float* out, float* absout, int B,
+                             int Cin, int Tin, int Cout, int Kw, int stride, int pad) {
+    const int Tout = (Tin - 1) * stride - 2 * pad + Kw;
+    memset(out, 0, (size_t)B * Cout * Tout * sizeof(float));
+    if (absout) memset(absout, 0, (size_t)B * Cout * Tout * sizeof(float));
+    for (int n = 0; n < B; n++) {
+        for (int c = 0; c < Cin; c++)
+            for (int ti = 0; ti < Tin; ti++) {
+                const float xv = x[((size_t)n * Cin + c) * Tin + ti];
+                for (int k = 0; k < Kw; k++) {
+                    const int to = ti * stride + k - pad;
+                    if (to < 0 || to >= Tout) continue;
+                    for (int o = 0; o < Cout; o++) {
+                        const float p = w[((size_t)c * Cout + o) * Kw + k] * xv;
+                        out[((size_t)n * Cout + o) * Tout + to] += p;
+                        if (absout) absout[((size_t)n * Cout + o) * Tout + to] += fabsf(p);
+                    }
+                }
+            }
+        if (b)
+            for (int o = 0; o < Cout; o++)
+                for (int t = 0; t < Tout; t++) {
+                    out[((size_t)n * Cout + o) * Tout + t] += b[o];
+                    if (absout) absout[((size_t)n * Cout + o) * Tout + t] += fabsf(b[o]);
+                }
+    }
+}

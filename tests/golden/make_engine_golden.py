@@ -11,7 +11,8 @@ src/*.c built without VOXCPM_CUDA, so every projection runs through
 tensor_matmul_nt's scalar loop (src/tensor.c:617-678) -- for a 64-token
 input (token seed 1) and writes into this folder:
 
-  engine_c4_q8.npz    latents [patches, 64, 4] of loc_dit_sample
+  engine_c4_q8.npz    latents [patches, 64, 4] of loc_dit_sample, and the
+                      peak-normalised audio voxcpm_generate returns
   engine_c4_q8.json   the model files' CRC32C (to pin that a GPU host
                       regenerates the same bytes), the run's settings and
                       its per-stage CPU times (one host thread)
@@ -50,15 +51,17 @@ def main() -> None:
     gen = json.loads(subprocess.run([os.path.join(BUILD, "make_model"), prefix, "--seed", str(args.model_seed)],
                                     check=True, capture_output=True, text=True).stdout.strip().splitlines()[-1])
     lat = os.path.join(work, "cpu_latents.f32")
+    aud = os.path.join(work, "cpu_audio.f32")
     r = subprocess.run([os.path.join(BUILD, "voxq_engine_run_cpu"), "--model", prefix + ".vxcpm", "--patches",
                         str(args.patches), "--tokens", str(args.tokens), "--token-seed", str(args.token_seed),
-                        "--latents", lat], capture_output=True, text=True)
+                        "--latents", lat, "--audio", aud], capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stderr[-4000:])
         raise SystemExit(f"CPU engine failed ({r.returncode})")
     run = json.loads(r.stdout.strip().splitlines()[-1])
     latents = np.fromfile(lat, dtype=np.float32).reshape(args.patches, 64, 4)
-    np.savez_compressed(os.path.join(HERE, "engine_c4_q8.npz"), latents=latents)
+    audio = np.fromfile(aud, dtype=np.float32)
+    np.savez_compressed(os.path.join(HERE, "engine_c4_q8.npz"), latents=latents, audio=audio)
     meta = {"model": {k: gen[k] for k in ("model_bytes", "model_tensors", "model_data_crc32c", "audiovae_bytes",
                                           "audiovae_tensors", "audiovae_data_crc32c", "seed")},
             "patches": args.patches, "tokens": args.tokens, "token_seed": args.token_seed,

@@ -9,11 +9,29 @@ and runs voxcpm_generate (src/model.c:630-1048): TSLM and RALM prefill over 64
 token ids, then per patch the LocDiT sampler (10 Euler steps, CFG 2.0), the
 AudioVAE decode and the LocEnc -> fusion -> RALM update.
 
+The libvoxq build also sends the AudioVAE decoder's convolutions
+(conv1d_forward / conv1d_transpose_forward, src/nn.c:765-931), which the
+reference runs on the host even in its GPU build, to libvoxq's device
+convolutions.
+
 Oracle: the same engine built without VOXCPM_CUDA (the reference CPU path, one
-scalar loop per output, src/tensor.c:617-678) on the same model, whose latents
-are committed in tests/golden/engine_c4_q8.npz (tests/golden/make_engine_golden.py).
-The model's projection weights are exactly representable in Q8, so both runs
-multiply by identical weights.  Rule (north star): latents within 1e-2 max-abs.
+scalar loop per output, src/tensor.c:617-678, and the host convolutions) on the
+same model, whose latents and audio are committed in
+tests/golden/engine_c4_q8.npz (tests/golden/make_engine_golden.py).  The
+model's projection weights are exactly representable in Q8, so both runs
+multiply by identical weights.  Rule (north star): latents within 1e-2
+max-abs.
+
+The device convolutions are checked on the engine's own data by a second run
+of the libvoxq build with VOXQ_ENGINE_VAE=cpu (the reference's host
+convolutions): both runs have bit-identical latents, so their audio differs
+only by the convolution path (fp32 on both sides, different summation order).
+The random-init AudioVAE saturates: its peak-normalised output sits at +-1
+except for isolated transition samples between the two, which move with the
+last bits of their inputs (one sample seen at -0.30 vs -0.35).  Rules on the
+audio: mean |difference| <= 5e-4 and 99th percentile <= 5e-3.  (It is not
+compared with the CPU engine's audio, whose slightly different latents move
+the transitions.)
 """
 from __future__ import annotations
 
@@ -32,6 +50,7 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 BUILD = os.path.join(REPO, "voxcpm2-c_b200", "engine", "_build")
 GOLDEN = os.path.join(REPO, "tests", "golden")
 TOL = 1e-2
+AUDIO_MEAN_TOL, AUDIO_P99_TOL = 5e-4, 5e-3
 
 
 def _workdir():
@@ -44,7 +63,8 @@ def _workdir():
 
 def test_unchanged_engine_on_libvoxq_matches_cpu_engine():
     meta = json.load(open(os.path.join(GOLDEN, "engine_c4_q8.json")))
-    want = np.load(os.path.join(GOLDEN, "engine_c4_q8.npz"))["latents"]
+    gold = np.load(os.path.join(GOLDEN, "engine_c4_q8.npz"))
+    want, want_audio = gold["latents"], gold["audio"]
     for exe in ("make_model", "voxq_engine_run_gpu"):
         assert os.path.exists(os.path.join(BUILD, exe)), \
             f"{exe} missing: build it with `make -C voxcpm2-c_b200/engine REF=<reference checkout>`"
@@ -56,19 +76,24 @@ def test_unchanged_engine_on_libvoxq_matches_cpu_engine():
                                         text=True).stdout.strip().splitlines()[-1])
         for k in ("model_data_crc32c", "audiovae_data_crc32c", "model_bytes", "audiovae_bytes"):
             assert gen[k] == meta["model"][k], f"regenerated model differs from the golden run's ({k})"
-        lat = os.path.join(work, "gpu_latents.f32")
-        env = dict(os.environ, VOXCPM_QUANT="q8")
-        r = subprocess.run([os.path.join(BUILD, "voxq_engine_run_gpu"), "--model", prefix + ".vxcpm", "--gpu",
-                            "--patches", str(meta["patches"]), "--tokens", str(meta["tokens"]),
-                            "--token-seed", str(meta["token_seed"]), "--latents", lat],
-                           env=env, capture_output=True, text=True, timeout=1200)
-        assert r.returncode == 0, r.stderr[-3000:]
-        assert "GPU upload complete" in r.stderr
-        run = json.loads(r.stdout.strip().splitlines()[-1])
-        got = np.fromfile(lat, dtype=np.float32).reshape(want.shape)
+        runs = {}
+        for vae in ("gpu", "cpu"):
+            lat = os.path.join(work, f"lat_{vae}.f32")
+            aud = os.path.join(work, f"audio_{vae}.f32")
+            env = dict(os.environ, VOXCPM_QUANT="q8", VOXQ_ENGINE_VAE=vae)
+            r = subprocess.run([os.path.join(BUILD, "voxq_engine_run_gpu"), "--model", prefix + ".vxcpm", "--gpu",
+                                "--patches", str(meta["patches"]), "--tokens", str(meta["tokens"]),
+                                "--token-seed", str(meta["token_seed"]), "--latents", lat, "--audio", aud],
+                               env=env, capture_output=True, text=True, timeout=1200)
+            assert r.returncode == 0, r.stderr[-3000:]
+            assert "GPU upload complete" in r.stderr
+            runs[vae] = (json.loads(r.stdout.strip().splitlines()[-1]),
+                         np.fromfile(lat, dtype=np.float32).reshape(want.shape), np.fromfile(aud, dtype=np.float32))
+        run, got, got_audio = runs["gpu"]
+        _, got_cpu_vae, host_audio = runs["cpu"]
     finally:
         shutil.rmtree(work, ignore_errors=True)
-    assert run["build"] == "gpu"
+    assert run["build"] == "gpu" and run["vae"] == "gpu"
     mm = run["stages"]["tensor_matmul_nt"]
     assert mm["calls"] == meta["cpu_run"]["stages"]["tensor_matmul_nt"]["calls"]
     # the projections ran on the device: the CPU loop takes ~80 ms per call here
@@ -77,3 +102,12 @@ def test_unchanged_engine_on_libvoxq_matches_cpu_engine():
     assert np.isfinite(got).all()
     assert float(err.max()) <= TOL, f"latents max-abs error {float(err.max()):.3e} per patch " \
                                     f"{[float(e) for e in err.reshape(len(err), -1).max(1)]}"
+    print(f"latents max-abs error per patch: {[float(e) for e in err.reshape(len(err), -1).max(1)]}")
+    # the convolution path: same latents, device vs host convolutions
+    assert np.array_equal(got, got_cpu_vae)
+    assert got_audio.shape == want_audio.shape == host_audio.shape and np.isfinite(got_audio).all()
+    d = np.abs(got_audio.astype(np.float64) - host_audio)
+    mean, p99 = float(d.mean()), float(np.quantile(d, 0.99))
+    print(f"audio, device vs host convolutions on the same latents: mean |d| {mean:.2e}, p99 {p99:.2e}, "
+          f"max {float(d.max()):.2e}")
+    assert mean <= AUDIO_MEAN_TOL and p99 <= AUDIO_P99_TOL, f"audio mean |d| {mean:.2e}, p99 {p99:.2e}"

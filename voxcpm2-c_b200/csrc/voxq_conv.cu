@@ -1,0 +1,266 @@
+// voxq_conv.cu -- the AudioVAE's 1-D convolutions on the device.
+//
+// The reference decodes audio on the host even in its GPU build (src/model.c:
+// 554-556 keeps every AudioVAE weight on the CPU); its decoder is a chain of
+// weight-normalised 1-D convolutions -- depthwise k = 7, pointwise k = 1, the
+// 64 -> 2048 projection and six transposed upsampling convolutions -- computed by
+// conv1d_forward and conv1d_transpose_forward (src/nn.c:765-931).  These entry
+// points compute the same functions on the device, in fp32 like the reference:
+//
+//   conv1d:      out[n,o,t] = b[o] + sum_{c in group(o)} sum_k
+//                             w[o, c - c0, k] * x[n, c, t*stride + k - pad]
+//   transposed:  out[n,o,t] = b[o] + sum_c sum_{k, s: s*stride + k - pad = t}
+//                             w[c, o, k] * x[n, c, s]
+//
+// One thread computes kTPT consecutive time steps of one output channel; a
+// warp covers 32 * kTPT consecutive steps of that channel (coalesced loads of x
+// and stores of out, one broadcast weight per tap).  Host tensors are staged
+// through the library stream; host weights are uploaded once per pointer and
+// kept (the AudioVAE's effective weights are fixed for the model's lifetime),
+// keyed by pointer, size and a content fingerprint.
+#include <mutex>
+#include <unordered_map>
+
+#include "voxq_common.cuh"
+#include "voxq_internal.h"
+
+namespace voxq {
+
+constexpr int kTPT = 4;           // time steps per thread
+constexpr int kConvThreads = 256;  // 8 output channels per block
+
+__global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                              const float* __restrict__ b, float* __restrict__ out,
+                                                              int Cin, int Tin, int Cout, int Tout, int Kw, int stride,
+                                                              int pad, int groups) {
+    const int o = blockIdx.y * (kConvThreads / 32) + (threadIdx.x >> 5);
+    const int n = blockIdx.z;
+    const int t0 = (blockIdx.x * 32 + (threadIdx.x & 31)) * kTPT;
+    if (o >= Cout || t0 >= Tout) return;
+    const int ipg = Cin / groups, opg = Cout / groups;
+    const int c0 = (o / opg) * ipg;
+    const float* xn = x + (int64_t)n * Cin * Tin;
+    const float* wo = w + (int64_t)o * ipg * Kw;
+    float acc[kTPT];
+#pragma unroll
+    for (int j = 0; j < kTPT; j++) acc[j] = b ? b[o] : 0.0f;
+    for (int c = 0; c < ipg; c++) {
+        const float* xc = xn + (int64_t)(c0 + c) * Tin;
+        const float* wc = wo + c * Kw;
+        for (int k = 0; k < Kw; k++) {
+            const float wv = __ldg(wc + k);
+#pragma unroll
+            for (int j = 0; j < kTPT; j++) {
+                const int ti = (t0 + j) * stride + k - pad;
+                if (ti >= 0 && ti < Tin) acc[j] = fmaf(wv, __ldg(xc + ti), acc[j]);
+            }
+        }
+    }
+    float* on = out + ((int64_t)n * Cout + o) * Tout;
+#pragma unroll
+    for (int j = 0; j < kTPT; j++)
+        if (t0 + j < Tout) on[t0 + j] = acc[j];
+}
+
+__global__ void __launch_bounds__(kConvThreads) convt1d_kernel(const float* __restrict__ x,
+                                                               const float* __restrict__ w,
+                                                               const float* __restrict__ b, float* __restrict__ out,
+                                                               int Cin, int Tin, int Cout, int Tout, int Kw,
+                                                               int stride, int pad) {
+    const int o = blockIdx.y * (kConvThreads / 32) + (threadIdx.x >> 5);
+    const int n = blockIdx.z;
+    const int t0 = (blockIdx.x * 32 + (threadIdx.x & 31)) * kTPT;
+    if (o >= Cout || t0 >= Tout) return;
+    const float* xn = x + (int64_t)n * Cin * Tin;
+    float acc[kTPT];
+#pragma unroll
+    for (int j = 0; j < kTPT; j++) acc[j] = 0.0f;
+    for (int c = 0; c < Cin; c++) {
+        const float* xc = xn + (int64_t)c * Tin;
+        const float* wc = w + ((int64_t)c * Cout + o) * Kw;
+#pragma unroll
+        for (int j = 0; j < kTPT; j++) {
+            // taps k with (t + pad - k) a non-negative multiple of stride below Tin * stride
+            const int tp = t0 + j + pad;
+            for (int k = tp % stride; k < Kw && k <= tp; k += stride) {
+                const int s = (tp - k) / stride;
+                if (s < Tin) acc[j] = fmaf(__ldg(wc + k), __ldg(xc + s), acc[j]);
+            }
+        }
+    }
+    float* on = out + ((int64_t)n * Cout + o) * Tout;
+#pragma unroll
+    for (int j = 0; j < kTPT; j++)
+        if (t0 + j < Tout) on[t0 + j] = acc[j] + (b ? b[o] : 0.0f);
+}
+
+namespace {
+
+struct DevBuf {
+    float* p;
+    size_t n;
+    uint64_t fp;  // fingerprint of the host contents uploaded
+};
+
+// FNV-1a over the size and 64 evenly spaced values (first and last included):
+// a host buffer freed and reallocated at the same address with other contents
+// is uploaded again.  Constant cost per call; a weight changed in place at
+// unsampled positions is not detected (voxq_conv_cache_clear drops the cache).
+uint64_t fingerprint(const float* h, size_t n) {
+    uint64_t f = 0xcbf29ce484222325ull ^ n;
+    const size_t samples = n < 64 ? n : 64;
+    for (size_t i = 0; i < samples; i++) {
+        const size_t j = samples > 1 ? i * (n - 1) / (samples - 1) : 0;
+        uint32_t bits;
+        memcpy(&bits, h + j, 4);
+        f = (f ^ bits) * 0x100000001b3ull;
+    }
+    return f;
+}
+std::mutex g_conv_mu;
+std::unordered_map<const void*, DevBuf> g_conv_w;  // host weight / bias pointer -> device copy
+float* g_conv_io[2] = {nullptr, nullptr};          // device staging of x and out
+size_t g_conv_io_n[2] = {0, 0};
+
+// Device pointer of a Tensor's fp32 payload: its own for device tensors, a
+// cached upload for host tensors (weights and biases).
+VoxCPMError weight_ptr(const Tensor* t, cudaStream_t st, const float** out) {
+    *out = nullptr;
+    if (!t) return VOXCPM_SUCCESS;
+    if (t->is_fp16 || !t->data) return VOXCPM_ERR_UNSUPPORTED;
+    if (t->is_cuda) {
+        *out = t->data;
+        return VOXCPM_SUCCESS;
+    }
+    std::lock_guard<std::mutex> lk(g_conv_mu);
+    const uint64_t fp = fingerprint(t->data, t->size);
+    auto it = g_conv_w.find(t->data);
+    if (it != g_conv_w.end() && it->second.n == t->size && it->second.fp == fp) {
+        *out = it->second.p;
+        return VOXCPM_SUCCESS;
+    }
+    float* d = nullptr;
+    VOXQ_CUDA_TRY(cudaMalloc(&d, t->size * sizeof(float)));
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(d, t->data, t->size * sizeof(float), cudaMemcpyHostToDevice, st));
+    VOXQ_CUDA_TRY(cudaStreamSynchronize(st));
+    if (it != g_conv_w.end()) cudaFree(it->second.p);
+    g_conv_w[t->data] = DevBuf{d, t->size, fp};
+    *out = d;
+    return VOXCPM_SUCCESS;
+}
+
+float* io_buf(int k, size_t n) {
+    if (g_conv_io_n[k] >= n) return g_conv_io[k];
+    size_t want = 1 << 18;
+    while (want < n) want <<= 1;
+    float* p = nullptr;
+    if (cudaMalloc(&p, want * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (g_conv_io[k]) {
+        cudaDeviceSynchronize();  // the old buffer may still be read by queued work
+        cudaFree(g_conv_io[k]);
+    }
+    g_conv_io[k] = p;
+    g_conv_io_n[k] = want;
+    return p;
+}
+
+// Runs one convolution with host or device x / out (x [B, Cin, Tin], out
+// [B, Cout, Tout] fp32, contiguous).
+template <typename Launch>
+VoxCPMError run_conv(const Tensor* x, Tensor* out, cudaStream_t st, Launch launch) {
+    const float* d_x = x->data;
+    float* d_o = out->data;
+    std::unique_lock<std::mutex> lk(g_conv_mu);
+    if (!x->is_cuda) {
+        float* b = io_buf(0, x->size);
+        if (!b) return VOXCPM_ERR_OOM;
+        VOXQ_CUDA_TRY(cudaMemcpyAsync(b, x->data, x->size * sizeof(float), cudaMemcpyHostToDevice, st));
+        d_x = b;
+    }
+    if (!out->is_cuda) {
+        d_o = io_buf(1, out->size);
+        if (!d_o) return VOXCPM_ERR_OOM;
+    }
+    launch(d_x, d_o);
+    VOXQ_CUDA_TRY(cudaGetLastError());
+    if (!out->is_cuda) {
+        VOXQ_CUDA_TRY(cudaMemcpyAsync(out->data, d_o, out->size * sizeof(float), cudaMemcpyDeviceToHost, st));
+    }
+    // host outputs are valid on return; staged inputs are free for the next call
+    if (!out->is_cuda || !x->is_cuda) VOXQ_CUDA_TRY(cudaStreamSynchronize(st));
+    return VOXCPM_SUCCESS;
+}
+
+}  // namespace
+
+void conv_cache_clear() {
+    std::lock_guard<std::mutex> lk(g_conv_mu);
+    for (auto& kv : g_conv_w) cudaFree(kv.second.p);
+    g_conv_w.clear();
+    for (int k = 0; k < 2; k++) {
+        if (g_conv_io[k]) cudaFree(g_conv_io[k]);
+        g_conv_io[k] = nullptr;
+        g_conv_io_n[k] = 0;
+    }
+}
+
+}  // namespace voxq
+
+using namespace voxq;
+
+extern "C" void voxq_conv_cache_clear(void) { conv_cache_clear(); }
+
+extern "C" VoxCPMError voxq_conv1d_forward(const voxq_conv1d_desc* conv, const Tensor* x, Tensor* out) {
+    if (!conv || !x || !out || !conv->weight) return VOXCPM_ERR_INTERNAL;
+    cudaStream_t st = (cudaStream_t)library_stream();
+    if (!st) return VOXCPM_ERR_CUDA_NOT_FOUND;
+    if (x->ndim != 3 || out->ndim != 3 || x->is_fp16 || out->is_fp16) return VOXCPM_ERR_SHAPE_MISMATCH;
+    const int B = x->shape[0], Cin = x->shape[1], Tin = x->shape[2];
+    const int Cout = conv->out_channels, Kw = conv->kernel_size, stride = conv->stride, pad = conv->padding;
+    const int groups = conv->groups > 0 ? conv->groups : 1;
+    if (Cin != conv->in_channels || Cin % groups || Cout % groups || stride < 1 || Kw < 1)
+        return VOXCPM_ERR_SHAPE_MISMATCH;
+    const int Tout = (Tin + 2 * pad - Kw) / stride + 1;
+    if (Tout <= 0 || out->shape[0] != B || out->shape[1] != Cout || out->shape[2] != Tout)
+        return VOXCPM_ERR_SHAPE_MISMATCH;
+    if (conv->weight->size != (size_t)Cout * (Cin / groups) * Kw || (conv->bias && conv->bias->size < (size_t)Cout))
+        return VOXCPM_ERR_SHAPE_MISMATCH;
+    const float *d_w = nullptr, *d_b = nullptr;
+    VoxCPMError e = weight_ptr(conv->weight, st, &d_w);
+    if (!e) e = weight_ptr(conv->bias, st, &d_b);
+    if (e) return e;
+    return run_conv(x, out, st, [&](const float* d_x, float* d_o) {
+        const dim3 grid((unsigned)((Tout + 32 * kTPT - 1) / (32 * kTPT)),
+                        (unsigned)((Cout + kConvThreads / 32 - 1) / (kConvThreads / 32)), (unsigned)B);
+        conv1d_kernel<<<grid, kConvThreads, 0, st>>>(d_x, d_w, d_b, d_o, Cin, Tin, Cout, Tout, Kw, stride, pad,
+                                                      groups);
+    });
+}
+
+extern "C" VoxCPMError voxq_conv1d_transpose_forward(const voxq_conv1d_transpose_desc* conv, const Tensor* x,
+                                                     Tensor* out) {
+    if (!conv || !x || !out || !conv->weight) return VOXCPM_ERR_INTERNAL;
+    cudaStream_t st = (cudaStream_t)library_stream();
+    if (!st) return VOXCPM_ERR_CUDA_NOT_FOUND;
+    if (x->ndim != 3 || out->ndim != 3 || x->is_fp16 || out->is_fp16) return VOXCPM_ERR_SHAPE_MISMATCH;
+    const int B = x->shape[0], Cin = x->shape[1], Tin = x->shape[2];
+    const int Cout = conv->out_channels, Kw = conv->kernel_size, stride = conv->stride, pad = conv->padding;
+    if (Cin != conv->in_channels || stride < 1 || Kw < 1 || pad < 0) return VOXCPM_ERR_SHAPE_MISMATCH;
+    const int Tout = (Tin - 1) * stride - 2 * pad + Kw;
+    if (Tout <= 0 || out->shape[0] != B || out->shape[1] != Cout || out->shape[2] != Tout)
+        return VOXCPM_ERR_SHAPE_MISMATCH;
+    if (conv->weight->size != (size_t)Cin * Cout * Kw || (conv->bias && conv->bias->size < (size_t)Cout))
+        return VOXCPM_ERR_SHAPE_MISMATCH;
+    const float *d_w = nullptr, *d_b = nullptr;
+    VoxCPMError e = weight_ptr(conv->weight, st, &d_w);
+    if (!e) e = weight_ptr(conv->bias, st, &d_b);
+    if (e) return e;
+    return run_conv(x, out, st, [&](const float* d_x, float* d_o) {
+        const dim3 grid((unsigned)((Tout + 32 * kTPT - 1) / (32 * kTPT)),
+                        (unsigned)((Cout + kConvThreads / 32 - 1) / (kConvThreads / 32)), (unsigned)B);
+        convt1d_kernel<<<grid, kConvThreads, 0, st>>>(d_x, d_w, d_b, d_o, Cin, Tin, Cout, Tout, Kw, stride, pad);
+    });
+}

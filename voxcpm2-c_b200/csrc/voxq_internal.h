@@ -46,6 +46,14 @@ int* device_error_word();
 // device variable; reading it allocates nothing).  -1 if it cannot be read.
 int noalloc_error(bool clear);
 
+// The current device's library stream (tensor_cuda_init), or nullptr when the
+// library is not initialised on it.
+void* library_stream();
+
+// Drops the AudioVAE convolutions' cached device weights and staging
+// (voxq_conv.cu); called by tensor_cuda_shutdown.
+void conv_cache_clear();
+
 // Per-device workspace arena (voxq_runtime.cu): grows on demand, never
 // shrinks, ordered on the stream that uses it.
 void* workspace(size_t bytes);

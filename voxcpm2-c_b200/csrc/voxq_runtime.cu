@@ -163,6 +163,11 @@ static DevState* state() {
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+void* library_stream() {
+    DevState* s = state();
+    return (s && s->init) ? (void*)s->stream : nullptr;
+}
+
 }  // namespace voxq
 
 using namespace voxq;
@@ -271,6 +276,7 @@ extern "C" void tensor_cuda_shutdown(void) {
     if (!s || !s->init) return;
     cudaStreamSynchronize(s->stream);
     cudaDeviceSynchronize();  // the workspaces may also serve voxq_* calls on other streams
+    conv_cache_clear();
     for (int k = 0; k < kSlots; k++) {
         if (s->slot[k]) cudaFree(s->slot[k]);
         s->slot[k] = nullptr;

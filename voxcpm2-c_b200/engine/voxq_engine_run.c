@@ -6,7 +6,7 @@
  * the time spent per stage and the real-time factor.
  *
  *   voxq_engine_run --model M.vxcpm [--patches N] [--tokens T] [--token-seed S]
- *                   [--gpu] [--latents OUT.f32] [--ralm-max-seq L]
+ *                   [--gpu] [--latents OUT.f32] [--audio OUT.f32] [--ralm-max-seq L]
  *   prints one JSON line.
  *
  * The engine's sources are compiled as they are.  The run is observed at the
@@ -26,6 +26,13 @@
  *                      seeded xorshift64 (a vocabulary of placeholder
  *                      strings is built with tokenizer_create_bpe so the
  *                      engine holds a real tokenizer object);
+ *   conv1d_forward, conv1d_transpose_forward (the libvoxq build only)
+ *                      the AudioVAE decoder's convolutions (src/nn.c:765-931),
+ *                      which the reference runs on the host even in its GPU
+ *                      build, go to voxq_conv1d_forward /
+ *                      voxq_conv1d_transpose_forward on the device (same
+ *                      functions, fp32); VOXQ_ENGINE_VAE=cpu keeps them on the
+ *                      host;
  *   ralm_setup_cache   with --ralm-max-seq L, sets the RALM cache length to
  *                      L before the cache is allocated.  voxcpm_generate fixes
  *                      it at 2048 positions (src/model.c:709), which holds
@@ -40,9 +47,13 @@
 #include <time.h>
 
 #include "model.h"
+#include "nn.h"
 #include "tensor.h"
 #include "tokenizer.h"
 #include "voxcpm.h"
+#ifdef VOXQ_ENGINE_LIBVOXQ
+#include "voxq.h"
+#endif
 
 static double now(void) {
     struct timespec ts;
@@ -173,6 +184,28 @@ VoxCPMError __wrap_loc_dit_sample(const LocDiT* dit, const Tensor* mu, const Ten
     return r;
 }
 
+#ifdef VOXQ_ENGINE_LIBVOXQ
+/* Conv1D / Conv1DTranspose (include/nn.h:198-229) and voxq's descriptors have
+ * the same layout. */
+static int g_vae_gpu = 1;
+VoxCPMError __real_conv1d_forward(const Conv1D* conv, const Tensor* x, Tensor* out);
+VoxCPMError __wrap_conv1d_forward(const Conv1D* conv, const Tensor* x, Tensor* out) {
+    if (g_vae_gpu) {
+        const VoxCPMError r = voxq_conv1d_forward((const voxq_conv1d_desc*)conv, x, out);
+        if (r != VOXCPM_ERR_CUDA_NOT_FOUND) return r;
+    }
+    return __real_conv1d_forward(conv, x, out);
+}
+VoxCPMError __real_conv1d_transpose_forward(const Conv1DTranspose* conv, const Tensor* x, Tensor* out);
+VoxCPMError __wrap_conv1d_transpose_forward(const Conv1DTranspose* conv, const Tensor* x, Tensor* out) {
+    if (g_vae_gpu) {
+        const VoxCPMError r = voxq_conv1d_transpose_forward((const voxq_conv1d_transpose_desc*)conv, x, out);
+        if (r != VOXCPM_ERR_CUDA_NOT_FOUND) return r;
+    }
+    return __real_conv1d_transpose_forward(conv, x, out);
+}
+#endif
+
 VoxCPMError __real_ralm_setup_cache(RALM* ralm, int batch_size);
 VoxCPMError __wrap_ralm_setup_cache(RALM* ralm, int batch_size) {
     if (ralm && g_ralm_max_seq > 0) ralm->max_seq_len = g_ralm_max_seq;
@@ -212,6 +245,7 @@ int __wrap_tokenizer_encode(const Tokenizer* tok, const char* text, int32_t* out
 int main(int argc, char** argv) {
     const char* model_path = NULL;
     const char* latents_path = NULL;
+    const char* audio_path = NULL;
     int patches = 4, gpu = 0;
     for (int i = 1; i < argc; i++) {
         const char* a = argv[i];
@@ -221,11 +255,12 @@ int main(int argc, char** argv) {
         else if (!strcmp(a, "--tokens") && v) { g_tokens = atoi(v); i++; }
         else if (!strcmp(a, "--token-seed") && v) { g_token_seed = strtoull(v, NULL, 10); i++; }
         else if (!strcmp(a, "--latents") && v) { latents_path = v; i++; }
+        else if (!strcmp(a, "--audio") && v) { audio_path = v; i++; }
         else if (!strcmp(a, "--ralm-max-seq") && v) { g_ralm_max_seq = atoi(v); i++; }
         else if (!strcmp(a, "--gpu")) gpu = 1;
         else {
             fprintf(stderr, "usage: %s --model M.vxcpm [--patches N] [--tokens T] [--token-seed S] [--gpu] "
-                            "[--latents OUT.f32] [--ralm-max-seq L]\n", argv[0]);
+                            "[--latents OUT.f32] [--audio OUT.f32] [--ralm-max-seq L]\n", argv[0]);
             return 2;
         }
     }
@@ -233,6 +268,9 @@ int main(int argc, char** argv) {
     const char* mm_log = getenv("VOXQ_ENGINE_MATMUL_LOG");
     if (mm_log && *mm_log) g_mm_log = fopen(mm_log, "w");
     g_dump_calls = getenv("VOXQ_ENGINE_DUMP_CALL");
+#ifdef VOXQ_ENGINE_LIBVOXQ
+    if (getenv("VOXQ_ENGINE_VAE") && !strcmp(getenv("VOXQ_ENGINE_VAE"), "cpu")) g_vae_gpu = 0;
+#endif
     g_dump_dir = getenv("VOXQ_ENGINE_DUMP_DIR");
 
     const double t_create = now();
@@ -288,11 +326,24 @@ int main(int argc, char** argv) {
             return 1;
         }
     }
-    printf("{\"build\": \"%s\", \"patches\": %d, \"tokens\": %d, \"token_seed\": %llu, \"latent_floats\": %d, "
+    if (audio_path) {
+        FILE* f = fopen(audio_path, "wb");
+        const size_t n = (size_t)audio.num_samples;
+        if (!f || fwrite(audio.samples, sizeof(float), n, f) != n || fclose(f)) {
+            fprintf(stderr, "cannot write %s\n", audio_path);
+            return 1;
+        }
+    }
+    printf("{\"build\": \"%s\", \"vae\": \"%s\", \"patches\": %d, \"tokens\": %d, \"token_seed\": %llu, \"latent_floats\": %d, "
            "\"samples\": %d, \"sample_rate\": %d, \"audio_s\": %.6f, \"generate_s\": %.4f, \"rtf\": %.5f, "
            "\"create_s\": %.3f, \"upload_s\": %.3f, \"audio_abs_mean\": %.9g, \"ralm_max_seq\": %d, \"stages\": {",
 #ifdef VOXCPM_CUDA
            "gpu",
+#else
+           "cpu",
+#endif
+#ifdef VOXQ_ENGINE_LIBVOXQ
+           g_vae_gpu ? "gpu" : "cpu",
 #else
            "cpu",
 #endif

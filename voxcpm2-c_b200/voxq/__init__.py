@@ -63,6 +63,20 @@ class QWeightDesc(C.Structure):
                 ("qtype", C.c_int32), ("q8_signed", C.c_int32)]
 
 
+class Conv1dDesc(C.Structure):
+    """voxq_conv1d_desc: the layout of the engine's Conv1D (include/nn.h:198-207)."""
+
+    _fields_ = [("weight", C.c_void_p), ("bias", C.c_void_p), ("in_channels", C.c_int), ("out_channels", C.c_int),
+                ("kernel_size", C.c_int), ("stride", C.c_int), ("padding", C.c_int), ("groups", C.c_int)]
+
+
+class Conv1dTransposeDesc(C.Structure):
+    """voxq_conv1d_transpose_desc: the layout of the engine's Conv1DTranspose (include/nn.h:221-229)."""
+
+    _fields_ = [("weight", C.c_void_p), ("bias", C.c_void_p), ("in_channels", C.c_int), ("out_channels", C.c_int),
+                ("kernel_size", C.c_int), ("stride", C.c_int), ("padding", C.c_int)]
+
+
 class Epilogue(C.Structure):
     _fields_ = [("bias", C.c_void_p), ("residual", C.c_void_p), ("ldr", C.c_int64),
                 ("up", C.POINTER(QWeightDesc))]
@@ -116,6 +130,9 @@ SIGNATURES = {
     "voxq_noalloc_device_error": ([_i], _i),
     "voxq_matmul_nt_dense": ([_vp, _i, _i64, _vp, _i, _i, _i, _vp, _i64, _vp], _i),
     "voxq_gemv_batch": ([C.POINTER(GemvItem), _i, _vp], _i),
+    "voxq_conv1d_forward": ([C.POINTER(Conv1dDesc), _TP, _TP], _i),
+    "voxq_conv1d_transpose_forward": ([C.POINTER(Conv1dTransposeDesc), _TP, _TP], _i),
+    "voxq_conv_cache_clear": ([], None),
     "voxq_vxcpm2_open": ([C.c_char_p, C.POINTER(_vp)], _i),
     "voxq_vxcpm2_close": ([_vp], None),
     "voxq_vxcpm2_info": ([_vp, C.POINTER(Vxcpm2Header), C.POINTER(_i)], _i),
