@@ -13,6 +13,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -177,6 +178,16 @@ using namespace voxq;
 // ===========================================================================
 
 extern "C" const char* voxq_version(void) { return "voxq-b200 0.1 (sm_100a)"; }
+
+// tensor_matmul_nt_cuda's work counters (voxq_matmul_traffic)
+static std::atomic<uint64_t> g_mm_calls{0}, g_mm_wbytes{0};
+
+extern "C" void voxq_matmul_traffic(uint64_t* calls, uint64_t* weight_bytes, int reset) {
+    const uint64_t c = reset ? g_mm_calls.exchange(0) : g_mm_calls.load();
+    const uint64_t b = reset ? g_mm_wbytes.exchange(0) : g_mm_wbytes.load();
+    if (calls) *calls = c;
+    if (weight_bytes) *weight_bytes = b;
+}
 
 extern "C" int voxq_device_error(int clear) {
     int* e = device_error_word();
@@ -519,9 +530,12 @@ extern "C" VoxCPMError tensor_matmul_nt_cuda(const Tensor* a, const Tensor* b, T
     }
     // weight
     VoxCPMError e;
+    g_mm_calls.fetch_add(1, std::memory_order_relaxed);
     if (qit != g_qtab.end()) {
         const QRec& q = qit->second;
         voxq_qweight w = {q.codes, q.scales, q.N, q.K, q.qtype, 0};
+        g_mm_wbytes.fetch_add(voxq_codes_bytes(q.N, q.K, q.qtype) + voxq_scales_bytes(q.N, q.K, q.qtype),
+                              std::memory_order_relaxed);
         if (M > 8) {
             void* ws = slot_get(*s, 3, gemm_workspace_bytes(M, N, K, q.qtype, false));
             if (!ws) return VOXCPM_ERR_OOM;
@@ -533,6 +547,7 @@ extern "C" VoxCPMError tensor_matmul_nt_cuda(const Tensor* a, const Tensor* b, T
         }
     } else {
         const void* d_w = b->is_fp16 ? (const void*)b->data_fp16 : (const void*)b->data;
+        g_mm_wbytes.fetch_add((uint64_t)N * K * (b->is_fp16 ? 2 : 4), std::memory_order_relaxed);
         if (!b->is_cuda) {
             const size_t wb = (size_t)N * K * (b->is_fp16 ? 2 : 4);
             void* dw = slot_get(*s, 2, wb);

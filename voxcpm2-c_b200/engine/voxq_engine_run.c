@@ -9,6 +9,14 @@
  *                   [--gpu] [--latents OUT.f32] [--audio OUT.f32] [--ralm-max-seq L]
  *   prints one JSON line.
  *
+ *   voxq_engine_run --model M.vxcpm --serve [--gpu] [--ralm-max-seq L] [--latents-dir D]
+ *   serving worker: loads the model once, prints {"ready": ...}, then runs one
+ *   utterance per line read from standard input ("INDEX TOKENS TOKEN_SEED
+ *   PATCHES"), printing one JSON line per utterance (its time, the hash of its
+ *   latents, and with D the latents in D/utt<INDEX>.f32) until "quit" or end
+ *   of input.  voxcpm_generate re-creates its caches on every call
+ *   (src/model.c:706-730), so utterances are independent.
+ *
  * The engine's sources are compiled as they are.  The run is observed at the
  * engine's own function boundaries, which the linker redirects here
  * (-Wl,--wrap=NAME sends model.c's calls of NAME, defined in another object,
@@ -242,8 +250,99 @@ int __wrap_tokenizer_encode(const Tokenizer* tok, const char* text, int32_t* out
     return g_tokens;
 }
 
+/* FNV-1a 64 of the bytes of the latents gathered so far */
+static unsigned long long latents_fnv(void) {
+    unsigned long long h = 1469598103934665603ull;
+    const unsigned char* b = (const unsigned char*)g_latents;
+    for (size_t i = 0; i < (size_t)g_latent_n * sizeof(float); i++) {
+        h ^= b[i];
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+static void print_stages(void) {
+    printf("\"stages\": {");
+    for (int s = 0; s < ST_N; s++) {
+        printf("%s\"%s\": {\"s\": %.5f, \"calls\": %ld", s ? ", " : "", k_stage[s], g_stage_s[s], g_stage_calls[s]);
+        if (s != ST_MATMUL) printf(", \"matmul_s\": %.5f", g_matmul_in[s]);  /* tensor_matmul_nt time inside */
+        printf("}");
+    }
+    printf("}");
+}
+
+/* Serving worker: one utterance per input line, until "quit" or end of input. */
+static int serve(VoxCPMModel* model, const char* latents_dir) {
+    char line[256];
+    while (fgets(line, sizeof line, stdin)) {
+        if (!strncmp(line, "quit", 4)) break;
+        long idx = -1;
+        int tokens = 0, patches = 0;
+        unsigned long long seed = 0;
+        if (sscanf(line, "%ld %d %llu %d", &idx, &tokens, &seed, &patches) != 4 || idx < 0 || tokens < 1 ||
+            patches < 1) {
+            printf("{\"error\": \"bad request\"}\n");
+            fflush(stdout);
+            continue;
+        }
+        g_tokens = tokens;
+        g_token_seed = seed;
+        g_latent_n = 0;
+        memset(g_stage_s, 0, sizeof(g_stage_s));
+        memset(g_stage_calls, 0, sizeof(g_stage_calls));
+        memset(g_matmul_in, 0, sizeof(g_matmul_in));
+#ifdef VOXQ_ENGINE_LIBVOXQ
+        voxq_matmul_traffic(NULL, NULL, 1);
+#endif
+        VoxCPMGenConfig gen = voxcpm_gen_config_default();
+        gen.text = "synthetic token ids";
+        gen.cfg_value = 2.0f;
+        gen.inference_timesteps = 10;
+        gen.max_new_tokens = 4 * patches;
+        VoxCPMAudio audio;
+        memset(&audio, 0, sizeof(audio));
+        const double t0 = now();
+        const VoxCPMError err = voxcpm_generate(model, &gen, &audio);
+        const double gen_s = now() - t0;
+        unsigned long long calls = 0, wbytes = 0;
+#ifdef VOXQ_ENGINE_LIBVOXQ
+        uint64_t c64 = 0, b64 = 0;
+        voxq_matmul_traffic(&c64, &b64, 1);
+        calls = c64;
+        wbytes = b64;
+#endif
+        if (err != VOXCPM_SUCCESS) {
+            printf("{\"utt\": %ld, \"error\": \"%s\"}\n", idx, voxcpm_error_string(err));
+            fflush(stdout);
+            continue;
+        }
+        if (latents_dir) {
+            char path[1024];
+            snprintf(path, sizeof path, "%s/utt%ld.f32", latents_dir, idx);
+            FILE* f = fopen(path, "wb");
+            if (f) {
+                fwrite(g_latents, sizeof(float), (size_t)g_latent_n, f);
+                fclose(f);
+            }
+        }
+        const double audio_s = audio.sample_rate > 0 ? (double)audio.num_samples / audio.sample_rate : 0.0;
+        printf("{\"utt\": %ld, \"tokens\": %d, \"token_seed\": %llu, \"patches\": %d, \"latent_floats\": %d, "
+               "\"latents_fnv\": \"%016llx\", \"samples\": %d, \"audio_s\": %.6f, \"generate_s\": %.4f, "
+               "\"matmul_calls\": %llu, \"weight_bytes\": %llu, ",
+               idx, tokens, seed, g_latent_n / 256, g_latent_n, latents_fnv(), audio.num_samples, audio_s, gen_s,
+               calls, wbytes);
+        print_stages();
+        printf("}\n");
+        fflush(stdout);
+        voxcpm_audio_free(&audio);
+    }
+    return 0;
+}
+
 int main(int argc, char** argv) {
     const char* model_path = NULL;
+    const char* latents_dir = NULL;
+    int serve_mode = 0;
     const char* latents_path = NULL;
     const char* audio_path = NULL;
     int patches = 4, gpu = 0;
@@ -257,10 +356,13 @@ int main(int argc, char** argv) {
         else if (!strcmp(a, "--latents") && v) { latents_path = v; i++; }
         else if (!strcmp(a, "--audio") && v) { audio_path = v; i++; }
         else if (!strcmp(a, "--ralm-max-seq") && v) { g_ralm_max_seq = atoi(v); i++; }
+        else if (!strcmp(a, "--latents-dir") && v) { latents_dir = v; i++; }
+        else if (!strcmp(a, "--serve")) serve_mode = 1;
         else if (!strcmp(a, "--gpu")) gpu = 1;
         else {
             fprintf(stderr, "usage: %s --model M.vxcpm [--patches N] [--tokens T] [--token-seed S] [--gpu] "
-                            "[--latents OUT.f32] [--audio OUT.f32] [--ralm-max-seq L]\n", argv[0]);
+                            "[--latents OUT.f32] [--audio OUT.f32] [--ralm-max-seq L] [--serve [--latents-dir D]]\n",
+                    argv[0]);
             return 2;
         }
     }
@@ -295,6 +397,22 @@ int main(int argc, char** argv) {
             voxcpm_free(model);
             return 1;
         }
+    }
+
+    if (serve_mode) {
+        printf("{\"ready\": true, \"build\": \"%s\", \"create_s\": %.3f, \"upload_s\": %.3f, \"ralm_max_seq\": %d}\n",
+#ifdef VOXCPM_CUDA
+               "gpu",
+#else
+               "cpu",
+#endif
+               create_s, upload_s, g_ralm_max_seq);
+        fflush(stdout);
+        const int rc = serve(model, latents_dir);
+        voxcpm_free(model);
+        free(g_latents);
+        if (g_mm_log) fclose(g_mm_log);
+        return rc;
     }
 
     VoxCPMGenConfig gen = voxcpm_gen_config_default();
@@ -336,7 +454,7 @@ int main(int argc, char** argv) {
     }
     printf("{\"build\": \"%s\", \"vae\": \"%s\", \"patches\": %d, \"tokens\": %d, \"token_seed\": %llu, \"latent_floats\": %d, "
            "\"samples\": %d, \"sample_rate\": %d, \"audio_s\": %.6f, \"generate_s\": %.4f, \"rtf\": %.5f, "
-           "\"create_s\": %.3f, \"upload_s\": %.3f, \"audio_abs_mean\": %.9g, \"ralm_max_seq\": %d, \"stages\": {",
+           "\"create_s\": %.3f, \"upload_s\": %.3f, \"audio_abs_mean\": %.9g, \"ralm_max_seq\": %d, ",
 #ifdef VOXCPM_CUDA
            "gpu",
 #else
@@ -350,12 +468,8 @@ int main(int argc, char** argv) {
            patches, g_tokens, (unsigned long long)g_token_seed, g_latent_n, audio.num_samples, audio.sample_rate,
            audio_s, gen_s, audio_s > 0 ? gen_s / audio_s : 0.0, create_s, upload_s,
            audio.num_samples ? asum / audio.num_samples : 0.0, g_ralm_max_seq);
-    for (int s = 0; s < ST_N; s++) {
-        printf("%s\"%s\": {\"s\": %.5f, \"calls\": %ld", s ? ", " : "", k_stage[s], g_stage_s[s], g_stage_calls[s]);
-        if (s != ST_MATMUL) printf(", \"matmul_s\": %.5f", g_matmul_in[s]);  /* tensor_matmul_nt time inside */
-        printf("}");
-    }
-    printf("}}\n");
+    print_stages();
+    printf("}\n");
     voxcpm_audio_free(&audio);
     voxcpm_free(model);
     free(g_latents);

@@ -116,6 +116,7 @@ SIGNATURES = {
     "voxq_version": ([], C.c_char_p),
     "voxq_set_device": ([_i], _i),
     "voxq_device_error": ([_i], _i),
+    "voxq_matmul_traffic": ([C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), _i], None),
     "voxq_selftest_wait_timeout": ([_i], _i),
     "voxq_quant_bytes": ([_sz, _i], _sz),
     "voxq_quantize": ([_vp, _sz, _i, _vp, _vp], _i),
