@@ -226,12 +226,10 @@ def run_ours(args, torch, dist, rank, world, local_rank):
                     "q8_c3": measure_abi_calls(torch, voxq, "q8", shapes, 40),
                 }
             configs["reference_gpu"] = measure_ref_gpu(args)
-            try:
-                configs["c4"] = measure_c4(args.c4_patches)
-            except Exception as e:  # the engine run is reported, never fatal to the headline line
-                configs["c4"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
         if args.cpu_seconds > 0:
             cpu = cpu_baseline(args.cpu_seconds, threads=1)
+    if args.configs:
+        configs.update(engine_configs(args, dist, rank, world, local_rank))
 
     # the single-row launch runs the tensor-path GEMV unless VOXQ_GEMV_MMA=0
     mma = os.environ.get("VOXQ_GEMV_MMA", "1")[:1] != "0"
@@ -882,7 +880,64 @@ def _engine_run(exe, model, patches, env_extra, extra_args=()):
     return d
 
 
-def measure_c4(patches=4, workdir=None, cpu_patches=0):
+def _make_model(base=None):
+    """Writes the seeded random-init model (make_model, seed 1) into a new folder under `base`;
+    returns (folder, model path, make_model's summary) or raises."""
+    import shutil
+    import tempfile
+    base = base or os.environ.get("VOXQ_MODEL_DIR") or tempfile.gettempdir()
+    if shutil.disk_usage(base).free < 12e9:
+        raise RuntimeError(f"less than 12 GB free in {base} for the 5 GB model")
+    work = tempfile.mkdtemp(prefix="voxq_model_", dir=base)
+    t0 = time.perf_counter()
+    gen = json.loads(subprocess.run([os.path.join(ENGINE_BUILD, "make_model"), os.path.join(work, "rand"),
+                                     "--seed", "1"], check=True, capture_output=True,
+                                    text=True).stdout.strip().splitlines()[-1])
+    gen["gen_s"] = round(time.perf_counter() - t0, 1)
+    return work, os.path.join(work, "rand.vxcpm"), gen
+
+
+C5_UTTERANCES_PER_GPU, C5_PATCHES = 16, 4
+
+
+def measure_c5(model, gpu, utterances, workers_per_gpu):
+    """BASELINE config 5 slice: independent utterances (token counts uniform in
+    [32, 128], seeded ids), Q4, each synthesised by the unchanged engine on
+    libvoxq; `workers_per_gpu` engine processes per GPU, utterances placed by
+    LPT (voxq.serve).  Returns the serving summary without per-utterance rows."""
+    sys.path.insert(0, os.path.join(REPO, "voxcpm2-c_b200"))
+    from voxq import serve as S
+    cmd = [os.path.join(ENGINE_BUILD, "voxq_engine_run_gpu"), "--model", model, "--gpu", "--serve",
+           "--ralm-max-seq", "4096"]
+    est = max(30.0, 4.0 * (1.0 + 0.6 * max(u["patches"] for u in utterances)))
+    r = S.serve(cmd, utterances, gpus=[gpu], workers_per_gpu=workers_per_gpu,
+                env=dict(os.environ, VOXCPM_QUANT="q4"), deadline_s=est)
+    res = r.pop("results")
+    r["patches"] = sum(int(x["patches"]) for x in res if "error" not in x)
+    r["weight_bytes"] = sum(int(x.get("weight_bytes", 0)) for x in res if "error" not in x)
+    r["weight_bytes_per_patch"] = round(r["weight_bytes"] / max(1, r["patches"]))
+    r["generate_s_per_utterance"] = [round(float(x["generate_s"]), 3) for x in res if "error" not in x]
+    return r
+
+
+def c5_cpu_estimate(patches):
+    """The reference CPU path's utterances/s for the C5 slice, estimated from the committed
+    CPU engine run (tests/golden/engine_c4_q8.json, one host thread, 64 tokens): one process per
+    core, 8 processes, prefill + patches x per-patch time; not measured on the GPU host."""
+    if not os.path.exists(ENGINE_GOLDEN):
+        return None
+    g = json.load(open(ENGINE_GOLDEN))
+    c = g["cpu_run"]
+    pre = c["stages"]["tslm_forward"]["s"]
+    per_patch = (c["generate_s"] - pre) / c["patches"]
+    t_utt = pre + patches * per_patch
+    return {"utt_per_s": round(8 / t_utt, 5), "processes": 8, "s_per_utterance": round(t_utt, 1),
+            "basis": f"CPU engine run on the build host ({g.get('cpu', '?')}), 1 thread, 64 tokens, "
+                     f"{c['patches']} patches: prefill {pre:.1f} s + {per_patch:.1f} s per patch; 8 processes "
+                     "assumed to scale perfectly"}
+
+
+def measure_c4(patches=4, workdir=None, cpu_patches=0, model=None):
     """one utterance through the unchanged reference engine
     (src/*.c compiled as they are) on the seeded random-init model: 64 token
     ids, `patches` patches (4 frames each), 10 Euler steps, CFG 2.0.  Three
@@ -892,24 +947,22 @@ def measure_c4(patches=4, workdir=None, cpu_patches=0):
     path, one host thread).  RTF = wall time of voxcpm_generate / audio
     seconds; per-stage times from the harness (voxq_engine_run.c)."""
     import shutil
-    import tempfile
     for exe in ("make_model", "voxq_engine_run_gpu"):
         if not os.path.exists(os.path.join(ENGINE_BUILD, exe)):
             return {"unavailable": f"{exe} not built (make -C voxcpm2-c_b200/engine REF=<reference checkout>)"}
-    base = workdir or os.environ.get("VOXQ_MODEL_DIR") or tempfile.gettempdir()
-    if shutil.disk_usage(base).free < 12e9:
-        return {"unavailable": f"less than 12 GB free in {base} for the 5 GB model"}
-    work = tempfile.mkdtemp(prefix="voxq_c4_", dir=base)
+    work = None
     try:
-        t0 = time.perf_counter()
-        gen = json.loads(subprocess.run([os.path.join(ENGINE_BUILD, "make_model"), os.path.join(work, "rand"),
-                                         "--seed", "1"], check=True, capture_output=True,
-                                        text=True).stdout.strip().splitlines()[-1])
-        gen_s = time.perf_counter() - t0
-        model = os.path.join(work, "rand.vxcpm")
+        if model is None:
+            try:
+                work, model, gen = _make_model(workdir)
+            except RuntimeError as e:
+                return {"unavailable": str(e)}
+        else:
+            gen = model[1]
+            model = model[0]
         out = {"workload": f"BASELINE config 4 slice: unchanged engine, 64 token ids, {patches} patches, "
                            "10 Euler steps, CFG 2.0, random-init model (Q8-exact projection weights)",
-               "model_gen_s": round(gen_s, 1), "model_bytes": gen["model_bytes"] + gen["audiovae_bytes"]}
+               "model_gen_s": gen["gen_s"], "model_bytes": gen["model_bytes"] + gen["audiovae_bytes"]}
         out["ours"] = _engine_run("voxq_engine_run_gpu", model, patches, {"VOXCPM_QUANT": "q8"}, ["--gpu"])
         if os.path.exists(os.path.join(ENGINE_BUILD, "voxq_engine_run_refgpu")):
             out["reference_gpu"] = _engine_run("voxq_engine_run_refgpu", model, patches, {}, ["--gpu"])
@@ -923,7 +976,87 @@ def measure_c4(patches=4, workdir=None, cpu_patches=0):
             out["reference_cpu"] = c
         return out
     finally:
-        shutil.rmtree(work, ignore_errors=True)
+        if work:
+            shutil.rmtree(work, ignore_errors=True)
+
+
+def engine_configs(args, dist, rank, world, local_rank):
+    """Configs 4 and 5 on the unchanged engine.  One model file for both (rank 0 writes it;
+    under torchrun the others use the same file).  C4 (one utterance) on 1 GPU only; C5 on every
+    rank: 16 utterances per GPU (weak scaling), LPT-partitioned over the ranks, each rank's share
+    served by its own engine workers; the aggregate is all answers over the slowest rank's time.
+    Never fatal to the headline line: failures are reported as `unavailable`."""
+    import shutil
+    sys.path.insert(0, os.path.join(REPO, "voxcpm2-c_b200"))
+    from voxq import serve as S
+    from voxq.parallel import lpt_partition
+    out = {}
+    if not all(os.path.exists(os.path.join(ENGINE_BUILD, e)) for e in ("make_model", "voxq_engine_run_gpu")):
+        return {"c5": {"unavailable": "engine not built (make -C voxcpm2-c_b200/engine REF=<reference checkout>)"}}
+    made = [None]
+    if rank == 0:
+        try:
+            made = [_make_model()]
+        except Exception as e:  # reported, never fatal
+            made = [f"{type(e).__name__}: {e}"[:300]]
+    if world > 1:
+        dist.broadcast_object_list(made, src=0)
+    if isinstance(made[0], str) or made[0] is None:
+        return {"c5": {"unavailable": made[0] or "model not written"}}
+    work, model, gen = made[0]
+    try:
+        if world == 1:
+            try:
+                out["c4"] = measure_c4(args.c4_patches, model=(model, gen))
+            except Exception as e:
+                out["c4"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+        utts = S.workload(C5_UTTERANCES_PER_GPU * world, patches=C5_PATCHES, seed=5)
+        mine = [utts[i] for i in lpt_partition([S.cost(u) for u in utts], world)[rank]]
+        wpg = max(1, min(4, (os.cpu_count() or 8) // (2 * world)))
+        try:
+            res = measure_c5(model, local_rank, mine, wpg)
+        except Exception as e:
+            res = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+        allres = [res]
+        if world > 1:
+            allres = [None] * world
+            dist.all_gather_object(allres, res)
+        if rank == 0:
+            bad = [r for r in allres if "unavailable" in r]
+            if bad:
+                out["c5"] = {"unavailable": bad[0]["unavailable"]}
+            else:
+                wall = max(r["wall_s"] for r in allres)
+                answered = sum(r["answered"] for r in allres)
+                wb = sum(r["weight_bytes"] for r in allres)
+                per_gpu = {}
+                for r in allres:
+                    per_gpu.update(r["per_gpu"])
+                out["c5"] = {
+                    "metric": "c5_utterances_per_s", "value": round(answered / wall, 4), "unit": "utt/s",
+                    "workload": f"BASELINE config 5 slice: {len(utts)} utterances ({C5_UTTERANCES_PER_GPU} per GPU, "
+                                f"token counts uniform in [32, 128], seeded ids), {C5_PATCHES} patches each, Q4, "
+                                "unchanged engine on libvoxq, LPT over GPUs and engine workers",
+                    "scaling": "weak", "n_gpus": world, "workers_per_gpu": wpg, "answered": answered,
+                    "wall_s_max": wall, "per_rank_wall_s": [r["wall_s"] for r in allres],
+                    "GBps_per_gpu": {g: v["GBps"] for g, v in per_gpu.items()},
+                    "weight_bytes_per_patch": allres[0]["weight_bytes_per_patch"],
+                    "rtf_aggregate": round(wall / sum(r["audio_s"] for r in allres), 4),
+                    "load_s_max": max(r["load_s"] for r in allres),
+                    "dead_workers": sum(len(r["dead_workers"]) for r in allres),
+                    "weight_bytes": wb,
+                    "cpu_estimate": c5_cpu_estimate(C5_PATCHES),
+                    "per_rank": [{k: r[k] for k in ("answered", "wall_s", "utt_per_s", "load_s", "per_gpu")}
+                                 for r in allres] if world > 1 else None,
+                }
+                if world == 1:
+                    out["c5"]["generate_s_per_utterance"] = allres[0]["generate_s_per_utterance"]
+    finally:
+        if world > 1:
+            dist.barrier()
+        if rank == 0:
+            shutil.rmtree(work, ignore_errors=True)
+    return out
 
 
 def run_c4(args):
