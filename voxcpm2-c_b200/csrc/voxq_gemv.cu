@@ -220,7 +220,7 @@ struct GemvParams {
     int32_t count;
     int32_t total_tiles;
     int32_t limb_bytes;  // tensor-path kernel: largest item's limb record (shared-memory buffer)
-    int32_t pad;
+    int32_t first_weight;  // tensor-path kernel: per-mille share weight of the grid's first half (1000: even)
     int* err;
     GemvItemDev it[MAXI];
 };
@@ -729,8 +729,16 @@ __global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const
     mbar_fence_init();
     __syncthreads();
 
-    const int tb = (int)((int64_t)p.total_tiles * blockIdx.x / gridDim.x);
-    const int te = (int)((int64_t)p.total_tiles * (blockIdx.x + 1) / gridDim.x);
+    // Contiguous tile ranges, the first half of the grid weighted by
+    // first_weight / 1000 against the second: with two CTAs per SM the block
+    // scheduler gives every SM one CTA of each half, and the SM's first CTA
+    // gets more issue slots than its second, so equal ranges would leave the
+    // second CTA running alone at the end.
+    const int64_t H = gridDim.x / 2, w1 = p.first_weight, w2 = 1000;
+    const int64_t wsum = H * w1 + ((int64_t)gridDim.x - H) * w2;
+    auto wpos = [&](int64_t b) { return b <= H ? b * w1 : H * w1 + (b - H) * w2; };
+    const int tb = (int)((int64_t)p.total_tiles * wpos(blockIdx.x) / wsum);
+    const int te = (int)((int64_t)p.total_tiles * wpos(blockIdx.x + 1) / wsum);
 
     if (warp == kMmaWarps) {
         if (lane == 0) produce_split(p, tb, te, full, empty, smem);
@@ -948,7 +956,7 @@ static VoxCPMError launch_t(const GemvParams<MAXI>& p, cudaStream_t st) {
 }
 
 template <int QT, bool SIGNED, bool TRX, int MAXI>
-static VoxCPMError launch_mma_t(const GemvParams<MAXI>& p, cudaStream_t st) {
+static VoxCPMError launch_mma_t(GemvParams<MAXI>& p, cudaStream_t st) {
     auto kern = gemv_mma_kernel<QT, SIGNED, TRX, MAXI>;
     // occupancy for each limb-buffer size, in 1 KB steps
     static int occ[kMmaLimbMax / 1024 + 1] = {};
@@ -961,6 +969,16 @@ static VoxCPMError launch_mma_t(const GemvParams<MAXI>& p, cudaStream_t st) {
     if (occ[lk] == 0) cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ[lk], kern, (kMmaWarps + 1) * 32, smem);
     const int cap = device_sm_count() * (occ[lk] > 0 ? occ[lk] : 1);
     const int blocks = p.total_tiles < cap ? p.total_tiles : cap;
+    // Weighted ranges only when the grid is two full CTAs per SM (one CTA of
+    // each half on every SM); otherwise even ranges.  1.2 : 1 measured best on
+    // a B200 for the config-2 step (1.0: 56.8 us, 1.15: 55.3, 1.2: 54.7, 1.25:
+    // 54.3, 1.3: 57.2); VOXQ_GEMV_FIRST_WEIGHT (per mille) overrides.
+    static const int weight = [] {
+        const char* e = getenv("VOXQ_GEMV_FIRST_WEIGHT");
+        const int v = e ? atoi(e) : 1200;
+        return v >= 500 && v <= 3000 ? v : 1200;
+    }();
+    p.first_weight = (occ[lk] == 2 && blocks == cap) ? weight : 1000;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks < 1 ? 1 : blocks);
     cfg.blockDim = dim3((kMmaWarps + 1) * 32);
@@ -995,7 +1013,7 @@ static bool mma_item(const voxq_gemv_item& x) {
 }
 
 template <int MAXI>
-static VoxCPMError dispatch(const GemvParams<MAXI>& p, int qtype, int mt, bool swi, bool sgn, bool mma,
+static VoxCPMError dispatch(GemvParams<MAXI>& p, int qtype, int mt, bool swi, bool sgn, bool mma,
                             cudaStream_t st) {
     if (mma) {
         if (qtype == VOXQ_Q4) {
