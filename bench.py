@@ -964,6 +964,10 @@ def measure_c4(patches=4, workdir=None, cpu_patches=0, model=None):
                            "10 Euler steps, CFG 2.0, random-init model (Q8-exact projection weights)",
                "model_gen_s": gen["gen_s"], "model_bytes": gen["model_bytes"] + gen["audiovae_bytes"]}
         out["ours"] = _engine_run("voxq_engine_run_gpu", model, patches, {"VOXCPM_QUANT": "q8"}, ["--gpu"])
+        # the same build with the transformer blocks left to the engine's host code
+        # (only their projections on the device), for comparison
+        out["ours_blocks_on_host"] = _engine_run("voxq_engine_run_gpu", model, patches,
+                                                 {"VOXCPM_QUANT": "q8", "VOXQ_ENGINE_BLOCK": "cpu"}, ["--gpu"])
         if os.path.exists(os.path.join(ENGINE_BUILD, "voxq_engine_run_refgpu")):
             out["reference_gpu"] = _engine_run("voxq_engine_run_refgpu", model, patches, {}, ["--gpu"])
         if cpu_patches > 0:

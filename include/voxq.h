@@ -314,6 +314,69 @@ VOXQ_API VoxCPMError voxq_conv1d_transpose_forward(const voxq_conv1d_transpose_d
  * counterpart in the reference). */
 VOXQ_API void voxq_conv_cache_clear(void);
 
+/* ---- Transformer block on the device -------------------------------------
+ * transformer_block_forward (src/nn.c:579-700) with every step on the device:
+ *   h   = x + Attention(RMSNorm_attn(x))
+ *   out = h + SwiGLU(RMSNorm_ffn(h))
+ * where RMSNorm (src/tensor.c:811-849) is x / sqrt(mean(x^2) + eps) * weight
+ * (sum of squares in double, NaN counted as 0), Attention is
+ * attention_forward (src/nn.c:208-530: Q/K/V projections, RoPE
+ * tensor_rotary_emb (src/tensor.c:883-950) at positions pos.. when freqs_cis
+ * is given, K/V written into the cache at [pos, pos + seq), scores
+ * q.k / sqrt(head_dim) + mask[s][t], softmax with 1 / (sum + 1e-10)
+ * (src/tensor.c:710-752), GQA head h reading kv head h / (n_heads /
+ * n_kv_heads), output projection) and SwiGLU is swiglu_forward
+ * (src/nn.c:100-170: silu(x W1^T) * (x W3^T), then W2).  The residual adds
+ * and SiLU-gating are fused into the projections' epilogues.
+ *
+ * Descriptors have the layouts of the engine's TransformerBlock, RmsNorm,
+ * Attention and SwiGLU (include/nn.h:26-29, 58-64, 79-89, 136-141).  x, out
+ * [batch, seq, d_model], the caches [batch, n_kv_heads, max_seq, head_dim],
+ * mask [rows, cols] and freqs_cis [positions, head_dim / 2, 2] are host
+ * tensors; the projection weights must be device weights quantized by
+ * tensor_to_cuda (VOXCPM_QUANT=q8|q4) and the norm weights host tensors
+ * (uploaded on first use and kept, keyed by pointer and a fingerprint).  The
+ * caches are mirrored on the device per cache pointer (rows [0, pos) are
+ * re-read from the host when the mirror cannot vouch for them: first use,
+ * pos == 0 restarts, or a host row that no longer matches) and the new rows
+ * are also written back to the host cache, so the engine's own state stays
+ * exact.  out is valid on return.  Returns VOXCPM_ERR_CUDA_NOT_FOUND (the
+ * caller then runs its host code) when the library is not initialised, a
+ * weight is not a quantized device weight, an operand is already on the
+ * device, or a shape is outside what the kernels take (head_dim a multiple
+ * of 4 up to 256, cache positions up to 32768); the reference's own shape
+ * errors are left to that host path. */
+typedef struct {
+    Tensor* weight;  /* [d_model] */
+    float eps;
+} voxq_rmsnorm_desc;
+typedef struct {
+    Tensor* wq;  /* [n_heads * head_dim, d_model] */
+    Tensor* wk;  /* [n_kv_heads * head_dim, d_model] */
+    Tensor* wv;
+    Tensor* wo;  /* [d_model, n_heads * head_dim] */
+    int d_model, n_heads, n_kv_heads, head_dim;
+} voxq_attention_desc;
+typedef struct {
+    Tensor* w1;  /* gate [d_ff, d_model] */
+    Tensor* w2;  /* down [d_model, d_ff] */
+    Tensor* w3;  /* up   [d_ff, d_model] */
+    int d_model, d_ff;
+} voxq_swiglu_desc;
+typedef struct {
+    voxq_rmsnorm_desc* rms_attn;
+    voxq_attention_desc* attn;
+    voxq_rmsnorm_desc* rms_ffn;
+    voxq_swiglu_desc* ffn;
+} voxq_block_desc;
+
+/* src/nn.c:579-700 (transformer_block_forward). */
+VOXQ_API VoxCPMError voxq_transformer_block_forward(const voxq_block_desc* block, const Tensor* x, Tensor* cache_k,
+                                                    Tensor* cache_v, const Tensor* mask, const Tensor* freqs_cis,
+                                                    int pos, Tensor* out);
+/* Drops the blocks' device cache mirrors, norm weights and staging. */
+VOXQ_API void voxq_block_cache_clear(void);
+
 /* ---- quantize.py weight containers (VXCPM2) ---------------------------
  * Reads the container written by the reference's quantizer
  * (scripts/quantize.py:110-312): a 256-byte header, the layer-group offset

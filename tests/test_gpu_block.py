@@ -1,0 +1,234 @@
+"""The engine's transformer block on the device (voxq_transformer_block_forward).
+
+Oracle: a float64 numpy restatement of transformer_block_forward
+(src/nn.c:579-700) and what it calls: RMSNorm (src/tensor.c:811-849),
+attention_forward (src/nn.c:208-530) with RoPE (src/tensor.c:883-950), the
+KV-cache write, the additive mask and softmax (src/tensor.c:710-752), and
+swiglu_forward (src/nn.c:100-170).  The projection weights are exactly
+representable in the tested format (every 32-weight block holds its format's
+lowest and highest code on a power-of-two grid), so quantization at upload is
+the identity and the oracle multiplies by the same weights.
+
+Cases follow how the engine calls the block: a DiT-style call that fills a
+fresh cache (pos 0, seq = cache length, no mask, no RoPE); a causal prefill
+into a longer cache with RoPE; single-token decode steps that read the rows
+earlier calls wrote (the device mirror); a host cache changed behind the
+library's back (the mirror must notice and re-read it); a restart at pos 0 on
+the same cache; batch rows both below (GEMV) and above (GEMM) 8.  Checked:
+the block output and the cache rows written back to the host.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+import voxq
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3  # |out - ref| <= TOL * (|ref| + rms(ref))
+
+
+def exact_weight(rng, n, k, qname):
+    """[n, k] weights on the format's grid with every 32-block spanning its full code range."""
+    if qname == "q8":
+        q = rng.integers(0, 256, size=(n, k))
+        q[:, 0::32], q[:, 1::32] = 0, 255
+        return ((q - 128) * 2.0 ** -11).astype(np.float32)
+    q = rng.integers(0, 16, size=(n, k))
+    q[:, 0::32], q[:, 1::32] = 0, 15
+    return ((q - 8) * 2.0 ** -7).astype(np.float32)
+
+
+def rmsnorm(x, w, eps):
+    d = x.shape[-1]
+    ss = (np.where(np.isnan(x), 0.0, x).astype(np.float64) ** 2).sum(-1, keepdims=True)
+    return x.astype(np.float64) / np.sqrt(ss / d + eps) * w
+
+
+def rope(t, freqs, pos):
+    """t [B, heads, S, hd]; freqs [positions, hd/2, 2] (cos, sin)."""
+    half = t.shape[-1] // 2
+    S = t.shape[2]
+    c = freqs[pos:pos + S, :, 0][None, None]
+    s = freqs[pos:pos + S, :, 1][None, None]
+    x0, x1 = t[..., :half], t[..., half:]
+    return np.concatenate([x0 * c - x1 * s, x0 * s + x1 * c], axis=-1)
+
+
+def block_ref(x, W, ck, cv, mask, freqs, pos, H, KVH, hd, eps):
+    """Returns out and updates the float64 caches ck, cv [B, KVH, max_seq, hd] in place."""
+    B, S, D = x.shape
+    n = rmsnorm(x, W["n1"], eps)
+    q = (n @ W["wq"].T).reshape(B, S, H, hd).transpose(0, 2, 1, 3)
+    k = (n @ W["wk"].T).reshape(B, S, KVH, hd).transpose(0, 2, 1, 3)
+    v = (n @ W["wv"].T).reshape(B, S, KVH, hd).transpose(0, 2, 1, 3)
+    if freqs is not None:
+        q, k = rope(q, freqs, pos), rope(k, freqs, pos)
+    ck[:, :, pos:pos + S] = k
+    cv[:, :, pos:pos + S] = v
+    L = pos + S
+    kk = np.repeat(ck[:, :, :L], H // KVH, axis=1)
+    vv = np.repeat(cv[:, :, :L], H // KVH, axis=1)
+    sc = q @ kk.transpose(0, 1, 3, 2) / np.sqrt(hd)
+    if mask is not None:
+        r, c = min(mask.shape[0], S), min(mask.shape[1], L)
+        sc[:, :, :r, :c] += mask[:r, :c]
+    sc = sc - sc.max(-1, keepdims=True)
+    p = np.exp(sc)
+    p = p / (p.sum(-1, keepdims=True) + 1e-10)
+    a = (p @ vv).transpose(0, 2, 1, 3).reshape(B, S, H * hd)
+    h = x + a @ W["wo"].T
+    n2 = rmsnorm(h, W["n2"], eps)
+    g = n2 @ W["w1"].T
+    g = g / (1.0 + np.exp(-g)) * (n2 @ W["w3"].T)
+    return h + g @ W["w2"].T
+
+
+def close(got, ref, what):
+    ref = np.asarray(ref, dtype=np.float64)
+    scale = np.sqrt((ref ** 2).mean()) + np.abs(ref)
+    err = np.abs(got.astype(np.float64) - ref)
+    bad = err > TOL * scale
+    assert np.isfinite(got).all(), what
+    assert not bad.any(), f"{what}: {int(bad.sum())} of {bad.size} beyond tol; worst {float((err / scale).max()):.2e}"
+    return float((err / scale).max())
+
+
+def as_array(t):
+    """Writable numpy view of a host fp32 Tensor's data."""
+    c = t.contents
+    shape = tuple(c.shape[i] for i in range(c.ndim))
+    return np.ctypeslib.as_array(c.data, shape=(int(c.size),)).reshape(shape)
+
+
+def causal(S, L):
+    vis = (L - S) + np.arange(S)[:, None]
+    return np.where(np.arange(L)[None, :] <= vis, 0.0, -np.inf).astype(np.float32)
+
+
+@pytest.mark.parametrize("qname", ["q8", "q4"])
+def test_block_on_device_matches_reference(qname):
+    L = voxq.lib()
+    os.environ["VOXCPM_QUANT"] = qname
+    L.tensor_cuda_shutdown()
+    assert L.tensor_cuda_init() == 0
+    rng = np.random.default_rng(11)
+    B, D, H, KVH, hd, F, eps = 1, 256, 4, 2, 64, 512, 1e-6
+    W = {"wq": exact_weight(rng, H * hd, D, qname), "wk": exact_weight(rng, KVH * hd, D, qname),
+         "wv": exact_weight(rng, KVH * hd, D, qname), "wo": exact_weight(rng, D, H * hd, qname),
+         "w1": exact_weight(rng, F, D, qname), "w2": exact_weight(rng, D, F, qname),
+         "w3": exact_weight(rng, F, D, qname),
+         "n1": (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32),
+         "n2": (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32)}
+    keep = []
+    try:
+        T = {k: voxq.host_tensor(W[k]) for k in W}
+        keep += list(T.values())
+        for k in ("wq", "wk", "wv", "wo", "w1", "w2", "w3"):
+            voxq.check(L.tensor_to_cuda(T[k]), "tensor_to_cuda")
+        n1 = voxq.RmsNormDesc(T["n1"], eps)
+        n2 = voxq.RmsNormDesc(T["n2"], eps)
+        at = voxq.AttentionDesc(T["wq"], T["wk"], T["wv"], T["wo"], D, H, KVH, hd)
+        ff = voxq.SwigluDesc(T["w1"], T["w2"], T["w3"], D, F)
+        bd = voxq.BlockDesc(C.pointer(n1), C.pointer(at), C.pointer(n2), C.pointer(ff))
+        positions = 64
+        inv = 10000.0 ** (-np.arange(hd // 2) * 2.0 / hd)
+        ang = np.arange(positions)[:, None] * inv[None, :]
+        freqs_np = np.stack([np.cos(ang), np.sin(ang)], -1).astype(np.float32)
+        freqs = voxq.host_tensor(freqs_np)
+        keep.append(freqs)
+
+        def run(S, pos, ck, cv, ref_ck, ref_cv, use_mask, use_freqs, what):
+            x_np = rng.standard_normal((B, S, D)).astype(np.float32)
+            x, out = voxq.host_tensor(x_np), voxq.host_tensor(np.zeros((B, S, D), np.float32))
+            mask_np = causal(S, pos + S) if use_mask else None
+            mask = voxq.host_tensor(mask_np) if use_mask else None
+            try:
+                r = L.voxq_transformer_block_forward(C.byref(bd), x, ck, cv, mask, freqs if use_freqs else None,
+                                                     pos, out)
+                assert r == 0, f"{what}: error {r}"
+                got = voxq.host_tensor_view(out)
+            finally:
+                for t in (x, out) + ((mask,) if use_mask else ()):
+                    voxq.free_tensor(t)
+            ref = block_ref(x_np, W, ref_ck, ref_cv, mask_np, freqs_np if use_freqs else None, pos, H, KVH, hd, eps)
+            e = close(got, ref, what)
+            e2 = close(as_array(ck)[:, :, pos:pos + S], ref_ck[:, :, pos:pos + S], what + " (cache K rows)")
+            close(as_array(cv)[:, :, pos:pos + S], ref_cv[:, :, pos:pos + S], what + " (cache V rows)")
+            return e, e2
+
+        def cache(max_seq):
+            ck = voxq.host_tensor(np.zeros((B, KVH, max_seq, hd), np.float32))
+            cv = voxq.host_tensor(np.zeros((B, KVH, max_seq, hd), np.float32))
+            keep.extend([ck, cv])
+            return ck, cv, np.zeros((B, KVH, max_seq, hd)), np.zeros((B, KVH, max_seq, hd))
+
+        # DiT-style: a fresh cache filled whole, no mask, no RoPE (GEMV and GEMM projections)
+        for S in (5, 9):
+            ck, cv, rk, rv = cache(S)
+            run(S, 0, ck, cv, rk, rv, False, False, f"fill S={S}")
+        # prefill with a causal mask and RoPE into a longer cache, then decode steps
+        ck, cv, rk, rv = cache(48)
+        run(16, 0, ck, cv, rk, rv, True, True, "prefill S=16")
+        for pos in (16, 17, 18):
+            run(1, pos, ck, cv, rk, rv, False, True, f"decode pos={pos}")
+        # the host cache changed behind the library: the mirror must re-read it
+        hk = as_array(ck)
+        hk[0, 0, 18, :] += 0.5
+        rk[0, 0, 18, :] = hk[0, 0, 18, :]
+        hk[0, 1, 3, :] -= 0.25  # a row the last-row check alone would miss is re-read with it
+        rk[0, 1, 3, :] = hk[0, 1, 3, :]
+        run(1, 19, ck, cv, rk, rv, False, True, "decode after host change")
+        # a two-token continuation with its causal mask
+        run(2, 20, ck, cv, rk, rv, True, True, "continuation S=2")
+        # restart at pos 0 on the same cache
+        rk[:] = 0.0
+        rv[:] = 0.0
+        run(3, 0, ck, cv, rk, rv, True, True, "restart S=3")
+        assert voxq.lib().voxq_device_error(1) == 0
+    finally:
+        for t in keep:
+            voxq.free_tensor(t)
+        L.voxq_block_cache_clear()
+        L.tensor_cuda_shutdown()
+        os.environ.pop("VOXCPM_QUANT", None)
+
+
+def test_block_declines_what_it_does_not_take():
+    """Unquantized weights, device operands or an uninitialised library: VOXCPM_ERR_CUDA_NOT_FOUND,
+    so the engine runs its own host code."""
+    L = voxq.lib()
+    os.environ.pop("VOXCPM_QUANT", None)
+    L.tensor_cuda_shutdown()
+    assert L.tensor_cuda_init() == 0
+    D, H, KVH, hd, F = 64, 2, 1, 32, 128
+    rng = np.random.default_rng(3)
+    keep = []
+    try:
+        T = {k: voxq.host_tensor(rng.standard_normal(s).astype(np.float32) * 0.05) for k, s in
+             (("wq", (H * hd, D)), ("wk", (KVH * hd, D)), ("wv", (KVH * hd, D)), ("wo", (D, H * hd)),
+              ("w1", (F, D)), ("w2", (D, F)), ("w3", (F, D)), ("n1", (D,)), ("n2", (D,)))}
+        keep += list(T.values())
+        for k in ("wq", "wk", "wv", "wo", "w1", "w2", "w3"):
+            voxq.check(L.tensor_to_cuda(T[k]), "tensor_to_cuda")  # dense fp32 device weights
+        n1, n2 = voxq.RmsNormDesc(T["n1"], 1e-6), voxq.RmsNormDesc(T["n2"], 1e-6)
+        at = voxq.AttentionDesc(T["wq"], T["wk"], T["wv"], T["wo"], D, H, KVH, hd)
+        ff = voxq.SwigluDesc(T["w1"], T["w2"], T["w3"], D, F)
+        bd = voxq.BlockDesc(C.pointer(n1), C.pointer(at), C.pointer(n2), C.pointer(ff))
+        x = voxq.host_tensor(np.zeros((1, 3, D), np.float32))
+        out = voxq.host_tensor(np.zeros((1, 3, D), np.float32))
+        ck = voxq.host_tensor(np.zeros((1, KVH, 3, hd), np.float32))
+        cv = voxq.host_tensor(np.zeros((1, KVH, 3, hd), np.float32))
+        keep += [x, out, ck, cv]
+        assert L.voxq_transformer_block_forward(C.byref(bd), x, ck, cv, None, None, 0, out) == voxq.CUDA_NOT_FOUND
+        L.tensor_cuda_shutdown()
+        assert L.voxq_transformer_block_forward(C.byref(bd), x, ck, cv, None, None, 0, out) == voxq.CUDA_NOT_FOUND
+    finally:
+        L.tensor_cuda_init()
+        for t in keep:
+            voxq.free_tensor(t)
+        L.tensor_cuda_shutdown()

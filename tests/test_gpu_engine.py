@@ -9,10 +9,12 @@ and runs voxcpm_generate (src/model.c:630-1048): TSLM and RALM prefill over 64
 token ids, then per patch the LocDiT sampler (10 Euler steps, CFG 2.0), the
 AudioVAE decode and the LocEnc -> fusion -> RALM update.
 
-The libvoxq build also sends the AudioVAE decoder's convolutions
-(conv1d_forward / conv1d_transpose_forward, src/nn.c:765-931), which the
-reference runs on the host even in its GPU build, to libvoxq's device
-convolutions.
+The libvoxq build also sends every transformer block
+(transformer_block_forward, src/nn.c:579-700: norms, attention with its KV
+cache, SwiGLU, residuals) to libvoxq's device block, and the AudioVAE
+decoder's convolutions (conv1d_forward / conv1d_transpose_forward,
+src/nn.c:765-931), which the reference runs on the host even in its GPU
+build, to libvoxq's device convolutions.
 
 Oracle: the same engine built without VOXCPM_CUDA (the reference CPU path, one
 scalar loop per output, src/tensor.c:617-678, and the host convolutions) on the
@@ -94,9 +96,11 @@ def test_unchanged_engine_on_libvoxq_matches_cpu_engine():
     finally:
         shutil.rmtree(work, ignore_errors=True)
     assert run["build"] == "gpu" and run["vae"] == "gpu"
+    # every transformer block (TSLM, RALM, LocDiT, LocEnc) ran on the device
+    assert run["blocks"]["device"] > 0 and run["blocks"]["host"] == 0, run["blocks"]
     mm = run["stages"]["tensor_matmul_nt"]
-    assert mm["calls"] == meta["cpu_run"]["stages"]["tensor_matmul_nt"]["calls"]
-    # the projections ran on the device: the CPU loop takes ~80 ms per call here
+    # the projections outside the blocks ran on the device: the CPU loop takes ~80 ms per call here
+    assert 0 < mm["calls"] < meta["cpu_run"]["stages"]["tensor_matmul_nt"]["calls"]
     assert mm["s"] / mm["calls"] < 2e-3, f"{mm['s'] / mm['calls'] * 1e3:.2f} ms per tensor_matmul_nt"
     err = np.abs(got.astype(np.float64) - want)
     assert np.isfinite(got).all()

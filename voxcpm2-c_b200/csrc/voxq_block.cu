@@ -1,0 +1,586 @@
+// voxq_block.cu -- the engine's transformer block (src/nn.c:579-700) on the device.
+//
+// The reference runs everything of a block but its projections on one host
+// thread: RMSNorm, the attention (per-head permutes, RoPE, the KV-cache copy,
+// scores, softmax, the weighted sum), SiLU gating and the residual adds, with
+// a synchronous host <-> device round trip per projection.  Here one call
+// uploads the block input once, runs
+//
+//   n   = RMSNorm(x)                      rmsnorm_kernel
+//   q, k, v = n Wq^T, n Wk^T, n Wv^T      one grouped GEMV launch (M <= 8) or three GEMMs
+//   RoPE(q, k); k, v -> cache[pos ..]     rope_cache_kernel
+//   a   = softmax(q k^T / sqrt(d) + mask) v   attn_kernel (one CTA per query row and head)
+//   h   = x + a Wo^T                      projection with the residual epilogue
+//   n2  = RMSNorm(h)
+//   g   = silu(n2 W1^T) * (n2 W3^T)       projection with the SwiGLU epilogue
+//   out = h + g W2^T                      projection with the residual epilogue
+//
+// and downloads the output and the new cache rows once, with one wait.  The
+// KV cache is mirrored on the device per host cache pointer; the host cache is
+// kept identical (new rows written back), so a call that falls back to the
+// host code, or any other reader of the cache, sees the reference's state.
+#include <math.h>
+#include <string.h>
+
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "voxq_common.cuh"
+#include "voxq_internal.h"
+
+namespace voxq {
+
+constexpr int kBlockThreads = 256;
+constexpr int kAttnThreads = 128;
+constexpr int kMaxCacheLen = 32768;  // score row in shared memory (128 KB)
+constexpr int kMaxHeadDim = 256;
+
+// RMSNorm of one row per CTA: sum of squares in double (NaN counted as 0),
+// rms = sqrt(sum / D + eps) in double, out = (float)(x * (1 / rms)) * w.
+__global__ void __launch_bounds__(kBlockThreads) rmsnorm_kernel(const float* __restrict__ x,
+                                                                const float* __restrict__ w, float eps,
+                                                                float* __restrict__ out, int D) {
+    __shared__ double red[kBlockThreads / 32];
+    const float* xr = x + (int64_t)blockIdx.x * D;
+    double s = 0.0;
+    for (int d = threadIdx.x; d < D; d += kBlockThreads) {
+        float v = xr[d];
+        if (isnan(v)) v = 0.0f;
+        s += (double)v * (double)v;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double t = threadIdx.x < kBlockThreads / 32 ? red[threadIdx.x] : 0.0;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const double inv = 1.0 / sqrt(red[0] / (double)D + (double)eps);
+    float* orow = out + (int64_t)blockIdx.x * D;
+    for (int d = threadIdx.x; d < D; d += kBlockThreads) {
+        const float n = (float)((double)xr[d] * inv);
+        orow[d] = w ? n * w[d] : n;
+    }
+}
+
+// RoPE and the cache write.  blockIdx.x = token m = b * seq + s; blockIdx.y =
+// head slot: [0, H) query heads, [H, H + KVH) key heads, [H + KVH, H + 2 KVH)
+// value heads.  Pair (i, i + half): (x0 c - x1 s, x0 s + x1 c) with (c, s) =
+// freqs[s][i] (freqs holds the call's rows only, [seq][half][2]).
+// q_out [B][H][seq][hd]; cache [B][KVH][max_seq][hd] at row pos + s; knew /
+// vnew [B][KVH][seq][hd] (the rows written back to the host cache).
+__global__ void rope_cache_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                  const float* __restrict__ v, const float* __restrict__ freqs,
+                                  float* __restrict__ q_out, float* __restrict__ ck, float* __restrict__ cv,
+                                  float* __restrict__ knew, float* __restrict__ vnew, int seq, int H, int KVH,
+                                  int hd, int max_seq, int pos) {
+    const int m = blockIdx.x, slot = blockIdx.y;
+    const int b = m / seq, s = m % seq;
+    const int half = hd / 2;
+    const float* src;
+    float* dst;
+    float* dst2 = nullptr;
+    bool rope = freqs != nullptr;
+    if (slot < H) {
+        src = q + ((int64_t)m * H + slot) * hd;
+        dst = q_out + (((int64_t)b * H + slot) * seq + s) * hd;
+    } else if (slot < H + KVH) {
+        const int h = slot - H;
+        src = k + ((int64_t)m * KVH + h) * hd;
+        dst = ck + (((int64_t)b * KVH + h) * max_seq + pos + s) * hd;
+        dst2 = knew + (((int64_t)b * KVH + h) * seq + s) * hd;
+    } else {
+        const int h = slot - H - KVH;
+        src = v + ((int64_t)m * KVH + h) * hd;
+        dst = cv + (((int64_t)b * KVH + h) * max_seq + pos + s) * hd;
+        dst2 = vnew + (((int64_t)b * KVH + h) * seq + s) * hd;
+        rope = false;
+    }
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        float x0 = src[i], x1 = src[i + half];
+        if (rope) {
+            const float c = freqs[((int64_t)s * half + i) * 2], sn = freqs[((int64_t)s * half + i) * 2 + 1];
+            const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+            const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+            x0 = y0;
+            x1 = y1;
+        }
+        dst[i] = x0;
+        dst[i + half] = x1;
+        if (dst2) {
+            dst2[i] = x0;
+            dst2[i + half] = x1;
+        }
+    }
+}
+
+// One query row of one head per CTA: scores over the cache's first L
+// positions, softmax, weighted sum of the value rows.  blockIdx = (s, h, b).
+// out [B][seq][H][hd] (the [M][H*hd] input of the output projection).
+// mask: [mrows][mcols] rows of the call's queries (host mask rows 0 .. seq),
+// added where s < mrows and t < mcols.
+__global__ void __launch_bounds__(kAttnThreads) attn_kernel(const float* __restrict__ q, const float* __restrict__ ck,
+                                                            const float* __restrict__ cv,
+                                                            const float* __restrict__ mask, int mrows, int mcols,
+                                                            float* __restrict__ out, int seq, int H, int KVH, int hd,
+                                                            int max_seq, int L, float inv_scale) {
+    extern __shared__ float sh[];
+    float* qs = sh;              // [hd]
+    float* sc = sh + kMaxHeadDim;  // [L]
+    __shared__ float red[kAttnThreads / 32];
+    const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int kh = h / (H / KVH);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* qr = q + (((int64_t)b * H + h) * seq + s) * hd;
+    for (int d = threadIdx.x; d < hd; d += kAttnThreads) qs[d] = qr[d];
+    __syncthreads();
+    const float* kb = ck + ((int64_t)b * KVH + kh) * max_seq * hd;
+    const float* vb = cv + ((int64_t)b * KVH + kh) * max_seq * hd;
+    // scores: one warp per key row, lanes over head_dim
+    for (int t = warp; t < L; t += kAttnThreads / 32) {
+        const float* kr = kb + (int64_t)t * hd;
+        float acc = 0.0f;
+        for (int d = lane; d < hd; d += 32) acc = fmaf(qs[d], kr[d], acc);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) {
+            float v = acc * inv_scale;
+            if (mask && s < mrows && t < mcols) v += mask[(int64_t)s * mcols + t];
+            sc[t] = v;
+        }
+    }
+    __syncthreads();
+    // softmax over [0, L): max, exp(x - max), 1 / (sum + 1e-10)
+    float mx = -INFINITY;
+    for (int t = threadIdx.x; t < L; t += kAttnThreads) mx = fmaxf(mx, sc[t]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int w = 1; w < kAttnThreads / 32; w++) mx = fmaxf(mx, red[w]);
+    __syncthreads();
+    float sum = 0.0f;
+    for (int t = threadIdx.x; t < L; t += kAttnThreads) {
+        const float e = expf(sc[t] - mx);
+        sc[t] = e;
+        sum += e;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    sum = 0.0f;
+    for (int w = 0; w < kAttnThreads / 32; w++) sum += red[w];
+    const float inv = 1.0f / (sum + 1e-10f);
+    for (int t = threadIdx.x; t < L; t += kAttnThreads) sc[t] *= inv;
+    __syncthreads();
+    // out[d] = sum over t in order of p[t] v[t][d]
+    float* orow = out + (((int64_t)b * seq + s) * H + h) * hd;
+    for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
+        float acc = 0.0f;
+        for (int t = 0; t < L; t++) acc = fmaf(sc[t], vb[(int64_t)t * hd + d], acc);
+        orow[d] = acc;
+    }
+}
+
+// Gathers cache rows [r0, r1) of every (b, kv head) from a contiguous host
+// staging block [B][KVH][r1 - r0][hd] into the device cache.
+__global__ void cache_fill_kernel(const float* __restrict__ src, float* __restrict__ dst, int BK, int rows, int hd,
+                                  int max_seq, int r0) {
+    const int64_t n = (int64_t)BK * rows * hd;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int d = (int)(i % hd);
+        const int64_t rr = i / hd;
+        const int r = (int)(rr % rows), bk = (int)(rr / rows);
+        dst[((int64_t)bk * max_seq + r0 + r) * hd + d] = src[i];
+    }
+}
+
+namespace {
+
+// Device mirror of one host KV cache (K and V of one layer).
+struct Mirror {
+    float* k = nullptr;
+    float* v = nullptr;
+    size_t floats = 0;           // per buffer
+    int BK = 0, max_seq = 0, hd = 0;
+    int valid = 0;               // leading positions equal to the host cache
+    std::vector<float> last_row;  // host K row valid - 1 of (b 0, kv head 0), as last written
+    uint64_t used = 0;
+};
+
+struct NormW {
+    float* p = nullptr;
+    size_t n = 0;
+    uint64_t fp = 0;
+};
+
+struct BlockDev {
+    std::unordered_map<const void*, Mirror> mirrors;  // host cache_k data pointer -> mirror
+    Mirror scratch;                                   // a cache filled whole by one call (pos 0, seq = max_seq)
+    std::vector<std::pair<size_t, float*>> spare;     // evicted mirror buffers, reused by size
+    std::unordered_map<const void*, NormW> norms;     // host norm weight pointer -> device copy
+    float* arena = nullptr;
+    size_t arena_floats = 0;
+    float* h_stage = nullptr;  // pinned
+    size_t h_stage_floats = 0;
+    uint64_t clock = 0;
+};
+
+constexpr int kMaxMirrors = 192;
+std::mutex g_blk_mu;
+BlockDev g_blk[16];
+
+uint64_t fingerprint(const float* h, size_t n) {
+    uint64_t f = 0xcbf29ce484222325ull ^ n;
+    const size_t samples = n < 64 ? n : 64;
+    for (size_t i = 0; i < samples; i++) {
+        const size_t j = samples > 1 ? i * (n - 1) / (samples - 1) : 0;
+        uint32_t bits;
+        memcpy(&bits, h + j, 4);
+        f = (f ^ bits) * 0x100000001b3ull;
+    }
+    return f;
+}
+
+void spare_put(BlockDev& bd, size_t floats, float* p) {
+    bd.spare.push_back({floats, p});
+    if (bd.spare.size() > 64) {  // keep the spare list short
+        cudaFree(bd.spare.front().second);
+        bd.spare.erase(bd.spare.begin());
+    }
+}
+
+float* dev_alloc(BlockDev& bd, size_t floats) {
+    for (size_t i = 0; i < bd.spare.size(); i++) {
+        if (bd.spare[i].first == floats) {
+            float* p = bd.spare[i].second;
+            bd.spare.erase(bd.spare.begin() + (long)i);
+            return p;
+        }
+    }
+    float* p = nullptr;
+    if (cudaMalloc(&p, floats * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return p;
+}
+
+// Grows a device or pinned buffer (old contents dropped).  The stream is
+// drained first: queued work may still use the old buffer.
+bool grow(float** p, size_t* have, size_t want, bool pinned, cudaStream_t st) {
+    if (*have >= want) return true;
+    size_t n = 1 << 16;
+    while (n < want) n <<= 1;
+    cudaStreamSynchronize(st);
+    if (*p) pinned ? cudaFreeHost(*p) : cudaFree(*p);
+    *p = nullptr;
+    *have = 0;
+    const cudaError_t e = pinned ? cudaMallocHost(p, n * sizeof(float)) : cudaMalloc(p, n * sizeof(float));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        *p = nullptr;
+        return false;
+    }
+    *have = n;
+    return true;
+}
+
+// Device copy of a host norm weight (fp32 or fp16), cached by pointer and fingerprint.
+VoxCPMError norm_weight(BlockDev& bd, const Tensor* t, cudaStream_t st, const float** out) {
+    *out = nullptr;
+    if (!t) return VOXCPM_SUCCESS;
+    if (t->is_cuda) return VOXCPM_ERR_CUDA_NOT_FOUND;
+    const void* key = t->is_fp16 ? (const void*)t->data_fp16 : (const void*)t->data;
+    if (!key) return VOXCPM_ERR_CUDA_NOT_FOUND;
+    std::vector<float> host(t->size);
+    for (size_t i = 0; i < t->size; i++) host[i] = t->is_fp16 ? half_to_float(t->data_fp16[i]) : t->data[i];
+    const uint64_t fp = fingerprint(host.data(), host.size());
+    auto it = bd.norms.find(key);
+    if (it != bd.norms.end() && it->second.n == t->size && it->second.fp == fp) {
+        *out = it->second.p;
+        return VOXCPM_SUCCESS;
+    }
+    float* d = nullptr;
+    VOXQ_CUDA_TRY(cudaMalloc(&d, t->size * sizeof(float)));
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(d, host.data(), t->size * sizeof(float), cudaMemcpyHostToDevice, st));
+    VOXQ_CUDA_TRY(cudaStreamSynchronize(st));
+    if (it != bd.norms.end()) cudaFree(it->second.p);
+    bd.norms[key] = NormW{d, t->size, fp};
+    *out = d;
+    return VOXCPM_SUCCESS;
+}
+
+// The mirror of a host cache, made valid for rows [0, pos).
+VoxCPMError mirror_for(BlockDev& bd, Tensor* ck, Tensor* cv, int BK, int max_seq, int hd, int pos, bool seq_fills,
+                       cudaStream_t st, Mirror** out) {
+    *out = nullptr;
+    const size_t floats = (size_t)BK * max_seq * hd;
+    if (pos == 0 && seq_fills) {  // the call writes the whole cache: no state to keep
+        Mirror& m = bd.scratch;
+        if (m.floats < floats) {
+            cudaStreamSynchronize(st);
+            if (m.k) cudaFree(m.k);
+            if (m.v) cudaFree(m.v);
+            m.k = m.v = nullptr;
+            m.floats = 0;
+            VOXQ_CUDA_TRY(cudaMalloc(&m.k, floats * sizeof(float)));
+            VOXQ_CUDA_TRY(cudaMalloc(&m.v, floats * sizeof(float)));
+            m.floats = floats;
+        }
+        m.BK = BK;
+        m.max_seq = max_seq;
+        m.hd = hd;
+        m.valid = 0;
+        *out = &m;
+        return VOXCPM_SUCCESS;
+    }
+    auto it = bd.mirrors.find(ck->data);
+    if (it != bd.mirrors.end() && (it->second.floats != floats || it->second.hd != hd || it->second.BK != BK)) {
+        spare_put(bd, it->second.floats, it->second.k);
+        spare_put(bd, it->second.floats, it->second.v);
+        bd.mirrors.erase(it);
+        it = bd.mirrors.end();
+    }
+    if (it == bd.mirrors.end()) {
+        if (bd.mirrors.size() >= (size_t)kMaxMirrors) {  // evict the least recently used
+            auto lru = bd.mirrors.begin();
+            for (auto m = bd.mirrors.begin(); m != bd.mirrors.end(); ++m)
+                if (m->second.used < lru->second.used) lru = m;
+            spare_put(bd, lru->second.floats, lru->second.k);
+            spare_put(bd, lru->second.floats, lru->second.v);
+            bd.mirrors.erase(lru);
+        }
+        Mirror m;
+        m.k = dev_alloc(bd, floats);
+        m.v = dev_alloc(bd, floats);
+        if (!m.k || !m.v) return VOXCPM_ERR_OOM;
+        m.floats = floats;
+        m.BK = BK;
+        m.max_seq = max_seq;
+        m.hd = hd;
+        it = bd.mirrors.emplace(ck->data, std::move(m)).first;
+    }
+    Mirror& m = it->second;
+    m.used = ++bd.clock;
+    if (pos == 0) m.valid = 0;
+    if (m.valid > pos) m.valid = pos;
+    // the host row the mirror last wrote must still be there
+    if (m.valid > 0) {
+        const float* hrow = ck->data + (size_t)(m.valid - 1) * hd;
+        if ((int)m.last_row.size() != hd || memcmp(hrow, m.last_row.data(), (size_t)hd * sizeof(float)) != 0)
+            m.valid = 0;
+    }
+    if (m.valid < pos) {  // rows [valid, pos) from the host cache
+        const int r0 = m.valid, rows = pos - r0;
+        const size_t n = (size_t)BK * rows * hd;
+        if (!grow(&bd.h_stage, &bd.h_stage_floats, 2 * n, true, st)) return VOXCPM_ERR_OOM;
+        for (int kv = 0; kv < 2; kv++) {
+            const float* src = kv ? cv->data : ck->data;
+            float* stage = bd.h_stage + kv * n;
+            for (int bk = 0; bk < BK; bk++)
+                memcpy(stage + (size_t)bk * rows * hd, src + ((size_t)bk * max_seq + r0) * hd,
+                       (size_t)rows * hd * sizeof(float));
+        }
+        float* tmp = dev_alloc(bd, 2 * n);
+        if (!tmp) return VOXCPM_ERR_OOM;
+        VOXQ_CUDA_TRY(cudaMemcpyAsync(tmp, bd.h_stage, 2 * n * sizeof(float), cudaMemcpyHostToDevice, st));
+        const int grid = (int)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024);
+        cache_fill_kernel<<<grid, 256, 0, st>>>(tmp, m.k, BK, rows, hd, max_seq, r0);
+        cache_fill_kernel<<<grid, 256, 0, st>>>(tmp + n, m.v, BK, rows, hd, max_seq, r0);
+        VOXQ_CUDA_TRY(cudaGetLastError());
+        VOXQ_CUDA_TRY(cudaStreamSynchronize(st));
+        cudaFree(tmp);  // rare: a cache the mirror cannot vouch for
+        m.valid = pos;
+        m.last_row.assign(ck->data + (size_t)(pos - 1) * hd, ck->data + (size_t)pos * hd);
+    }
+    *out = &m;
+    return VOXCPM_SUCCESS;
+}
+
+bool is_host_f32(const Tensor* t) { return t && t->data && !t->is_cuda && !t->is_fp16; }
+
+VoxCPMError project(const float* a, int M, int K, const voxq_qweight& w, float* out, const float* residual,
+                    const voxq_qweight* up, cudaStream_t st) {
+    voxq_epilogue epi = {nullptr, residual, w.N, up};
+    return voxq_matmul_nt_q(a, M, K, &w, out, w.N, (residual || up) ? &epi : nullptr, st);
+}
+
+}  // namespace
+
+void block_cache_clear() {
+    std::lock_guard<std::mutex> lk(g_blk_mu);
+    for (BlockDev& bd : g_blk) {
+        for (auto& m : bd.mirrors) {
+            cudaFree(m.second.k);
+            cudaFree(m.second.v);
+        }
+        for (auto& s : bd.spare) cudaFree(s.second);
+        for (auto& n : bd.norms) cudaFree(n.second.p);
+        if (bd.scratch.k) cudaFree(bd.scratch.k);
+        if (bd.scratch.v) cudaFree(bd.scratch.v);
+        if (bd.arena) cudaFree(bd.arena);
+        if (bd.h_stage) cudaFreeHost(bd.h_stage);
+        bd = BlockDev();
+    }
+}
+
+}  // namespace voxq
+
+using namespace voxq;
+
+extern "C" VoxCPMError voxq_transformer_block_forward(const voxq_block_desc* blk, const Tensor* x, Tensor* cache_k,
+                                                      Tensor* cache_v, const Tensor* mask, const Tensor* freqs_cis,
+                                                      int pos, Tensor* out) {
+    constexpr VoxCPMError kHost = VOXCPM_ERR_CUDA_NOT_FOUND;  // "run the host code instead"
+    if (!blk || !blk->rms_attn || !blk->attn || !blk->rms_ffn || !blk->ffn || !x || !out || !cache_k || !cache_v)
+        return kHost;
+    cudaStream_t st = (cudaStream_t)library_stream();
+    if (!st) return kHost;
+    const voxq_attention_desc& at = *blk->attn;
+    const voxq_swiglu_desc& ff = *blk->ffn;
+    // shapes the kernels take; anything else (including the reference's own
+    // shape errors) goes to the host code
+    if (!is_host_f32(x) || !is_host_f32(out) || x->ndim != 3 || out->ndim != 3) return kHost;
+    const int B = x->shape[0], seq = x->shape[1], D = x->shape[2];
+    if (out->shape[0] != B || out->shape[1] != seq || out->shape[2] != D || B < 1 || seq < 1) return kHost;
+    const int H = at.n_heads, KVH = at.n_kv_heads, hd = at.head_dim, F = ff.d_ff;
+    if (D != at.d_model || D != ff.d_model || H < 1 || KVH < 1 || H % KVH || hd < 4 || hd % 4 || hd > kMaxHeadDim)
+        return kHost;
+    if (!is_host_f32(cache_k) || !is_host_f32(cache_v) || cache_k->ndim != 4 || cache_v->ndim != 4) return kHost;
+    const int max_seq = cache_k->shape[2];
+    for (int i = 0; i < 4; i++)
+        if (cache_v->shape[i] != cache_k->shape[i]) return kHost;
+    if (cache_k->shape[0] != B || cache_k->shape[1] != KVH || cache_k->shape[3] != hd) return kHost;
+    const int L = pos + seq;  // cache length after this call
+    if (pos < 0 || L > max_seq || L > kMaxCacheLen) return kHost;
+    if (mask && (!is_host_f32(mask) || mask->ndim != 2)) return kHost;
+    const int half = hd / 2;
+    if (freqs_cis && (!is_host_f32(freqs_cis) || freqs_cis->size < (size_t)L * half * 2)) return kHost;
+    const int qk = H * hd, kv = KVH * hd, M = B * seq;
+    voxq_qweight wq, wk, wv, wo, w1, w2, w3;
+    if (!device_qweight(at.wq, &wq) || !device_qweight(at.wk, &wk) || !device_qweight(at.wv, &wv) ||
+        !device_qweight(at.wo, &wo) || !device_qweight(ff.w1, &w1) || !device_qweight(ff.w2, &w2) ||
+        !device_qweight(ff.w3, &w3))
+        return kHost;
+    if (wq.N != qk || wq.K != D || wk.N != kv || wk.K != D || wv.N != kv || wv.K != D || wo.N != D || wo.K != qk ||
+        w1.N != F || w1.K != D || w3.N != F || w3.K != D || w2.N != D || w2.K != F || w1.qtype != w3.qtype ||
+        w1.q8_signed != w3.q8_signed)
+        return kHost;
+    const int dev = current_device();
+    if (dev < 0 || dev >= 16) return kHost;
+
+    std::lock_guard<std::mutex> lk(g_blk_mu);
+    BlockDev& bd = g_blk[dev];
+    const float *wn1 = nullptr, *wn2 = nullptr;
+    VoxCPMError e = norm_weight(bd, blk->rms_attn->weight, st, &wn1);
+    if (!e) e = norm_weight(bd, blk->rms_ffn->weight, st, &wn2);
+    if (e) return e;
+
+    // device arena: x n q k v qr ao h n2 g o knew vnew freqs mask
+    const int mcols = mask ? (mask->shape[1] < L ? mask->shape[1] : L) : 0;
+    const int mrows = mask ? (mask->shape[0] < seq ? mask->shape[0] : seq) : 0;
+    const size_t nx = (size_t)M * D, nq = (size_t)M * qk, nk = (size_t)M * kv, ng = (size_t)M * F;
+    const size_t nf = freqs_cis ? (size_t)seq * half * 2 : 0, nm = (size_t)mrows * mcols;
+    auto al = [](size_t n) { return (n + 63) & ~(size_t)63; };  // 256-byte aligned parts
+    const size_t off_n = al(nx), off_q = off_n + al(nx), off_k = off_q + al(nq), off_v = off_k + al(nk),
+                 off_qr = off_v + al(nk), off_ao = off_qr + al(nq), off_h = off_ao + al(nq), off_n2 = off_h + al(nx),
+                 off_g = off_n2 + al(nx), off_o = off_g + al(ng), off_kn = off_o + al(nx), off_vn = off_kn + al(nk),
+                 off_f = off_vn + al(nk), off_m = off_f + al(nf), total = off_m + al(nm);
+    if (!grow(&bd.arena, &bd.arena_floats, total, false, st)) return VOXCPM_ERR_OOM;
+    // pinned staging: uploads x | freqs rows | mask rows, downloads out | knew | vnew
+    const size_t up_n = al(nx) + al(nf) + al(nm), down_n = al(nx) + 2 * al(nk);
+    if (!grow(&bd.h_stage, &bd.h_stage_floats, up_n + down_n, true, st)) return VOXCPM_ERR_OOM;
+
+    Mirror* mr = nullptr;
+    e = mirror_for(bd, cache_k, cache_v, B * KVH, max_seq, hd, pos, seq == max_seq, st, &mr);
+    if (e) return e;
+
+    float* A = bd.arena;
+    float *d_x = A, *d_n = A + off_n, *d_q = A + off_q, *d_k = A + off_k, *d_v = A + off_v, *d_qr = A + off_qr,
+          *d_ao = A + off_ao, *d_h = A + off_h, *d_n2 = A + off_n2, *d_g = A + off_g, *d_o = A + off_o,
+          *d_kn = A + off_kn, *d_vn = A + off_vn, *d_f = A + off_f, *d_m = A + off_m;
+    float* hs = bd.h_stage;
+    memcpy(hs, x->data, nx * sizeof(float));
+    if (nf) memcpy(hs + al(nx), freqs_cis->data + (size_t)pos * half * 2, nf * sizeof(float));
+    for (int r = 0; r < mrows; r++)
+        memcpy(hs + al(nx) + al(nf) + (size_t)r * mcols, mask->data + (size_t)r * mask->shape[1],
+               (size_t)mcols * sizeof(float));
+    // one upload: x, then the freqs and mask parts sit at the arena's f / m offsets
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(d_x, hs, nx * sizeof(float), cudaMemcpyHostToDevice, st));
+    if (nf) VOXQ_CUDA_TRY(cudaMemcpyAsync(d_f, hs + al(nx), nf * sizeof(float), cudaMemcpyHostToDevice, st));
+    if (nm)
+        VOXQ_CUDA_TRY(cudaMemcpyAsync(d_m, hs + al(nx) + al(nf), nm * sizeof(float), cudaMemcpyHostToDevice, st));
+
+    // n = RMSNorm(x)
+    rmsnorm_kernel<<<M, kBlockThreads, 0, st>>>(d_x, wn1, blk->rms_attn->eps, d_n, D);
+    VOXQ_CUDA_TRY(cudaGetLastError());
+    // q, k, v
+    if (M <= 8) {
+        voxq_gemv_item it[3] = {};
+        const voxq_qweight* ws[3] = {&wq, &wk, &wv};
+        float* outs[3] = {d_q, d_k, d_v};
+        for (int i = 0; i < 3; i++) {
+            it[i].w = *ws[i];
+            it[i].a = d_n;
+            it[i].out = outs[i];
+            it[i].M = M;
+            it[i].lda = D;
+            it[i].ldo = ws[i]->N;
+        }
+        e = voxq_gemv_batch(it, 3, st);
+    } else {
+        e = project(d_n, M, D, wq, d_q, nullptr, nullptr, st);
+        if (!e) e = project(d_n, M, D, wk, d_k, nullptr, nullptr, st);
+        if (!e) e = project(d_n, M, D, wv, d_v, nullptr, nullptr, st);
+    }
+    if (e) return e;
+    // RoPE, cache rows [pos, pos + seq)
+    rope_cache_kernel<<<dim3(M, H + 2 * KVH), 64, 0, st>>>(d_q, d_k, d_v, nf ? d_f : nullptr, d_qr, mr->k, mr->v,
+                                                          d_kn, d_vn, seq, H, KVH, hd, max_seq, pos);
+    VOXQ_CUDA_TRY(cudaGetLastError());
+    // attention over [0, L)
+    const int smem = (kMaxHeadDim + L) * (int)sizeof(float);
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (kMaxHeadDim + kMaxCacheLen) * (int)sizeof(float));
+    });
+    attn_kernel<<<dim3(seq, H, B), kAttnThreads, smem, st>>>(d_qr, mr->k, mr->v, nm ? d_m : nullptr, mrows, mcols,
+                                                            d_ao, seq, H, KVH, hd, max_seq, L,
+                                                            1.0f / sqrtf((float)hd));
+    VOXQ_CUDA_TRY(cudaGetLastError());
+    // h = x + a Wo^T ; n2 = RMSNorm(h) ; g = silu(n2 W1^T) * (n2 W3^T) ; o = h + g W2^T
+    e = project(d_ao, M, qk, wo, d_h, d_x, nullptr, st);
+    if (e) return e;
+    rmsnorm_kernel<<<M, kBlockThreads, 0, st>>>(d_h, wn2, blk->rms_ffn->eps, d_n2, D);
+    VOXQ_CUDA_TRY(cudaGetLastError());
+    e = project(d_n2, M, D, w1, d_g, nullptr, &w3, st);
+    if (!e) e = project(d_g, M, F, w2, d_o, d_h, nullptr, st);
+    if (e) return e;
+    // downloads: out, new cache rows; one wait
+    float* hd_out = hs + up_n;
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(hd_out, d_o, nx * sizeof(float), cudaMemcpyDeviceToHost, st));
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(hd_out + al(nx), d_kn, nk * sizeof(float), cudaMemcpyDeviceToHost, st));
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(hd_out + al(nx) + al(nk), d_vn, nk * sizeof(float), cudaMemcpyDeviceToHost, st));
+    VOXQ_CUDA_TRY(cudaStreamSynchronize(st));
+    memcpy(out->data, hd_out, nx * sizeof(float));
+    for (int kvs = 0; kvs < 2; kvs++) {
+        const float* src = hd_out + al(nx) + kvs * al(nk);
+        float* dst = kvs ? cache_v->data : cache_k->data;
+        for (int bk = 0; bk < B * KVH; bk++)
+            memcpy(dst + ((size_t)bk * max_seq + pos) * hd, src + (size_t)bk * seq * hd, (size_t)seq * hd * sizeof(float));
+    }
+    mr->valid = L;
+    mr->last_row.assign(cache_k->data + (size_t)(L - 1) * hd, cache_k->data + (size_t)L * hd);
+    return VOXCPM_SUCCESS;
+}
+
+extern "C" void voxq_block_cache_clear(void) { block_cache_clear(); }

@@ -138,31 +138,6 @@ struct Sha256 {
     }
 };
 
-float half_to_float(uint16_t h) {
-    // IEEE binary16 -> binary32, exact (include/tensor.h:350-371 decodes the same way)
-    const uint32_t s = (uint32_t)(h >> 15) << 31, e = (h >> 10) & 31, m = h & 1023;
-    uint32_t bits;
-    if (e == 0) {
-        if (m == 0) {
-            bits = s;
-        } else {  // subnormal: renormalise
-            int sh = 0;
-            uint32_t mm = m;
-            while (!(mm & 1024)) {
-                mm <<= 1;
-                sh++;
-            }
-            bits = s | (uint32_t)(127 - 15 + 1 - sh) << 23 | (mm & 1023) << 13;
-        }
-    } else if (e == 31) {
-        bits = s | 0x7F800000u | m << 13;
-    } else {
-        bits = s | (e - 15 + 127) << 23 | m << 13;
-    }
-    float f;
-    memcpy(&f, &bits, 4);
-    return f;
-}
 
 VoxCPMError parse(voxq_vxcpm2* f) {
     const uint8_t* b = f->base;
@@ -214,6 +189,33 @@ VoxCPMError parse(voxq_vxcpm2* f) {
 }
 
 }  // namespace
+
+float half_to_float(uint16_t h) {
+    // IEEE binary16 -> binary32, exact (include/tensor.h:350-371 decodes the same way)
+    const uint32_t s = (uint32_t)(h >> 15) << 31, e = (h >> 10) & 31, m = h & 1023;
+    uint32_t bits;
+    if (e == 0) {
+        if (m == 0) {
+            bits = s;
+        } else {  // subnormal: renormalise
+            int sh = 0;
+            uint32_t mm = m;
+            while (!(mm & 1024)) {
+                mm <<= 1;
+                sh++;
+            }
+            bits = s | (uint32_t)(127 - 15 + 1 - sh) << 23 | (mm & 1023) << 13;
+        }
+    } else if (e == 31) {
+        bits = s | 0x7F800000u | m << 13;
+    } else {
+        bits = s | (e - 15 + 127) << 23 | m << 13;
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
 }  // namespace voxq
 
 extern "C" {

@@ -54,6 +54,17 @@ void* library_stream();
 // (voxq_conv.cu); called by tensor_cuda_shutdown.
 void conv_cache_clear();
 
+// The packed layout of a weight that tensor_to_cuda quantized (looked up by
+// its device pointer); false for any other tensor (voxq_runtime.cu).
+bool device_qweight(const Tensor* w, voxq_qweight* out);
+
+// binary16 -> binary32 on the host, as include/tensor.h:350-371 (voxq_container.cu).
+float half_to_float(uint16_t h);
+
+// Drops the transformer blocks' device cache mirrors, norm weights and
+// staging (voxq_block.cu); called by tensor_cuda_shutdown.
+void block_cache_clear();
+
 // Per-device workspace arena (voxq_runtime.cu): grows on demand, never
 // shrinks, ordered on the stream that uses it.
 void* workspace(size_t bytes);

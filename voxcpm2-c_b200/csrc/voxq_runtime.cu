@@ -164,6 +164,16 @@ static DevState* state() {
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+bool device_qweight(const Tensor* w, voxq_qweight* out) {
+    if (!w || !w->is_cuda || !w->data) return false;
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_qtab.find(w->data);
+    if (it == g_qtab.end()) return false;
+    const QRec& q = it->second;
+    *out = voxq_qweight{q.codes, q.scales, q.N, q.K, q.qtype, 0};
+    return true;
+}
+
 void* library_stream() {
     DevState* s = state();
     return (s && s->init) ? (void*)s->stream : nullptr;
@@ -288,6 +298,7 @@ extern "C" void tensor_cuda_shutdown(void) {
     cudaStreamSynchronize(s->stream);
     cudaDeviceSynchronize();  // the workspaces may also serve voxq_* calls on other streams
     conv_cache_clear();
+    block_cache_clear();
     for (int k = 0; k < kSlots; k++) {
         if (s->slot[k]) cudaFree(s->slot[k]);
         s->slot[k] = nullptr;

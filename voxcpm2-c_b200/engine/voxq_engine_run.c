@@ -204,6 +204,30 @@ VoxCPMError __wrap_conv1d_forward(const Conv1D* conv, const Tensor* x, Tensor* o
     }
     return __real_conv1d_forward(conv, x, out);
 }
+/* transformer_block_forward (src/nn.c:579-700), called from tslm.c, ralm.c,
+ * loc_dit.c and loc_enc.c, goes to voxq_transformer_block_forward: the whole
+ * block on the device (TransformerBlock, RmsNorm, Attention and SwiGLU have
+ * voxq's descriptor layouts).  VOXQ_ENGINE_BLOCK=cpu keeps the host code. */
+static int g_block_gpu = 1;
+static long g_block_dev = 0, g_block_host = 0;
+VoxCPMError __real_transformer_block_forward(const TransformerBlock* block, const Tensor* x, Tensor* cache_k,
+                                             Tensor* cache_v, const Tensor* mask, const Tensor* freqs_cis, int pos,
+                                             Tensor* out);
+VoxCPMError __wrap_transformer_block_forward(const TransformerBlock* block, const Tensor* x, Tensor* cache_k,
+                                             Tensor* cache_v, const Tensor* mask, const Tensor* freqs_cis, int pos,
+                                             Tensor* out) {
+    if (g_block_gpu) {
+        const VoxCPMError r = voxq_transformer_block_forward((const voxq_block_desc*)block, x, cache_k, cache_v, mask,
+                                                             freqs_cis, pos, out);
+        if (r != VOXCPM_ERR_CUDA_NOT_FOUND) {
+            g_block_dev++;
+            return r;
+        }
+    }
+    g_block_host++;
+    return __real_transformer_block_forward(block, x, cache_k, cache_v, mask, freqs_cis, pos, out);
+}
+
 VoxCPMError __real_conv1d_transpose_forward(const Conv1DTranspose* conv, const Tensor* x, Tensor* out);
 VoxCPMError __wrap_conv1d_transpose_forward(const Conv1DTranspose* conv, const Tensor* x, Tensor* out) {
     if (g_vae_gpu) {
@@ -262,6 +286,9 @@ static unsigned long long latents_fnv(void) {
 }
 
 static void print_stages(void) {
+#ifdef VOXQ_ENGINE_LIBVOXQ
+    printf("\"blocks\": {\"device\": %ld, \"host\": %ld}, ", g_block_dev, g_block_host);
+#endif
     printf("\"stages\": {");
     for (int s = 0; s < ST_N; s++) {
         printf("%s\"%s\": {\"s\": %.5f, \"calls\": %ld", s ? ", " : "", k_stage[s], g_stage_s[s], g_stage_calls[s]);
@@ -293,6 +320,7 @@ static int serve(VoxCPMModel* model, const char* latents_dir) {
         memset(g_matmul_in, 0, sizeof(g_matmul_in));
 #ifdef VOXQ_ENGINE_LIBVOXQ
         voxq_matmul_traffic(NULL, NULL, 1);
+        g_block_dev = g_block_host = 0;
 #endif
         VoxCPMGenConfig gen = voxcpm_gen_config_default();
         gen.text = "synthetic token ids";
@@ -372,6 +400,7 @@ int main(int argc, char** argv) {
     g_dump_calls = getenv("VOXQ_ENGINE_DUMP_CALL");
 #ifdef VOXQ_ENGINE_LIBVOXQ
     if (getenv("VOXQ_ENGINE_VAE") && !strcmp(getenv("VOXQ_ENGINE_VAE"), "cpu")) g_vae_gpu = 0;
+    if (getenv("VOXQ_ENGINE_BLOCK") && !strcmp(getenv("VOXQ_ENGINE_BLOCK"), "cpu")) g_block_gpu = 0;
 #endif
     g_dump_dir = getenv("VOXQ_ENGINE_DUMP_DIR");
 

@@ -103,6 +103,30 @@ class Vxcpm2Tensor(C.Structure):
                 ("group", C.c_int32), ("elements", C.c_uint64), ("offset", C.c_uint64), ("bytes", C.c_uint64)]
 
 
+class RmsNormDesc(C.Structure):
+    """voxq_rmsnorm_desc (include/voxq.h; the engine's RmsNorm)."""
+    _fields_ = [("weight", C.POINTER(Tensor)), ("eps", C.c_float)]
+
+
+class AttentionDesc(C.Structure):
+    """voxq_attention_desc (the engine's Attention)."""
+    _fields_ = [("wq", C.POINTER(Tensor)), ("wk", C.POINTER(Tensor)), ("wv", C.POINTER(Tensor)),
+                ("wo", C.POINTER(Tensor)), ("d_model", C.c_int), ("n_heads", C.c_int), ("n_kv_heads", C.c_int),
+                ("head_dim", C.c_int)]
+
+
+class SwigluDesc(C.Structure):
+    """voxq_swiglu_desc (the engine's SwiGLU)."""
+    _fields_ = [("w1", C.POINTER(Tensor)), ("w2", C.POINTER(Tensor)), ("w3", C.POINTER(Tensor)),
+                ("d_model", C.c_int), ("d_ff", C.c_int)]
+
+
+class BlockDesc(C.Structure):
+    """voxq_block_desc (the engine's TransformerBlock)."""
+    _fields_ = [("rms_attn", C.POINTER(RmsNormDesc)), ("attn", C.POINTER(AttentionDesc)),
+                ("rms_ffn", C.POINTER(RmsNormDesc)), ("ffn", C.POINTER(SwigluDesc))]
+
+
 _vp, _sz, _i, _i64 = C.c_void_p, C.c_size_t, C.c_int, C.c_int64
 _TP = C.POINTER(Tensor)
 SIGNATURES = {
@@ -134,6 +158,8 @@ SIGNATURES = {
     "voxq_conv1d_forward": ([C.POINTER(Conv1dDesc), _TP, _TP], _i),
     "voxq_conv1d_transpose_forward": ([C.POINTER(Conv1dTransposeDesc), _TP, _TP], _i),
     "voxq_conv_cache_clear": ([], None),
+    "voxq_transformer_block_forward": ([C.POINTER(BlockDesc), _TP, _TP, _TP, _TP, _TP, _i, _TP], _i),
+    "voxq_block_cache_clear": ([], None),
     "voxq_vxcpm2_open": ([C.c_char_p, C.POINTER(_vp)], _i),
     "voxq_vxcpm2_close": ([_vp], None),
     "voxq_vxcpm2_info": ([_vp, C.POINTER(Vxcpm2Header), C.POINTER(_i)], _i),
