@@ -314,6 +314,35 @@ VOXQ_API VoxCPMError voxq_conv1d_transpose_forward(const voxq_conv1d_transpose_d
  * counterpart in the reference). */
 VOXQ_API void voxq_conv_cache_clear(void);
 
+/* The AudioVAE decoder (audio_vae_decode, src/audio_vae.c:941-1116) as a
+ * list of steps run on the device with the activation resident: the latent
+ * [batch, time, latent_dim] (host) is permuted to [batch, latent_dim, time]
+ * and uploaded once, each step transforms the current activation h, and the
+ * final h [batch, 1, samples] is copied to waveform ([batch, samples], or
+ * [samples] for batch 1) with audio_vae_decode's shape rules.  Steps:
+ *   VOXQ_VAE_CONV / VOXQ_VAE_CONVT  h = conv(h) (conv1d_forward /
+ *                                   conv1d_transpose_forward, as above)
+ *   VOXQ_VAE_SNAKE      h = h + sin(alpha[c] h)^2 / beta per channel c
+ *                       (snake_forward, src/audio_vae.c:310-351; alpha a
+ *                       host tensor of >= channels values)
+ *   VOXQ_VAE_SAVE       remember h (a residual sub-block's input)
+ *   VOXQ_VAE_ADD_SAVED  h = h + the remembered tensor
+ *                       (residual_sub_block_forward, src/audio_vae.c:354-421)
+ *   VOXQ_VAE_TANH       h = tanh(h) (tensor_tanh)
+ * An engine builds the list from its AudioVAEDecoder (include/model.h:
+ * 352-417).  Shape errors -> VOXCPM_ERR_SHAPE_MISMATCH; not initialised ->
+ * VOXCPM_ERR_CUDA_NOT_FOUND. */
+enum { VOXQ_VAE_CONV = 1, VOXQ_VAE_CONVT = 2, VOXQ_VAE_SNAKE = 3, VOXQ_VAE_SAVE = 4, VOXQ_VAE_ADD_SAVED = 5,
+       VOXQ_VAE_TANH = 6 };
+typedef struct {
+    int kind;
+    const voxq_conv1d_desc* conv;             /* VOXQ_VAE_CONV */
+    const voxq_conv1d_transpose_desc* convt;  /* VOXQ_VAE_CONVT */
+    const Tensor* alpha;                      /* VOXQ_VAE_SNAKE */
+} voxq_vae_op;
+VOXQ_API VoxCPMError voxq_vae_decode(const voxq_vae_op* ops, int n_ops, float snake_beta, const Tensor* latent,
+                                     Tensor* waveform);
+
 /* ---- Transformer block on the device -------------------------------------
  * transformer_block_forward (src/nn.c:579-700) with every step on the device:
  *   h   = x + Attention(RMSNorm_attn(x))

@@ -112,3 +112,99 @@ def test_conv_shape_errors_and_no_bias(lib):
     assert lib.voxq_conv1d_forward(C.byref(bad), xt, ot) == voxq.SHAPE_MISMATCH
     for t in (wt, xt, ot):
         voxq.free_tensor(t)
+
+
+def test_vae_decode_steps(lib):
+    """voxq_vae_decode: the decoder's step list (conv_in, proj_up, snake, a transposed upsampling
+    conv, a residual sub-block with its saved input, the final snake, conv_out, tanh) on a resident
+    activation, against the checker's convolutions and a float64 snake / tanh
+    (src/audio_vae.c:310-351, 354-421, 941-1116), fp32 between steps.  Rule: the tanh-bounded
+    output within 2e-4 absolute."""
+    rs = np.random.RandomState(7)
+    B, T, D, C1, C2 = 1, 4, 16, 32, 8
+    keep = []
+
+    def host(a):
+        t = voxq.host_tensor(a.astype(np.float32))
+        keep.append(t)
+        return t
+
+    def conv_desc(w, b, cin, cout, k, stride, pad, groups):
+        d = voxq.Conv1dDesc(C.cast(host(w), C.c_void_p), C.cast(host(b), C.c_void_p) if b is not None else None,
+                            cin, cout, k, stride, pad, groups)
+        keep.append(d)
+        return d
+
+    def convt_desc(w, b, cin, cout, k, stride, pad):
+        d = voxq.Conv1dTransposeDesc(C.cast(host(w), C.c_void_p),
+                                     C.cast(host(b), C.c_void_p) if b is not None else None, cin, cout, k, stride, pad)
+        keep.append(d)
+        return d
+
+    z = rs.standard_normal((B, T, D)).astype(np.float32)
+    w_in = (rs.standard_normal((D, 1, 7)) * 0.3).astype(np.float32)
+    w_up = (rs.standard_normal((C1, D, 1)) * 0.3).astype(np.float32)
+    b_up = (rs.standard_normal(C1) * 0.1).astype(np.float32)
+    a0 = (0.5 + rs.random_sample(C1)).astype(np.float32)
+    w_t = (rs.standard_normal((C1, C2, 4)) * 0.2).astype(np.float32)
+    b_t = (rs.standard_normal(C2) * 0.1).astype(np.float32)
+    a1 = (0.5 + rs.random_sample(C2)).astype(np.float32)
+    w_dw = (rs.standard_normal((C2, 1, 7)) * 0.3).astype(np.float32)
+    a2 = (0.5 + rs.random_sample(C2)).astype(np.float32)
+    w_pw = (rs.standard_normal((C2, C2, 1)) * 0.3).astype(np.float32)
+    af = (0.5 + rs.random_sample(C2)).astype(np.float32)
+    w_out = (rs.standard_normal((1, C2, 7)) * 0.3).astype(np.float32)
+    b_out = np.array([0.05], np.float32)
+
+    ops_spec = [("conv", conv_desc(w_in, None, D, D, 7, 1, 3, D)),
+                ("conv", conv_desc(w_up, b_up, D, C1, 1, 1, 0, 1)),
+                ("snake", host(a0)),
+                ("convt", convt_desc(w_t, b_t, C1, C2, 4, 2, 1)),
+                ("save", None), ("snake", host(a1)), ("conv", conv_desc(w_dw, None, C2, C2, 7, 1, 3, C2)),
+                ("snake", host(a2)), ("conv", conv_desc(w_pw, None, C2, C2, 1, 1, 0, 1)), ("add", None),
+                ("snake", host(af)), ("conv", conv_desc(w_out, b_out, C2, 1, 7, 1, 3, 1)), ("tanh", None)]
+    kinds = {"conv": 1, "convt": 2, "snake": 3, "save": 4, "add": 5, "tanh": 6}
+    ops = (voxq.VaeOp * len(ops_spec))()
+    for i, (k, v) in enumerate(ops_spec):
+        ops[i].kind = kinds[k]
+        if k == "conv":
+            ops[i].conv = C.pointer(v)
+        elif k == "convt":
+            ops[i].convt = C.pointer(v)
+        elif k == "snake":
+            ops[i].alpha = v
+
+    # reference chain: the checker's convolutions, float64 elementwise steps, float32 between steps
+    def snake(h, a):
+        return (h + np.sin(a[None, :, None].astype(np.float64) * h) ** 2 / 1.0).astype(np.float32)
+
+    h = np.ascontiguousarray(z.transpose(0, 2, 1))
+    h, _ = O.conv1d(h, w_in, None, 1, 3, D)
+    h, _ = O.conv1d(h, w_up, b_up, 1, 0, 1)
+    h = snake(h, a0)
+    h, _ = O.conv1d_transpose(h, w_t, b_t, 2, 1)
+    skip = h.copy()
+    h = snake(h, a1)
+    h, _ = O.conv1d(h, w_dw, None, 1, 3, C2)
+    h = snake(h, a2)
+    h, _ = O.conv1d(h, w_pw, None, 1, 0, 1)
+    h = h + skip
+    h = snake(h, af)
+    h, _ = O.conv1d(h, w_out, b_out, 1, 3, 1)
+    ref = np.tanh(h.astype(np.float64))
+    wave = voxq.host_tensor(np.zeros((B, ref.shape[2]), np.float32))
+    keep.append(wave)
+    try:
+        assert lib.voxq_vae_decode(ops, len(ops_spec), C.c_float(1.0), host(z), wave) == 0
+        got = voxq.host_tensor_view(wave)
+        err = np.abs(got.astype(np.float64) - ref[:, 0, :])
+        # the chain amplifies the per-step 1e-4 bound; its output is tanh-bounded
+        assert float(err.max()) <= 2e-4, f"max err {float(err.max()):.3e}"
+        # a wrong waveform shape is the reference's shape error
+        bad = voxq.host_tensor(np.zeros((B, ref.shape[2] + 1), np.float32))
+        keep.append(bad)
+        assert lib.voxq_vae_decode(ops, len(ops_spec), C.c_float(1.0), host(z), bad) == voxq.SHAPE_MISMATCH
+    finally:
+        for t in keep:
+            if isinstance(t, C.POINTER(voxq.Tensor)):
+                voxq.free_tensor(t)

@@ -95,7 +95,7 @@ def test_unchanged_engine_on_libvoxq_matches_cpu_engine():
         _, got_cpu_vae, host_audio = runs["cpu"]
     finally:
         shutil.rmtree(work, ignore_errors=True)
-    assert run["build"] == "gpu" and run["vae"] == "gpu"
+    assert run["build"] == "gpu" and run["vae"] == "device"
     # every transformer block (TSLM, RALM, LocDiT, LocEnc) ran on the device
     assert run["blocks"]["device"] > 0 and run["blocks"]["host"] == 0, run["blocks"]
     mm = run["stages"]["tensor_matmul_nt"]

@@ -20,6 +20,7 @@
 // keyed by pointer, size and a content fingerprint.
 #include <mutex>
 #include <unordered_map>
+#include <utility>
 
 #include "voxq_common.cuh"
 #include "voxq_internal.h"
@@ -92,6 +93,43 @@ __global__ void __launch_bounds__(kConvThreads) convt1d_kernel(const float* __re
 #pragma unroll
     for (int j = 0; j < kTPT; j++)
         if (t0 + j < Tout) on[t0 + j] = acc[j] + (b ? b[o] : 0.0f);
+}
+
+// h = h + sin(alpha[c] h)^2 / beta over [B][C][T] (snake_forward).
+__global__ void snake_kernel(float* __restrict__ h, const float* __restrict__ alpha, int C, int T, float beta,
+                             int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)((i / T) % C);
+        const float v = h[i];
+        const float sn = sinf(alpha[c] * v);
+        h[i] = v + (sn * sn) / beta;
+    }
+}
+
+__global__ void add_kernel(float* __restrict__ h, const float* __restrict__ r, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        h[i] = h[i] + r[i];
+}
+
+__global__ void tanh_kernel(float* __restrict__ h, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        h[i] = tanhf(h[i]);
+}
+
+// [B][T][D] -> [B][D][T]
+__global__ void btd_to_bdt_kernel(const float* __restrict__ x, float* __restrict__ y, int T, int D, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i % T);
+        const int64_t r = i / T;
+        const int d = (int)(r % D);
+        const int64_t b = r / D;
+        y[i] = x[(b * T + t) * D + d];
+    }
+}
+
+static int ew_grid(int64_t n) {
+    const int64_t g = (n + 255) / 256;
+    return (int)(g < 4096 ? (g > 0 ? g : 1) : 4096);
 }
 
 namespace {
@@ -194,10 +232,20 @@ VoxCPMError run_conv(const Tensor* x, Tensor* out, cudaStream_t st, Launch launc
     return VOXCPM_SUCCESS;
 }
 
+// The decoder's resident activations: current, next, and a residual
+// sub-block's saved input (each as large as the largest activation).
+float* g_vae_buf[3] = {nullptr, nullptr, nullptr};
+size_t g_vae_n = 0;
+
 }  // namespace
 
 void conv_cache_clear() {
     std::lock_guard<std::mutex> lk(g_conv_mu);
+    for (int k = 0; k < 3; k++) {
+        if (g_vae_buf[k]) cudaFree(g_vae_buf[k]);
+        g_vae_buf[k] = nullptr;
+    }
+    g_vae_n = 0;
     for (auto& kv : g_conv_w) cudaFree(kv.second.p);
     g_conv_w.clear();
     for (int k = 0; k < 2; k++) {
@@ -263,4 +311,118 @@ extern "C" VoxCPMError voxq_conv1d_transpose_forward(const voxq_conv1d_transpose
                         (unsigned)((Cout + kConvThreads / 32 - 1) / (kConvThreads / 32)), (unsigned)B);
         convt1d_kernel<<<grid, kConvThreads, 0, st>>>(d_x, d_w, d_b, d_o, Cin, Tin, Cout, Tout, Kw, stride, pad);
     });
+}
+
+extern "C" VoxCPMError voxq_vae_decode(const voxq_vae_op* ops, int n_ops, float snake_beta, const Tensor* latent,
+                                       Tensor* waveform) {
+    if (!ops || n_ops < 0 || !latent || !waveform) return VOXCPM_ERR_INTERNAL;
+    cudaStream_t st = (cudaStream_t)library_stream();
+    if (!st) return VOXCPM_ERR_CUDA_NOT_FOUND;
+    if (latent->ndim != 3 || latent->is_cuda || latent->is_fp16 || !latent->data) return VOXCPM_ERR_SHAPE_MISMATCH;
+    if (waveform->is_cuda || waveform->is_fp16 || !waveform->data) return VOXCPM_ERR_SHAPE_MISMATCH;
+    const int B = latent->shape[0], T0 = latent->shape[1], D0 = latent->shape[2];
+    // shapes of every step first (the checks of conv1d_forward / conv1d_transpose_forward / snake_forward)
+    int C = D0, T = T0;
+    size_t most = (size_t)B * C * T;
+    for (int i = 0; i < n_ops; i++) {
+        const voxq_vae_op& op = ops[i];
+        if (op.kind == VOXQ_VAE_CONV) {
+            const voxq_conv1d_desc* c = op.conv;
+            if (!c || !c->weight || c->in_channels != C || c->stride < 1 || c->kernel_size < 1)
+                return VOXCPM_ERR_SHAPE_MISMATCH;
+            T = (T + 2 * c->padding - c->kernel_size) / c->stride + 1;
+            C = c->out_channels;
+        } else if (op.kind == VOXQ_VAE_CONVT) {
+            const voxq_conv1d_transpose_desc* c = op.convt;
+            if (!c || !c->weight || c->in_channels != C || c->stride < 1 || c->kernel_size < 1)
+                return VOXCPM_ERR_SHAPE_MISMATCH;
+            T = (T - 1) * c->stride - 2 * c->padding + c->kernel_size;
+            C = c->out_channels;
+        } else if (op.kind == VOXQ_VAE_SNAKE) {
+            if (!op.alpha || op.alpha->is_fp16 || op.alpha->size < (size_t)C) return VOXCPM_ERR_SHAPE_MISMATCH;
+        } else if (op.kind < VOXQ_VAE_SAVE || op.kind > VOXQ_VAE_TANH) {
+            return VOXCPM_ERR_INTERNAL;
+        }
+        if (T <= 0 || C <= 0) return VOXCPM_ERR_SHAPE_MISMATCH;
+        const size_t n = (size_t)B * C * T;
+        if (n > most) most = n;
+    }
+    if (C != 1) return VOXCPM_ERR_SHAPE_MISMATCH;
+    const int samples = T;
+    if (waveform->ndim == 2) {
+        if (waveform->shape[0] != B || waveform->shape[1] != samples) return VOXCPM_ERR_SHAPE_MISMATCH;
+    } else if (waveform->ndim == 1) {
+        if (B != 1 || waveform->size < (size_t)samples) return VOXCPM_ERR_SHAPE_MISMATCH;
+    } else {
+        return VOXCPM_ERR_SHAPE_MISMATCH;
+    }
+    {
+        std::lock_guard<std::mutex> lk(g_conv_mu);
+        if (g_vae_n < most) {
+            cudaStreamSynchronize(st);
+            for (int k = 0; k < 3; k++) {
+                if (g_vae_buf[k]) cudaFree(g_vae_buf[k]);
+                g_vae_buf[k] = nullptr;
+            }
+            g_vae_n = 0;
+            for (int k = 0; k < 3; k++) VOXQ_CUDA_TRY(cudaMalloc(&g_vae_buf[k], most * sizeof(float)));
+            g_vae_n = most;
+        }
+    }
+    float *cur = g_vae_buf[0], *nxt = g_vae_buf[1], *saved = g_vae_buf[2];
+    // latent [B][T][D] -> h [B][D][T] (staged through `nxt`)
+    const int64_t n0 = (int64_t)B * T0 * D0;
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(nxt, latent->data, (size_t)n0 * sizeof(float), cudaMemcpyHostToDevice, st));
+    btd_to_bdt_kernel<<<ew_grid(n0), 256, 0, st>>>(nxt, cur, T0, D0, n0);
+    VOXQ_CUDA_TRY(cudaGetLastError());
+    C = D0;
+    T = T0;
+    int saved_c = -1, saved_t = -1;
+    for (int i = 0; i < n_ops; i++) {
+        const voxq_vae_op& op = ops[i];
+        const int64_t n = (int64_t)B * C * T;
+        if (op.kind == VOXQ_VAE_CONV || op.kind == VOXQ_VAE_CONVT) {
+            const int Cout = op.kind == VOXQ_VAE_CONV ? op.conv->out_channels : op.convt->out_channels;
+            const int Tout = op.kind == VOXQ_VAE_CONV
+                                 ? (T + 2 * op.conv->padding - op.conv->kernel_size) / op.conv->stride + 1
+                                 : (T - 1) * op.convt->stride - 2 * op.convt->padding + op.convt->kernel_size;
+            int sx[3] = {B, C, T}, so[3] = {B, Cout, Tout};
+            Tensor tx = {}, to = {};
+            tx.data = cur;
+            tx.shape = sx;
+            tx.ndim = 3;
+            tx.size = (size_t)n;
+            tx.is_cuda = true;
+            to.data = nxt;
+            to.shape = so;
+            to.ndim = 3;
+            to.size = (size_t)B * Cout * Tout;
+            to.is_cuda = true;
+            const VoxCPMError e = op.kind == VOXQ_VAE_CONV ? voxq_conv1d_forward(op.conv, &tx, &to)
+                                                           : voxq_conv1d_transpose_forward(op.convt, &tx, &to);
+            if (e) return e;
+            std::swap(cur, nxt);  // the saved input is a third buffer, never written here
+            C = Cout;
+            T = Tout;
+        } else if (op.kind == VOXQ_VAE_SNAKE) {
+            const float* a = nullptr;
+            const VoxCPMError e = weight_ptr(op.alpha, st, &a);  // host alpha, uploaded once
+            if (e) return e;
+            snake_kernel<<<ew_grid(n), 256, 0, st>>>(cur, a, C, T, snake_beta, n);
+        } else if (op.kind == VOXQ_VAE_SAVE) {
+            VOXQ_CUDA_TRY(cudaMemcpyAsync(saved, cur, (size_t)n * sizeof(float), cudaMemcpyDeviceToDevice, st));
+            saved_c = C;
+            saved_t = T;
+        } else if (op.kind == VOXQ_VAE_ADD_SAVED) {
+            if (saved_c != C || saved_t != T) return VOXCPM_ERR_SHAPE_MISMATCH;
+            add_kernel<<<ew_grid(n), 256, 0, st>>>(cur, saved, n);
+        } else if (op.kind == VOXQ_VAE_TANH) {
+            tanh_kernel<<<ew_grid(n), 256, 0, st>>>(cur, n);
+        }
+        VOXQ_CUDA_TRY(cudaGetLastError());
+    }
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(waveform->data, cur, (size_t)B * samples * sizeof(float), cudaMemcpyDeviceToHost,
+                                  st));
+    VOXQ_CUDA_TRY(cudaStreamSynchronize(st));
+    return VOXCPM_SUCCESS;
 }

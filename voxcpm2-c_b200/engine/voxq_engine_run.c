@@ -117,9 +117,10 @@ VoxCPMError __wrap_loc_enc_forward(const LocEnc* enc, const Tensor* feats, Tenso
 }
 
 VoxCPMError __real_audio_vae_decode(const AudioVAE* vae, const Tensor* z, Tensor* out);
+static VoxCPMError vae_decode(const AudioVAE* vae, const Tensor* z, Tensor* out);
 VoxCPMError __wrap_audio_vae_decode(const AudioVAE* vae, const Tensor* z, Tensor* out) {
     VoxCPMError r;
-    TIMED(ST_VAE, __real_audio_vae_decode(vae, z, out));
+    TIMED(ST_VAE, vae_decode(vae, z, out));
     return r;
 }
 
@@ -193,9 +194,95 @@ VoxCPMError __wrap_loc_dit_sample(const LocDiT* dit, const Tensor* mu, const Ten
 }
 
 #ifdef VOXQ_ENGINE_LIBVOXQ
+/* AudioVAE decode.  VOXQ_ENGINE_VAE = device (default): the whole decoder on
+ * the device with its activation resident (voxq_vae_decode, steps listed from
+ * the engine's AudioVAEDecoder in the order audio_vae_decode runs them,
+ * src/audio_vae.c:941-1116); convs: the engine's own decoder with only its
+ * convolutions on the device (conv1d_forward / conv1d_transpose_forward
+ * below); cpu: all on the host. */
+static int g_vae_gpu = 1;     /* convolutions go to the device */
+static int g_vae_whole = 1;   /* the whole decoder goes to the device */
+static const float kSnakeBeta = 1.0f;  /* AUDIOVAE_SNAKE_BETA, src/audio_vae.c:39 */
+
+static int wn_desc(const WNConv* wn, voxq_vae_op* op, voxq_conv1d_desc* c, voxq_conv1d_transpose_desc* t) {
+    /* wnconv_forward (src/audio_vae.c:279-305): the effective weight and the bias */
+    if (!wn || !wn->effective_weight) return 0;
+    memset(op, 0, sizeof(*op));
+    if (wn->is_transpose) {
+        *t = (voxq_conv1d_transpose_desc){wn->effective_weight, wn->bias, wn->in_channels, wn->out_channels,
+                                          wn->kernel_size, wn->stride, wn->padding};
+        op->kind = VOXQ_VAE_CONVT;
+        op->convt = t;
+    } else {
+        *c = (voxq_conv1d_desc){wn->effective_weight, wn->bias, wn->in_channels, wn->out_channels,
+                                wn->kernel_size, wn->stride, wn->padding, wn->groups};
+        op->kind = VOXQ_VAE_CONV;
+        op->conv = c;
+    }
+    return 1;
+}
+
+static VoxCPMError vae_decode_device(const AudioVAE* vae, const Tensor* z, Tensor* out) {
+    enum { kMaxOps = 256, kMaxConvs = 128 };
+    voxq_vae_op ops[kMaxOps];
+    voxq_conv1d_desc cd[kMaxConvs];
+    voxq_conv1d_transpose_desc td[kMaxConvs];
+    int n = 0, nc = 0;
+    const AudioVAEDecoder* d = vae ? vae->decoder : NULL;
+    if (!d || !z || z->ndim != 3 || z->shape[2] != vae->latent_dim) return VOXCPM_ERR_CUDA_NOT_FOUND;
+#define CONV(wn)                                                                     \
+    do {                                                                             \
+        if (n >= kMaxOps || nc >= kMaxConvs || !wn_desc((wn), &ops[n], &cd[nc], &td[nc])) \
+            return VOXCPM_ERR_CUDA_NOT_FOUND;                                        \
+        n++;                                                                         \
+        nc++;                                                                        \
+    } while (0)
+#define STEP(k, a)                                                                   \
+    do {                                                                             \
+        if (n >= kMaxOps) return VOXCPM_ERR_CUDA_NOT_FOUND;                          \
+        memset(&ops[n], 0, sizeof(ops[n]));                                          \
+        ops[n].kind = (k);                                                           \
+        ops[n].alpha = (a);                                                          \
+        n++;                                                                         \
+    } while (0)
+    CONV(d->conv_in);
+    CONV(d->proj_up);
+    for (int i = 0; i < AUDIOVAE_NUM_DECODER_BLOCKS; i++) {  /* decoder_block_forward */
+        const AudioVAEDecoderBlock* b = &d->decoder_blocks[i];
+        if (b->snake_alpha) STEP(VOXQ_VAE_SNAKE, b->snake_alpha);
+        CONV(b->convtr);
+        for (int j = 0; j < b->num_res_blocks && j < AUDIOVAE_RES_BLOCKS_PER_BLOCK; j++) {  /* residual_sub_block_forward */
+            const AudioVAEResBlock* rb = &b->res_blocks[j];
+            STEP(VOXQ_VAE_SAVE, NULL);
+            if (rb->snake_alpha1) STEP(VOXQ_VAE_SNAKE, rb->snake_alpha1);
+            CONV(rb->conv_depthwise);
+            if (rb->snake_alpha2) STEP(VOXQ_VAE_SNAKE, rb->snake_alpha2);
+            CONV(rb->conv_pointwise);
+            STEP(VOXQ_VAE_ADD_SAVED, NULL);
+        }
+    }
+    if (d->final_snake_alpha) STEP(VOXQ_VAE_SNAKE, d->final_snake_alpha);
+    CONV(d->conv_out);
+    STEP(VOXQ_VAE_TANH, NULL);
+#undef CONV
+#undef STEP
+    return voxq_vae_decode(ops, n, kSnakeBeta, z, out);
+}
+#endif
+
+static VoxCPMError vae_decode(const AudioVAE* vae, const Tensor* z, Tensor* out) {
+#ifdef VOXQ_ENGINE_LIBVOXQ
+    if (g_vae_whole) {
+        const VoxCPMError r = vae_decode_device(vae, z, out);
+        if (r != VOXCPM_ERR_CUDA_NOT_FOUND) return r;
+    }
+#endif
+    return __real_audio_vae_decode(vae, z, out);
+}
+
+#ifdef VOXQ_ENGINE_LIBVOXQ
 /* Conv1D / Conv1DTranspose (include/nn.h:198-229) and voxq's descriptors have
  * the same layout. */
-static int g_vae_gpu = 1;
 VoxCPMError __real_conv1d_forward(const Conv1D* conv, const Tensor* x, Tensor* out);
 VoxCPMError __wrap_conv1d_forward(const Conv1D* conv, const Tensor* x, Tensor* out) {
     if (g_vae_gpu) {
@@ -399,7 +486,11 @@ int main(int argc, char** argv) {
     if (mm_log && *mm_log) g_mm_log = fopen(mm_log, "w");
     g_dump_calls = getenv("VOXQ_ENGINE_DUMP_CALL");
 #ifdef VOXQ_ENGINE_LIBVOXQ
-    if (getenv("VOXQ_ENGINE_VAE") && !strcmp(getenv("VOXQ_ENGINE_VAE"), "cpu")) g_vae_gpu = 0;
+    {
+        const char* v = getenv("VOXQ_ENGINE_VAE");
+        if (v && !strcmp(v, "cpu")) g_vae_gpu = g_vae_whole = 0;
+        if (v && !strcmp(v, "convs")) g_vae_whole = 0;
+    }
     if (getenv("VOXQ_ENGINE_BLOCK") && !strcmp(getenv("VOXQ_ENGINE_BLOCK"), "cpu")) g_block_gpu = 0;
 #endif
     g_dump_dir = getenv("VOXQ_ENGINE_DUMP_DIR");
@@ -490,7 +581,7 @@ int main(int argc, char** argv) {
            "cpu",
 #endif
 #ifdef VOXQ_ENGINE_LIBVOXQ
-           g_vae_gpu ? "gpu" : "cpu",
+           g_vae_whole ? "device" : g_vae_gpu ? "convs" : "cpu",
 #else
            "cpu",
 #endif

@@ -103,6 +103,12 @@ class Vxcpm2Tensor(C.Structure):
                 ("group", C.c_int32), ("elements", C.c_uint64), ("offset", C.c_uint64), ("bytes", C.c_uint64)]
 
 
+class VaeOp(C.Structure):
+    """voxq_vae_op (include/voxq.h)."""
+    _fields_ = [("kind", C.c_int), ("conv", C.POINTER(Conv1dDesc)), ("convt", C.POINTER(Conv1dTransposeDesc)),
+                ("alpha", C.POINTER(Tensor))]
+
+
 class RmsNormDesc(C.Structure):
     """voxq_rmsnorm_desc (include/voxq.h; the engine's RmsNorm)."""
     _fields_ = [("weight", C.POINTER(Tensor)), ("eps", C.c_float)]
@@ -158,6 +164,7 @@ SIGNATURES = {
     "voxq_conv1d_forward": ([C.POINTER(Conv1dDesc), _TP, _TP], _i),
     "voxq_conv1d_transpose_forward": ([C.POINTER(Conv1dTransposeDesc), _TP, _TP], _i),
     "voxq_conv_cache_clear": ([], None),
+    "voxq_vae_decode": ([C.POINTER(VaeOp), _i, C.c_float, _TP, _TP], _i),
     "voxq_transformer_block_forward": ([C.POINTER(BlockDesc), _TP, _TP, _TP, _TP, _TP, _i, _TP], _i),
     "voxq_block_cache_clear": ([], None),
     "voxq_vxcpm2_open": ([C.c_char_p, C.POINTER(_vp)], _i),
