@@ -964,6 +964,11 @@ def measure_c4(patches=4, workdir=None, cpu_patches=0, model=None):
                            "10 Euler steps, CFG 2.0, random-init model (Q8-exact projection weights)",
                "model_gen_s": gen["gen_s"], "model_bytes": gen["model_bytes"] + gen["audiovae_bytes"]}
         out["ours"] = _engine_run("voxq_engine_run_gpu", model, patches, {"VOXCPM_QUANT": "q8"}, ["--gpu"])
+        # the full config: 200 patches (max_new_tokens 800); the RALM cache (about 52 positions
+        # per patch) set past the 2048 positions voxcpm_generate fixes (src/model.c:709), the one
+        # engine deviation
+        out["ours_200_patches"] = _engine_run("voxq_engine_run_gpu", model, 200, {"VOXCPM_QUANT": "q8"},
+                                              ["--gpu", "--ralm-max-seq", "16384"])
         # the same build with the transformer blocks left to the engine's host code
         # (only their projections on the device), for comparison
         out["ours_blocks_on_host"] = _engine_run("voxq_engine_run_gpu", model, patches,
@@ -1016,7 +1021,10 @@ def engine_configs(args, dist, rank, world, local_rank):
                 out["c4"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
         utts = S.workload(C5_UTTERANCES_PER_GPU * world, patches=C5_PATCHES, seed=5)
         mine = [utts[i] for i in lpt_partition([S.cost(u) for u in utts], world)[rank]]
-        wpg = max(1, min(4, (os.cpu_count() or 8) // (2 * world)))
+        # one engine process per GPU: with the blocks and the AudioVAE on the device the work is
+        # GPU-side, and further processes only time-slice the GPU between their contexts
+        # (16 utterances, 1 / 2 / 4 / 8 workers on one B200: 5.2 / 3.3 / 3.3 / 2.9 utt/s)
+        wpg = 1
         try:
             res = measure_c5(model, local_rank, mine, wpg)
         except Exception as e:
@@ -1040,7 +1048,7 @@ def engine_configs(args, dist, rank, world, local_rank):
                     "metric": "c5_utterances_per_s", "value": round(answered / wall, 4), "unit": "utt/s",
                     "workload": f"BASELINE config 5 slice: {len(utts)} utterances ({C5_UTTERANCES_PER_GPU} per GPU, "
                                 f"token counts uniform in [32, 128], seeded ids), {C5_PATCHES} patches each, Q4, "
-                                "unchanged engine on libvoxq, LPT over GPUs and engine workers",
+                                "unchanged engine on libvoxq (transformer blocks and AudioVAE on the device), LPT over GPUs",
                     "scaling": "weak", "n_gpus": world, "workers_per_gpu": wpg, "answered": answered,
                     "wall_s_max": wall, "per_rank_wall_s": [r["wall_s"] for r in allres],
                     "GBps_per_gpu": {g: v["GBps"] for g, v in per_gpu.items()},

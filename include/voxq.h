@@ -136,10 +136,11 @@ VOXQ_API VoxCPMError voxq_set_device(int device);
  * word cannot be read. */
 VOXQ_API int voxq_device_error(int clear);
 
-/* Work counted by tensor_matmul_nt_cuda in this process, all devices: calls,
- * and the weight bytes those calls streamed (packed codes + scales of a
- * quantized weight, 4 or 2 bytes per element of a dense one).  reset != 0
- * zeroes both counters after reading them.  Either pointer may be NULL. */
+/* Projections run in this process, all devices -- tensor_matmul_nt_cuda
+ * calls and the seven of every voxq_transformer_block_forward call -- and the
+ * weight bytes they streamed (packed codes + scales of a quantized weight, 4
+ * or 2 bytes per element of a dense one).  reset != 0 zeroes both counters
+ * after reading them.  Either pointer may be NULL. */
 VOXQ_API void voxq_matmul_traffic(uint64_t* calls, uint64_t* weight_bytes, int reset);
 
 /* Failure-detection self-test (no counterpart in the reference): launches one

@@ -578,6 +578,12 @@ extern "C" VoxCPMError voxq_transformer_block_forward(const voxq_block_desc* blk
         for (int bk = 0; bk < B * KVH; bk++)
             memcpy(dst + ((size_t)bk * max_seq + pos) * hd, src + (size_t)bk * seq * hd, (size_t)seq * hd * sizeof(float));
     }
+    {
+        uint64_t wb = 0;
+        for (const voxq_qweight* w : {&wq, &wk, &wv, &wo, &w1, &w2, &w3})
+            wb += voxq_codes_bytes(w->N, w->K, w->qtype) + voxq_scales_bytes(w->N, w->K, w->qtype);
+        count_matmul_traffic(7, wb);
+    }
     mr->valid = L;
     mr->last_row.assign(cache_k->data + (size_t)(L - 1) * hd, cache_k->data + (size_t)L * hd);
     return VOXCPM_SUCCESS;

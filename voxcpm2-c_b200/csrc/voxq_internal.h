@@ -58,6 +58,10 @@ void conv_cache_clear();
 // its device pointer); false for any other tensor (voxq_runtime.cu).
 bool device_qweight(const Tensor* w, voxq_qweight* out);
 
+// Adds to the counters voxq_matmul_traffic reports (projections the library
+// runs on behalf of an engine call other than tensor_matmul_nt_cuda).
+void count_matmul_traffic(uint64_t calls, uint64_t weight_bytes);
+
 // binary16 -> binary32 on the host, as include/tensor.h:350-371 (voxq_container.cu).
 float half_to_float(uint16_t h);
 

@@ -192,6 +192,11 @@ extern "C" const char* voxq_version(void) { return "voxq-b200 0.1 (sm_100a)"; }
 // tensor_matmul_nt_cuda's work counters (voxq_matmul_traffic)
 static std::atomic<uint64_t> g_mm_calls{0}, g_mm_wbytes{0};
 
+void voxq::count_matmul_traffic(uint64_t calls, uint64_t weight_bytes) {
+    g_mm_calls.fetch_add(calls, std::memory_order_relaxed);
+    g_mm_wbytes.fetch_add(weight_bytes, std::memory_order_relaxed);
+}
+
 extern "C" void voxq_matmul_traffic(uint64_t* calls, uint64_t* weight_bytes, int reset) {
     const uint64_t c = reset ? g_mm_calls.exchange(0) : g_mm_calls.load();
     const uint64_t b = reset ? g_mm_wbytes.exchange(0) : g_mm_wbytes.load();
