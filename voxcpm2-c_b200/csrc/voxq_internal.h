@@ -15,6 +15,10 @@ int current_device();
 // Programmatic dependent launch on the voxq kernels (VOXQ_PDL=0 disables).
 bool pdl_enabled();
 
+// Largest activation-row count the quantized matmul runs as GEMVs (groups of
+// 8 rows in one launch) instead of the tensor-core GEMM (VOXQ_GEMV_ROWS_MAX).
+int gemv_rows_max();
+
 // Grouped / single GEMV (voxq_gemv.cu).
 VoxCPMError validate_item(const voxq_gemv_item& x);
 VoxCPMError gemv_launch(const voxq_gemv_item* items, int count, cudaStream_t st);

@@ -73,6 +73,15 @@ int device_sm_count() {
     return g_dev[d].sms;
 }
 
+int gemv_rows_max() {
+    static const int v = [] {
+        const char* e = getenv("VOXQ_GEMV_ROWS_MAX");
+        const int r = e ? atoi(e) : 8;
+        return r >= 8 && r <= 64 ? r / 8 * 8 : 8;
+    }();
+    return v;
+}
+
 bool pdl_enabled() {
     static int v = -1;
     if (v < 0) {
@@ -234,24 +243,31 @@ extern "C" VoxCPMError voxq_matmul_nt_q(const float* d_a, int M, int64_t lda, co
     if (up && (up->N != w->N || up->K != w->K || up->qtype != w->qtype || up->q8_signed != w->q8_signed))
         return VOXCPM_ERR_SHAPE_MISMATCH;
     cudaStream_t st = (cudaStream_t)stream;
-    if (M <= 8) {
-        voxq_gemv_item it = {};
-        it.w = *w;
-        it.a = d_a;
-        it.out = d_out;
-        it.M = M;
-        it.lda = (int32_t)lda;
-        it.ldo = (int32_t)ldo;
-        if (epi) {
-            it.bias = epi->bias;
-            it.residual = epi->residual;
-            it.ldr = (int32_t)epi->ldr;
-            if (up) {
-                it.up_codes = up->codes;
-                it.up_scales = up->scales;
+    if (M <= gemv_rows_max()) {
+        // groups of up to 8 activation rows, one GEMV item each, in one launch
+        voxq_gemv_item its[VOXQ_MAX_BATCH / 2];
+        const int groups = (M + 7) / 8;
+        for (int g = 0; g < groups; g++) {
+            voxq_gemv_item& it = its[g];
+            it = voxq_gemv_item{};
+            const int m0 = 8 * g;
+            it.w = *w;
+            it.a = d_a + (int64_t)m0 * lda;
+            it.out = d_out + (int64_t)m0 * ldo;
+            it.M = M - m0 < 8 ? M - m0 : 8;
+            it.lda = (int32_t)lda;
+            it.ldo = (int32_t)ldo;
+            if (epi) {
+                it.bias = epi->bias;
+                it.residual = epi->residual ? epi->residual + (int64_t)m0 * epi->ldr : nullptr;
+                it.ldr = (int32_t)epi->ldr;
+                if (up) {
+                    it.up_codes = up->codes;
+                    it.up_scales = up->scales;
+                }
             }
         }
-        return gemv_launch(&it, 1, st);
+        return gemv_launch(its, groups, st);
     }
     void* ws = workspace(gemm_workspace_bytes(M, w->N, w->K, w->qtype, up != nullptr));
     if (!ws) return VOXCPM_ERR_OOM;
@@ -536,7 +552,7 @@ extern "C" VoxCPMError tensor_matmul_nt_cuda(const Tensor* a, const Tensor* b, T
     const size_t o_bytes = (size_t)M * N * sizeof(float);
     float* d_o = out->data;
     auto qit = b->is_cuda && b->data ? g_qtab.find(b->data) : g_qtab.end();
-    const bool direct_out = !out->is_cuda && qit != g_qtab.end() && M <= 8;
+    const bool direct_out = !out->is_cuda && qit != g_qtab.end() && M <= gemv_rows_max();
     if (direct_out) {
         if (!pinned_get(&s->h_out, &s->h_out_bytes, o_bytes)) return VOXCPM_ERR_OOM;
         d_o = (float*)s->h_out;
@@ -552,7 +568,7 @@ extern "C" VoxCPMError tensor_matmul_nt_cuda(const Tensor* a, const Tensor* b, T
         voxq_qweight w = {q.codes, q.scales, q.N, q.K, q.qtype, 0};
         g_mm_wbytes.fetch_add(voxq_codes_bytes(q.N, q.K, q.qtype) + voxq_scales_bytes(q.N, q.K, q.qtype),
                               std::memory_order_relaxed);
-        if (M > 8) {
+        if (M > gemv_rows_max()) {
             void* ws = slot_get(*s, 3, gemm_workspace_bytes(M, N, K, q.qtype, false));
             if (!ws) return VOXCPM_ERR_OOM;
             lk.unlock();
