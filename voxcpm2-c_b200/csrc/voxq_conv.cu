@@ -18,6 +18,7 @@
 // through the library stream; host weights are uploaded once per pointer and
 // kept (the AudioVAE's effective weights are fixed for the model's lifetime),
 // keyed by pointer, size and a content fingerprint.
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
 #include <utility>
@@ -33,19 +34,23 @@ constexpr int kConvThreads = 256;  // 8 output channels per block
 __global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                               const float* __restrict__ b, float* __restrict__ out,
                                                               int Cin, int Tin, int Cout, int Tout, int Kw, int stride,
-                                                              int pad, int groups) {
+                                                              int pad, int groups, int splits) {
+    // blockIdx.z = n * splits + part: with splits > 1 the CTA sums one slice of
+    // its group's input channels and writes a partial ([part][n][o][t], no
+    // bias) for split_sum_kernel; with one split it writes out directly
     const int o = blockIdx.y * (kConvThreads / 32) + (threadIdx.x >> 5);
-    const int n = blockIdx.z;
+    const int n = blockIdx.z / splits, sp = blockIdx.z % splits;
     const int t0 = (blockIdx.x * 32 + (threadIdx.x & 31)) * kTPT;
     if (o >= Cout || t0 >= Tout) return;
     const int ipg = Cin / groups, opg = Cout / groups;
     const int c0 = (o / opg) * ipg;
+    const int per = (ipg + splits - 1) / splits, cb = sp * per, ce = min(ipg, cb + per);
     const float* xn = x + (int64_t)n * Cin * Tin;
     const float* wo = w + (int64_t)o * ipg * Kw;
     float acc[kTPT];
 #pragma unroll
-    for (int j = 0; j < kTPT; j++) acc[j] = b ? b[o] : 0.0f;
-    for (int c = 0; c < ipg; c++) {
+    for (int j = 0; j < kTPT; j++) acc[j] = (b && splits == 1) ? b[o] : 0.0f;
+    for (int c = cb; c < ce; c++) {
         const float* xc = xn + (int64_t)(c0 + c) * Tin;
         const float* wc = wo + c * Kw;
         for (int k = 0; k < Kw; k++) {
@@ -57,7 +62,8 @@ __global__ void __launch_bounds__(kConvThreads) conv1d_kernel(const float* __res
             }
         }
     }
-    float* on = out + ((int64_t)n * Cout + o) * Tout;
+    const int B = gridDim.z / splits;
+    float* on = out + (((int64_t)sp * B + n) * Cout + o) * Tout;
 #pragma unroll
     for (int j = 0; j < kTPT; j++)
         if (t0 + j < Tout) on[t0 + j] = acc[j];
@@ -67,16 +73,18 @@ __global__ void __launch_bounds__(kConvThreads) convt1d_kernel(const float* __re
                                                                const float* __restrict__ w,
                                                                const float* __restrict__ b, float* __restrict__ out,
                                                                int Cin, int Tin, int Cout, int Tout, int Kw,
-                                                               int stride, int pad) {
+                                                               int stride, int pad, int splits) {
+    // blockIdx.z = n * splits + part, as in conv1d_kernel
     const int o = blockIdx.y * (kConvThreads / 32) + (threadIdx.x >> 5);
-    const int n = blockIdx.z;
+    const int n = blockIdx.z / splits, sp = blockIdx.z % splits;
     const int t0 = (blockIdx.x * 32 + (threadIdx.x & 31)) * kTPT;
     if (o >= Cout || t0 >= Tout) return;
+    const int per = (Cin + splits - 1) / splits, cb = sp * per, ce = min(Cin, cb + per);
     const float* xn = x + (int64_t)n * Cin * Tin;
     float acc[kTPT];
 #pragma unroll
     for (int j = 0; j < kTPT; j++) acc[j] = 0.0f;
-    for (int c = 0; c < Cin; c++) {
+    for (int c = cb; c < ce; c++) {
         const float* xc = xn + (int64_t)c * Tin;
         const float* wc = w + ((int64_t)c * Cout + o) * Kw;
 #pragma unroll
@@ -89,10 +97,21 @@ __global__ void __launch_bounds__(kConvThreads) convt1d_kernel(const float* __re
             }
         }
     }
-    float* on = out + ((int64_t)n * Cout + o) * Tout;
+    const int B = gridDim.z / splits;
+    float* on = out + (((int64_t)sp * B + n) * Cout + o) * Tout;
 #pragma unroll
     for (int j = 0; j < kTPT; j++)
-        if (t0 + j < Tout) on[t0 + j] = acc[j] + (b ? b[o] : 0.0f);
+        if (t0 + j < Tout) on[t0 + j] = acc[j] + ((b && splits == 1) ? b[o] : 0.0f);
+}
+
+// out[n][o][t] = (bias[o] + part[0][n][o][t]) + part[1][n][o][t] + ... (fixed order)
+__global__ void split_sum_kernel(const float* __restrict__ part, const float* __restrict__ b, float* __restrict__ out,
+                                 int Cout, int Tout, int splits, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        float r = b ? b[(int)((i / Tout) % Cout)] : 0.0f;
+        for (int sp = 0; sp < splits; sp++) r += part[(int64_t)sp * n + i];
+        out[i] = r;
+    }
 }
 
 // h = h + sin(alpha[c] h)^2 / beta over [B][C][T] (snake_forward).
@@ -187,6 +206,38 @@ VoxCPMError weight_ptr(const Tensor* t, cudaStream_t st, const float** out) {
     return VOXCPM_SUCCESS;
 }
 
+// Input-channel splits for a convolution whose outputs alone give too few
+// warps to keep the SMs' memory pipes busy (the decoder's first blocks: 1024
+// output channels x 32 steps, each warp walking 2048 channels): enough splits
+// for ~64 warps per SM, each split at least 16 channels, partials within 64 MB.
+float* g_conv_part = nullptr;
+size_t g_conv_part_n = 0;
+
+int conv_splits(int B, int Cout, int Tout, int chans) {
+    const int64_t warps = (int64_t)B * Cout * ((Tout + 32 * kTPT - 1) / (32 * kTPT));
+    const int64_t target = (int64_t)device_sm_count() * 64;
+    int64_t sp = (target + warps - 1) / warps;
+    sp = std::min<int64_t>(sp, std::max(1, chans / 16));
+    sp = std::min<int64_t>(sp, 64);
+    while (sp > 1 && sp * B * Cout * Tout > ((int64_t)16 << 20)) sp--;
+    return (int)std::max<int64_t>(sp, 1);
+}
+
+// The partials buffer (held under g_conv_mu); grows, draining the stream first.
+float* part_buf(size_t n, cudaStream_t st) {
+    if (g_conv_part_n >= n) return g_conv_part;
+    cudaStreamSynchronize(st);
+    if (g_conv_part) cudaFree(g_conv_part);
+    g_conv_part = nullptr;
+    g_conv_part_n = 0;
+    if (cudaMalloc(&g_conv_part, n * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    g_conv_part_n = n;
+    return g_conv_part;
+}
+
 float* io_buf(int k, size_t n) {
     if (g_conv_io_n[k] >= n) return g_conv_io[k];
     size_t want = 1 << 18;
@@ -222,7 +273,7 @@ VoxCPMError run_conv(const Tensor* x, Tensor* out, cudaStream_t st, Launch launc
         d_o = io_buf(1, out->size);
         if (!d_o) return VOXCPM_ERR_OOM;
     }
-    launch(d_x, d_o);
+    if (!launch(d_x, d_o)) return VOXCPM_ERR_OOM;
     VOXQ_CUDA_TRY(cudaGetLastError());
     if (!out->is_cuda) {
         VOXQ_CUDA_TRY(cudaMemcpyAsync(out->data, d_o, out->size * sizeof(float), cudaMemcpyDeviceToHost, st));
@@ -246,6 +297,9 @@ void conv_cache_clear() {
         g_vae_buf[k] = nullptr;
     }
     g_vae_n = 0;
+    if (g_conv_part) cudaFree(g_conv_part);
+    g_conv_part = nullptr;
+    g_conv_part_n = 0;
     for (auto& kv : g_conv_w) cudaFree(kv.second.p);
     g_conv_w.clear();
     for (int k = 0; k < 2; k++) {
@@ -280,11 +334,17 @@ extern "C" VoxCPMError voxq_conv1d_forward(const voxq_conv1d_desc* conv, const T
     VoxCPMError e = weight_ptr(conv->weight, st, &d_w);
     if (!e) e = weight_ptr(conv->bias, st, &d_b);
     if (e) return e;
-    return run_conv(x, out, st, [&](const float* d_x, float* d_o) {
+    const int splits = conv_splits(B, Cout, Tout, Cin / groups);
+    return run_conv(x, out, st, [&](const float* d_x, float* d_o) -> bool {
+        const size_t n = (size_t)B * Cout * Tout;
+        float* part = splits > 1 ? part_buf((size_t)splits * n, st) : nullptr;
+        if (splits > 1 && !part) return false;
         const dim3 grid((unsigned)((Tout + 32 * kTPT - 1) / (32 * kTPT)),
-                        (unsigned)((Cout + kConvThreads / 32 - 1) / (kConvThreads / 32)), (unsigned)B);
-        conv1d_kernel<<<grid, kConvThreads, 0, st>>>(d_x, d_w, d_b, d_o, Cin, Tin, Cout, Tout, Kw, stride, pad,
-                                                      groups);
+                        (unsigned)((Cout + kConvThreads / 32 - 1) / (kConvThreads / 32)), (unsigned)(B * splits));
+        conv1d_kernel<<<grid, kConvThreads, 0, st>>>(d_x, d_w, d_b, splits > 1 ? part : d_o, Cin, Tin, Cout, Tout, Kw,
+                                                      stride, pad, groups, splits);
+        if (splits > 1) split_sum_kernel<<<ew_grid((int64_t)n), 256, 0, st>>>(part, d_b, d_o, Cout, Tout, splits, (int64_t)n);
+        return true;
     });
 }
 
@@ -306,10 +366,17 @@ extern "C" VoxCPMError voxq_conv1d_transpose_forward(const voxq_conv1d_transpose
     VoxCPMError e = weight_ptr(conv->weight, st, &d_w);
     if (!e) e = weight_ptr(conv->bias, st, &d_b);
     if (e) return e;
-    return run_conv(x, out, st, [&](const float* d_x, float* d_o) {
+    const int splits = conv_splits(B, Cout, Tout, Cin);
+    return run_conv(x, out, st, [&](const float* d_x, float* d_o) -> bool {
+        const size_t n = (size_t)B * Cout * Tout;
+        float* part = splits > 1 ? part_buf((size_t)splits * n, st) : nullptr;
+        if (splits > 1 && !part) return false;
         const dim3 grid((unsigned)((Tout + 32 * kTPT - 1) / (32 * kTPT)),
-                        (unsigned)((Cout + kConvThreads / 32 - 1) / (kConvThreads / 32)), (unsigned)B);
-        convt1d_kernel<<<grid, kConvThreads, 0, st>>>(d_x, d_w, d_b, d_o, Cin, Tin, Cout, Tout, Kw, stride, pad);
+                        (unsigned)((Cout + kConvThreads / 32 - 1) / (kConvThreads / 32)), (unsigned)(B * splits));
+        convt1d_kernel<<<grid, kConvThreads, 0, st>>>(d_x, d_w, d_b, splits > 1 ? part : d_o, Cin, Tin, Cout, Tout, Kw,
+                                                       stride, pad, splits);
+        if (splits > 1) split_sum_kernel<<<ew_grid((int64_t)n), 256, 0, st>>>(part, d_b, d_o, Cout, Tout, splits, (int64_t)n);
+        return true;
     });
 }
 
