@@ -407,6 +407,50 @@ VOXQ_API VoxCPMError voxq_transformer_block_forward(const voxq_block_desc* block
 /* Drops the blocks' device cache mirrors, norm weights and staging. */
 VOXQ_API void voxq_block_cache_clear(void);
 
+/* ---- LocDiT sampler on the device ------------------------------------------
+ * loc_dit_sample (src/loc_dit.c:437-593) with loc_dit_forward
+ * (src/loc_dit.c:95-435) inside, the sequence resident on the device for the
+ * whole sampler: per Euler step t = 1 - i dt (dt = (1 - 1e-6) / n_timesteps),
+ * the time and delta embeddings (sinusoidal, interleaved sin / cos, then
+ * Linear-SiLU-Linear), the input projection of x_t, the sequence
+ * [mu; x_proj; cond_proj] + (time + delta), the n_layers transformer blocks
+ * (bidirectional, no RoPE), the output RMSNorm of the x rows and the output
+ * projection, then x_t -= dt * v.  With classifier-free guidance
+ * (cfg_value > 1 and a non-empty cond) the conditional and unconditional
+ * branches (cond replaced by zeros, so its projection is the bias) run as one
+ * batch of two sequences through every block and are combined as
+ * v = v_uncond + cfg (v_cond - v_uncond) -- the reference runs them as two
+ * forwards.  x_init [1, feat_dim, patch] is the starting noise (the reference
+ * draws it with tensor_rand_normal, seed 42); out [1, feat_dim, patch] (host)
+ * receives x after the last step.  The descriptor has the layout of the
+ * engine's LocDiT (include/model.h); its projection weights must be
+ * quantized device weights (VOXCPM_QUANT), biases and norm weights host
+ * tensors.  Returns VOXCPM_ERR_CUDA_NOT_FOUND (the caller then runs its host
+ * sampler) for anything else (batch other than 1, unquantized weights, ...). */
+typedef struct {
+    Tensor* in_proj_weight;  /* [d_model, feat_dim] */
+    Tensor* in_proj_bias;
+    Tensor* cond_proj_weight;  /* [d_model, feat_dim] */
+    Tensor* cond_proj_bias;
+    Tensor* out_proj_weight;  /* [feat_dim, d_model] */
+    Tensor* out_proj_bias;
+    Tensor* time_mlp_1_weight;  /* [d_model, d_model] */
+    Tensor* time_mlp_1_bias;
+    Tensor* time_mlp_2_weight;
+    Tensor* time_mlp_2_bias;
+    Tensor* delta_mlp_1_weight;
+    Tensor* delta_mlp_1_bias;
+    Tensor* delta_mlp_2_weight;
+    Tensor* delta_mlp_2_bias;
+    voxq_block_desc* layers;  /* n_layers blocks */
+    int n_layers;
+    voxq_rmsnorm_desc* output_norm;
+    int d_model;
+    int feat_dim;
+} voxq_locdit_desc;
+VOXQ_API VoxCPMError voxq_locdit_sample(const voxq_locdit_desc* dit, const Tensor* mu, const Tensor* cond,
+                                        int n_timesteps, float cfg_value, const Tensor* x_init, Tensor* out);
+
 /* ---- quantize.py weight containers (VXCPM2) ---------------------------
  * Reads the container written by the reference's quantizer
  * (scripts/quantize.py:110-312): a 256-byte header, the layer-group offset

@@ -20,6 +20,8 @@
 // kept identical (new rows written back), so a call that falls back to the
 // host code, or any other reader of the cache, sees the reference's state.
 #include <math.h>
+
+#include <algorithm>
 #include <string.h>
 
 #include <map>
@@ -94,12 +96,12 @@ __global__ void rope_cache_kernel(const float* __restrict__ q, const float* __re
         const int h = slot - H;
         src = k + ((int64_t)m * KVH + h) * hd;
         dst = ck + (((int64_t)b * KVH + h) * max_seq + pos + s) * hd;
-        dst2 = knew + (((int64_t)b * KVH + h) * seq + s) * hd;
+        if (knew) dst2 = knew + (((int64_t)b * KVH + h) * seq + s) * hd;
     } else {
         const int h = slot - H - KVH;
         src = v + ((int64_t)m * KVH + h) * hd;
         dst = cv + (((int64_t)b * KVH + h) * max_seq + pos + s) * hd;
-        dst2 = vnew + (((int64_t)b * KVH + h) * seq + s) * hd;
+        if (vnew) dst2 = vnew + (((int64_t)b * KVH + h) * seq + s) * hd;
         rope = false;
     }
     for (int i = threadIdx.x; i < half; i += blockDim.x) {
@@ -203,6 +205,77 @@ __global__ void cache_fill_kernel(const float* __restrict__ src, float* __restri
     }
 }
 
+// ---- LocDiT sampler kernels ----
+
+__global__ void silu_inplace_kernel(float* __restrict__ x, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        const float v = x[i];
+        x[i] = v / (1.0f + expf(-v));
+    }
+}
+
+__global__ void add_vec_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ c,
+                               int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) c[i] = a[i] + b[i];
+}
+
+// [rows][cols] -> [cols][rows]
+__global__ void transpose_kernel(const float* __restrict__ x, float* __restrict__ y, int rows, int cols) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < rows * cols) {
+        const int r = i / cols, c = i % cols;
+        y[(int64_t)c * rows + r] = x[i];
+    }
+}
+
+// The sequences of the nb branches, [nb][S][D] with S = 1 + P + Tc: row 0 mu,
+// rows 1..P the input projection, then the condition projection (branch 0)
+// or its bias alone (branch 1: the zero condition), each plus gc.
+__global__ void dit_seq_kernel(float* __restrict__ seq, const float* __restrict__ mu,
+                               const float* __restrict__ xproj, const float* __restrict__ crows,
+                               const float* __restrict__ cbias, const float* __restrict__ gc, int nb, int P, int Tc,
+                               int D) {
+    const int S = 1 + P + Tc;
+    const int64_t n = (int64_t)nb * S * D;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int d = (int)(i % D);
+        const int r = (int)((i / D) % S), j = (int)(i / ((int64_t)S * D));
+        float v;
+        if (r == 0) v = mu[d];
+        else if (r <= P) v = xproj[(int64_t)(r - 1) * D + d];
+        else v = j == 0 ? crows[(int64_t)(r - 1 - P) * D + d] : (cbias ? cbias[d] : 0.0f);
+        seq[i] = v + gc[d];
+    }
+}
+
+// x rows 1..P of every branch: [nb][S][D] -> [nb * P][D]
+__global__ void dit_slice_kernel(const float* __restrict__ seq, float* __restrict__ xs, int nb, int P, int S, int D) {
+    const int64_t n = (int64_t)nb * P * D;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int d = (int)(i % D);
+        const int p = (int)((i / D) % P), j = (int)(i / ((int64_t)P * D));
+        xs[i] = seq[((int64_t)j * S + 1 + p) * D + d];
+    }
+}
+
+// Euler step with guidance: v rows [nb * P][F] (branch 0 conditional);
+// x [F][P] -= dt * (v_u + cfg (v_c - v_u)) (or v_c alone).
+__global__ void dit_step_kernel(float* __restrict__ x, const float* __restrict__ v, int nb, int P, int F, float cfg,
+                                float dt) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= F * P) return;
+    const int f = i / P, p = i % P;
+    const float vc = v[(int64_t)p * F + f];
+    float pred = vc;
+    if (nb == 2) {
+        const float vu = v[(int64_t)(P + p) * F + f];
+        pred = vu + cfg * (vc - vu);
+    }
+    x[i] = x[i] - dt * pred;
+}
+
 namespace {
 
 // Device mirror of one host KV cache (K and V of one layer).
@@ -229,6 +302,8 @@ struct BlockDev {
     std::unordered_map<const void*, NormW> norms;     // host norm weight pointer -> device copy
     float* arena = nullptr;
     size_t arena_floats = 0;
+    float* dit_arena = nullptr;  // the LocDiT sampler's resident buffers
+    size_t dit_arena_floats = 0;
     float* h_stage = nullptr;  // pinned
     size_t h_stage_floats = 0;
     uint64_t clock = 0;
@@ -420,6 +495,136 @@ VoxCPMError project(const float* a, int M, int K, const voxq_qweight& w, float* 
     return voxq_matmul_nt_q(a, M, K, &w, out, w.N, (residual || up) ? &epi : nullptr, st);
 }
 
+// A block's resolved weights: the seven projections (quantized device
+// weights) and the two norm weights (device copies).
+struct BlockW {
+    voxq_qweight wq, wk, wv, wo, w1, w2, w3;
+    const float* wn1 = nullptr;
+    const float* wn2 = nullptr;
+    float eps1 = 0.f, eps2 = 0.f;
+    int D = 0, H = 0, KVH = 0, hd = 0, F = 0;
+};
+
+// false: not a block the device path takes (the caller runs the host code).
+bool block_weights(const voxq_block_desc* blk, BlockW* w) {
+    if (!blk || !blk->rms_attn || !blk->attn || !blk->rms_ffn || !blk->ffn) return false;
+    const voxq_attention_desc& at = *blk->attn;
+    const voxq_swiglu_desc& ff = *blk->ffn;
+    w->D = at.d_model;
+    w->H = at.n_heads;
+    w->KVH = at.n_kv_heads;
+    w->hd = at.head_dim;
+    w->F = ff.d_ff;
+    if (w->D != ff.d_model || w->H < 1 || w->KVH < 1 || w->H % w->KVH || w->hd < 4 || w->hd % 4 ||
+        w->hd > kMaxHeadDim)
+        return false;
+    if (!device_qweight(at.wq, &w->wq) || !device_qweight(at.wk, &w->wk) || !device_qweight(at.wv, &w->wv) ||
+        !device_qweight(at.wo, &w->wo) || !device_qweight(ff.w1, &w->w1) || !device_qweight(ff.w2, &w->w2) ||
+        !device_qweight(ff.w3, &w->w3))
+        return false;
+    const int D = w->D, qk = w->H * w->hd, kv = w->KVH * w->hd, F = w->F;
+    if (w->wq.N != qk || w->wq.K != D || w->wk.N != kv || w->wk.K != D || w->wv.N != kv || w->wv.K != D ||
+        w->wo.N != D || w->wo.K != qk || w->w1.N != F || w->w1.K != D || w->w3.N != F || w->w3.K != D ||
+        w->w2.N != D || w->w2.K != F || w->w1.qtype != w->w3.qtype || w->w1.q8_signed != w->w3.q8_signed)
+        return false;
+    w->eps1 = blk->rms_attn->eps;
+    w->eps2 = blk->rms_ffn->eps;
+    return true;
+}
+
+VoxCPMError block_norms(BlockDev& bd, const voxq_block_desc* blk, BlockW* w, cudaStream_t st) {
+    VoxCPMError e = norm_weight(bd, blk->rms_attn->weight, st, &w->wn1);
+    if (!e) e = norm_weight(bd, blk->rms_ffn->weight, st, &w->wn2);
+    return e;
+}
+
+uint64_t block_weight_bytes(const BlockW& w) {
+    uint64_t wb = 0;
+    for (const voxq_qweight* q : {&w.wq, &w.wk, &w.wv, &w.wo, &w.w1, &w.w2, &w.w3})
+        wb += voxq_codes_bytes(q->N, q->K, q->qtype) + voxq_scales_bytes(q->N, q->K, q->qtype);
+    return wb;
+}
+
+inline size_t al64(size_t n) { return (n + 63) & ~(size_t)63; }  // 256-byte aligned parts
+
+// The block's intermediate activations for M rows.
+struct Scratch {
+    float *n, *q, *k, *v, *qr, *ao, *h, *n2, *g;
+};
+size_t scratch_floats(int M, const BlockW& w) {
+    const size_t nx = (size_t)M * w.D, nq = (size_t)M * w.H * w.hd, nk = (size_t)M * w.KVH * w.hd;
+    return 3 * al64(nx) + 3 * al64(nq) + 2 * al64(nk) + al64((size_t)M * w.F);
+}
+Scratch scratch_at(float* p, int M, const BlockW& w) {
+    const size_t nx = (size_t)M * w.D, nq = (size_t)M * w.H * w.hd, nk = (size_t)M * w.KVH * w.hd;
+    Scratch s;
+    s.n = p;
+    s.q = s.n + al64(nx);
+    s.k = s.q + al64(nq);
+    s.v = s.k + al64(nk);
+    s.qr = s.v + al64(nk);
+    s.ao = s.qr + al64(nq);
+    s.h = s.ao + al64(nq);
+    s.n2 = s.h + al64(nx);
+    s.g = s.n2 + al64(nx);
+    return s;
+}
+
+// Enqueues the block on device rows: x [B*seq][D] -> out [B*seq][D] (out may
+// be x).  K/V rows go into the mirror at [pos, pos + seq) and, when kn / vn
+// are given, into them ([B][KVH][seq][hd], for the host write-back).
+VoxCPMError block_core(const BlockW& w, const Scratch& sc, const float* d_x, float* d_o, int B, int seq,
+                       const Mirror* mr, int max_seq, int pos, const float* d_mask, int mrows, int mcols,
+                       const float* d_freqs, float* d_kn, float* d_vn, cudaStream_t st) {
+    const int M = B * seq, D = w.D, H = w.H, KVH = w.KVH, hd = w.hd, F = w.F, qk = H * hd, L = pos + seq;
+    VoxCPMError e = VOXCPM_SUCCESS;
+    // n = RMSNorm(x)
+    rmsnorm_kernel<<<M, kBlockThreads, 0, st>>>(d_x, w.wn1, w.eps1, sc.n, D);
+    VOXQ_CUDA_TRY(cudaGetLastError());
+    // q, k, v
+    if (M <= 8) {
+        voxq_gemv_item it[3] = {};
+        const voxq_qweight* ws[3] = {&w.wq, &w.wk, &w.wv};
+        float* outs[3] = {sc.q, sc.k, sc.v};
+        for (int i = 0; i < 3; i++) {
+            it[i].w = *ws[i];
+            it[i].a = sc.n;
+            it[i].out = outs[i];
+            it[i].M = M;
+            it[i].lda = D;
+            it[i].ldo = ws[i]->N;
+        }
+        e = voxq_gemv_batch(it, 3, st);
+    } else {
+        e = project(sc.n, M, D, w.wq, sc.q, nullptr, nullptr, st);
+        if (!e) e = project(sc.n, M, D, w.wk, sc.k, nullptr, nullptr, st);
+        if (!e) e = project(sc.n, M, D, w.wv, sc.v, nullptr, nullptr, st);
+    }
+    if (e) return e;
+    // RoPE, cache rows [pos, pos + seq)
+    rope_cache_kernel<<<dim3(M, H + 2 * KVH), 64, 0, st>>>(sc.q, sc.k, sc.v, d_freqs, sc.qr, mr->k, mr->v, d_kn, d_vn,
+                                                          seq, H, KVH, hd, max_seq, pos);
+    VOXQ_CUDA_TRY(cudaGetLastError());
+    // attention over [0, L)
+    const int smem = (kMaxHeadDim + L) * (int)sizeof(float);
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (kMaxHeadDim + kMaxCacheLen) * (int)sizeof(float));
+    });
+    attn_kernel<<<dim3(seq, H, B), kAttnThreads, smem, st>>>(sc.qr, mr->k, mr->v, d_mask, mrows, mcols, sc.ao, seq, H,
+                                                            KVH, hd, max_seq, L, 1.0f / sqrtf((float)hd));
+    VOXQ_CUDA_TRY(cudaGetLastError());
+    // h = x + a Wo^T ; n2 = RMSNorm(h) ; g = silu(n2 W1^T) * (n2 W3^T) ; o = h + g W2^T
+    e = project(sc.ao, M, qk, w.wo, sc.h, d_x, nullptr, st);
+    if (e) return e;
+    rmsnorm_kernel<<<M, kBlockThreads, 0, st>>>(sc.h, w.wn2, w.eps2, sc.n2, D);
+    VOXQ_CUDA_TRY(cudaGetLastError());
+    e = project(sc.n2, M, D, w.w1, sc.g, nullptr, &w.w3, st);
+    if (!e) e = project(sc.g, M, F, w.w2, d_o, sc.h, nullptr, st);
+    return e;
+}
+
 }  // namespace
 
 void block_cache_clear() {
@@ -435,6 +640,7 @@ void block_cache_clear() {
         if (bd.scratch.k) cudaFree(bd.scratch.k);
         if (bd.scratch.v) cudaFree(bd.scratch.v);
         if (bd.arena) cudaFree(bd.arena);
+        if (bd.dit_arena) cudaFree(bd.dit_arena);
         if (bd.h_stage) cudaFreeHost(bd.h_stage);
         bd = BlockDev();
     }
@@ -448,20 +654,18 @@ extern "C" VoxCPMError voxq_transformer_block_forward(const voxq_block_desc* blk
                                                       Tensor* cache_v, const Tensor* mask, const Tensor* freqs_cis,
                                                       int pos, Tensor* out) {
     constexpr VoxCPMError kHost = VOXCPM_ERR_CUDA_NOT_FOUND;  // "run the host code instead"
-    if (!blk || !blk->rms_attn || !blk->attn || !blk->rms_ffn || !blk->ffn || !x || !out || !cache_k || !cache_v)
-        return kHost;
+    if (!x || !out || !cache_k || !cache_v) return kHost;
     cudaStream_t st = (cudaStream_t)library_stream();
     if (!st) return kHost;
-    const voxq_attention_desc& at = *blk->attn;
-    const voxq_swiglu_desc& ff = *blk->ffn;
+    BlockW w;
+    if (!block_weights(blk, &w)) return kHost;
     // shapes the kernels take; anything else (including the reference's own
     // shape errors) goes to the host code
     if (!is_host_f32(x) || !is_host_f32(out) || x->ndim != 3 || out->ndim != 3) return kHost;
     const int B = x->shape[0], seq = x->shape[1], D = x->shape[2];
-    if (out->shape[0] != B || out->shape[1] != seq || out->shape[2] != D || B < 1 || seq < 1) return kHost;
-    const int H = at.n_heads, KVH = at.n_kv_heads, hd = at.head_dim, F = ff.d_ff;
-    if (D != at.d_model || D != ff.d_model || H < 1 || KVH < 1 || H % KVH || hd < 4 || hd % 4 || hd > kMaxHeadDim)
+    if (out->shape[0] != B || out->shape[1] != seq || out->shape[2] != D || B < 1 || seq < 1 || D != w.D)
         return kHost;
+    const int KVH = w.KVH, hd = w.hd;
     if (!is_host_f32(cache_k) || !is_host_f32(cache_v) || cache_k->ndim != 4 || cache_v->ndim != 4) return kHost;
     const int max_seq = cache_k->shape[2];
     for (int i = 0; i < 4; i++)
@@ -472,39 +676,26 @@ extern "C" VoxCPMError voxq_transformer_block_forward(const voxq_block_desc* blk
     if (mask && (!is_host_f32(mask) || mask->ndim != 2)) return kHost;
     const int half = hd / 2;
     if (freqs_cis && (!is_host_f32(freqs_cis) || freqs_cis->size < (size_t)L * half * 2)) return kHost;
-    const int qk = H * hd, kv = KVH * hd, M = B * seq;
-    voxq_qweight wq, wk, wv, wo, w1, w2, w3;
-    if (!device_qweight(at.wq, &wq) || !device_qweight(at.wk, &wk) || !device_qweight(at.wv, &wv) ||
-        !device_qweight(at.wo, &wo) || !device_qweight(ff.w1, &w1) || !device_qweight(ff.w2, &w2) ||
-        !device_qweight(ff.w3, &w3))
-        return kHost;
-    if (wq.N != qk || wq.K != D || wk.N != kv || wk.K != D || wv.N != kv || wv.K != D || wo.N != D || wo.K != qk ||
-        w1.N != F || w1.K != D || w3.N != F || w3.K != D || w2.N != D || w2.K != F || w1.qtype != w3.qtype ||
-        w1.q8_signed != w3.q8_signed)
-        return kHost;
+    const int kv = KVH * hd, M = B * seq;
     const int dev = current_device();
     if (dev < 0 || dev >= 16) return kHost;
 
     std::lock_guard<std::mutex> lk(g_blk_mu);
     BlockDev& bd = g_blk[dev];
-    const float *wn1 = nullptr, *wn2 = nullptr;
-    VoxCPMError e = norm_weight(bd, blk->rms_attn->weight, st, &wn1);
-    if (!e) e = norm_weight(bd, blk->rms_ffn->weight, st, &wn2);
+    VoxCPMError e = block_norms(bd, blk, &w, st);
     if (e) return e;
 
-    // device arena: x n q k v qr ao h n2 g o knew vnew freqs mask
+    // device arena: x | block scratch | out | new K rows | new V rows | freqs rows | mask rows
     const int mcols = mask ? (mask->shape[1] < L ? mask->shape[1] : L) : 0;
     const int mrows = mask ? (mask->shape[0] < seq ? mask->shape[0] : seq) : 0;
-    const size_t nx = (size_t)M * D, nq = (size_t)M * qk, nk = (size_t)M * kv, ng = (size_t)M * F;
+    const size_t nx = (size_t)M * D, nk = (size_t)M * kv;
     const size_t nf = freqs_cis ? (size_t)seq * half * 2 : 0, nm = (size_t)mrows * mcols;
-    auto al = [](size_t n) { return (n + 63) & ~(size_t)63; };  // 256-byte aligned parts
-    const size_t off_n = al(nx), off_q = off_n + al(nx), off_k = off_q + al(nq), off_v = off_k + al(nk),
-                 off_qr = off_v + al(nk), off_ao = off_qr + al(nq), off_h = off_ao + al(nq), off_n2 = off_h + al(nx),
-                 off_g = off_n2 + al(nx), off_o = off_g + al(ng), off_kn = off_o + al(nx), off_vn = off_kn + al(nk),
-                 off_f = off_vn + al(nk), off_m = off_f + al(nf), total = off_m + al(nm);
+    const size_t off_s = al64(nx), off_o = off_s + scratch_floats(M, w), off_kn = off_o + al64(nx),
+                 off_vn = off_kn + al64(nk), off_f = off_vn + al64(nk), off_m = off_f + al64(nf),
+                 total = off_m + al64(nm);
     if (!grow(&bd.arena, &bd.arena_floats, total, false, st)) return VOXCPM_ERR_OOM;
     // pinned staging: uploads x | freqs rows | mask rows, downloads out | knew | vnew
-    const size_t up_n = al(nx) + al(nf) + al(nm), down_n = al(nx) + 2 * al(nk);
+    const size_t up_n = al64(nx) + al64(nf) + al64(nm), down_n = al64(nx) + 2 * al64(nk);
     if (!grow(&bd.h_stage, &bd.h_stage_floats, up_n + down_n, true, st)) return VOXCPM_ERR_OOM;
 
     Mirror* mr = nullptr;
@@ -512,75 +703,30 @@ extern "C" VoxCPMError voxq_transformer_block_forward(const voxq_block_desc* blk
     if (e) return e;
 
     float* A = bd.arena;
-    float *d_x = A, *d_n = A + off_n, *d_q = A + off_q, *d_k = A + off_k, *d_v = A + off_v, *d_qr = A + off_qr,
-          *d_ao = A + off_ao, *d_h = A + off_h, *d_n2 = A + off_n2, *d_g = A + off_g, *d_o = A + off_o,
-          *d_kn = A + off_kn, *d_vn = A + off_vn, *d_f = A + off_f, *d_m = A + off_m;
+    float *d_x = A, *d_o = A + off_o, *d_kn = A + off_kn, *d_vn = A + off_vn, *d_f = A + off_f, *d_m = A + off_m;
+    const Scratch sc = scratch_at(A + off_s, M, w);
     float* hs = bd.h_stage;
     memcpy(hs, x->data, nx * sizeof(float));
-    if (nf) memcpy(hs + al(nx), freqs_cis->data + (size_t)pos * half * 2, nf * sizeof(float));
+    if (nf) memcpy(hs + al64(nx), freqs_cis->data + (size_t)pos * half * 2, nf * sizeof(float));
     for (int r = 0; r < mrows; r++)
-        memcpy(hs + al(nx) + al(nf) + (size_t)r * mcols, mask->data + (size_t)r * mask->shape[1],
+        memcpy(hs + al64(nx) + al64(nf) + (size_t)r * mcols, mask->data + (size_t)r * mask->shape[1],
                (size_t)mcols * sizeof(float));
     float* hd_out = hs + up_n;
     // everything from the upload to the downloads, on `st`
     auto enqueue = [&]() -> VoxCPMError {
-        VoxCPMError e = VOXCPM_SUCCESS;
-        // one upload: x, then the freqs and mask parts sit at the arena's f / m offsets
         VOXQ_CUDA_TRY(cudaMemcpyAsync(d_x, hs, nx * sizeof(float), cudaMemcpyHostToDevice, st));
-        if (nf) VOXQ_CUDA_TRY(cudaMemcpyAsync(d_f, hs + al(nx), nf * sizeof(float), cudaMemcpyHostToDevice, st));
+        if (nf) VOXQ_CUDA_TRY(cudaMemcpyAsync(d_f, hs + al64(nx), nf * sizeof(float), cudaMemcpyHostToDevice, st));
         if (nm)
-            VOXQ_CUDA_TRY(cudaMemcpyAsync(d_m, hs + al(nx) + al(nf), nm * sizeof(float), cudaMemcpyHostToDevice, st));
-
-        // n = RMSNorm(x)
-        rmsnorm_kernel<<<M, kBlockThreads, 0, st>>>(d_x, wn1, blk->rms_attn->eps, d_n, D);
-        VOXQ_CUDA_TRY(cudaGetLastError());
-        // q, k, v
-        if (M <= 8) {
-            voxq_gemv_item it[3] = {};
-            const voxq_qweight* ws[3] = {&wq, &wk, &wv};
-            float* outs[3] = {d_q, d_k, d_v};
-            for (int i = 0; i < 3; i++) {
-                it[i].w = *ws[i];
-                it[i].a = d_n;
-                it[i].out = outs[i];
-                it[i].M = M;
-                it[i].lda = D;
-                it[i].ldo = ws[i]->N;
-            }
-            e = voxq_gemv_batch(it, 3, st);
-        } else {
-            e = project(d_n, M, D, wq, d_q, nullptr, nullptr, st);
-            if (!e) e = project(d_n, M, D, wk, d_k, nullptr, nullptr, st);
-            if (!e) e = project(d_n, M, D, wv, d_v, nullptr, nullptr, st);
-        }
-        if (e) return e;
-        // RoPE, cache rows [pos, pos + seq)
-        rope_cache_kernel<<<dim3(M, H + 2 * KVH), 64, 0, st>>>(d_q, d_k, d_v, nf ? d_f : nullptr, d_qr, mr->k, mr->v,
-                                                              d_kn, d_vn, seq, H, KVH, hd, max_seq, pos);
-        VOXQ_CUDA_TRY(cudaGetLastError());
-        // attention over [0, L)
-        const int smem = (kMaxHeadDim + L) * (int)sizeof(float);
-        static std::once_flag once;
-        std::call_once(once, [] {
-            cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (kMaxHeadDim + kMaxCacheLen) * (int)sizeof(float));
-        });
-        attn_kernel<<<dim3(seq, H, B), kAttnThreads, smem, st>>>(d_qr, mr->k, mr->v, nm ? d_m : nullptr, mrows, mcols,
-                                                                d_ao, seq, H, KVH, hd, max_seq, L,
-                                                                1.0f / sqrtf((float)hd));
-        VOXQ_CUDA_TRY(cudaGetLastError());
-        // h = x + a Wo^T ; n2 = RMSNorm(h) ; g = silu(n2 W1^T) * (n2 W3^T) ; o = h + g W2^T
-        e = project(d_ao, M, qk, wo, d_h, d_x, nullptr, st);
-        if (e) return e;
-        rmsnorm_kernel<<<M, kBlockThreads, 0, st>>>(d_h, wn2, blk->rms_ffn->eps, d_n2, D);
-        VOXQ_CUDA_TRY(cudaGetLastError());
-        e = project(d_n2, M, D, w1, d_g, nullptr, &w3, st);
-        if (!e) e = project(d_g, M, F, w2, d_o, d_h, nullptr, st);
-        if (e) return e;
+            VOXQ_CUDA_TRY(cudaMemcpyAsync(d_m, hs + al64(nx) + al64(nf), nm * sizeof(float), cudaMemcpyHostToDevice,
+                                          st));
+        const VoxCPMError ce = block_core(w, sc, d_x, d_o, B, seq, mr, max_seq, pos, nm ? d_m : nullptr, mrows,
+                                          mcols, nf ? d_f : nullptr, d_kn, d_vn, st);
+        if (ce) return ce;
         // downloads: out, new cache rows (the caller waits once)
         VOXQ_CUDA_TRY(cudaMemcpyAsync(hd_out, d_o, nx * sizeof(float), cudaMemcpyDeviceToHost, st));
-        VOXQ_CUDA_TRY(cudaMemcpyAsync(hd_out + al(nx), d_kn, nk * sizeof(float), cudaMemcpyDeviceToHost, st));
-        VOXQ_CUDA_TRY(cudaMemcpyAsync(hd_out + al(nx) + al(nk), d_vn, nk * sizeof(float), cudaMemcpyDeviceToHost, st));
+        VOXQ_CUDA_TRY(cudaMemcpyAsync(hd_out + al64(nx), d_kn, nk * sizeof(float), cudaMemcpyDeviceToHost, st));
+        VOXQ_CUDA_TRY(cudaMemcpyAsync(hd_out + al64(nx) + al64(nk), d_vn, nk * sizeof(float), cudaMemcpyDeviceToHost,
+                                      st));
         return VOXCPM_SUCCESS;
     };
     // A fill call (the whole cache written at pos 0) repeats with identical
@@ -590,15 +736,15 @@ extern "C" VoxCPMError voxq_transformer_block_forward(const voxq_block_desc* blk
         std::vector<uint64_t> key = {(uint64_t)(uintptr_t)blk, (uint64_t)B, (uint64_t)seq, (uint64_t)D,
                                      (uint64_t)(uintptr_t)mr->k, (uint64_t)(uintptr_t)mr->v,
                                      (uint64_t)(uintptr_t)bd.arena, (uint64_t)(uintptr_t)bd.h_stage,
-                                     (uint64_t)(uintptr_t)wn1, (uint64_t)(uintptr_t)wn2,
+                                     (uint64_t)(uintptr_t)w.wn1, (uint64_t)(uintptr_t)w.wn2,
                                      (uint64_t)mrows, (uint64_t)mcols, (uint64_t)nf};
         uint32_t eb[2];
-        memcpy(&eb[0], &blk->rms_attn->eps, 4);
-        memcpy(&eb[1], &blk->rms_ffn->eps, 4);
+        memcpy(&eb[0], &w.eps1, 4);
+        memcpy(&eb[1], &w.eps2, 4);
         key.push_back(((uint64_t)eb[0] << 32) | eb[1]);
-        for (const voxq_qweight* w : {&wq, &wk, &wv, &wo, &w1, &w2, &w3}) {
-            key.push_back((uint64_t)(uintptr_t)w->codes);
-            key.push_back((uint64_t)(uintptr_t)w->scales);
+        for (const voxq_qweight* q : {&w.wq, &w.wk, &w.wv, &w.wo, &w.w1, &w.w2, &w.w3}) {
+            key.push_back((uint64_t)(uintptr_t)q->codes);
+            key.push_back((uint64_t)(uintptr_t)q->scales);
         }
         auto g = bd.graphs.find(key);
         if (g != bd.graphs.end()) {
@@ -631,19 +777,196 @@ extern "C" VoxCPMError voxq_transformer_block_forward(const voxq_block_desc* blk
     VOXQ_CUDA_TRY(cudaStreamSynchronize(st));
     memcpy(out->data, hd_out, nx * sizeof(float));
     for (int kvs = 0; kvs < 2; kvs++) {
-        const float* src = hd_out + al(nx) + kvs * al(nk);
+        const float* src = hd_out + al64(nx) + kvs * al64(nk);
         float* dst = kvs ? cache_v->data : cache_k->data;
         for (int bk = 0; bk < B * KVH; bk++)
             memcpy(dst + ((size_t)bk * max_seq + pos) * hd, src + (size_t)bk * seq * hd, (size_t)seq * hd * sizeof(float));
     }
-    {
-        uint64_t wb = 0;
-        for (const voxq_qweight* w : {&wq, &wk, &wv, &wo, &w1, &w2, &w3})
-            wb += voxq_codes_bytes(w->N, w->K, w->qtype) + voxq_scales_bytes(w->N, w->K, w->qtype);
-        count_matmul_traffic(7, wb);
-    }
+    count_matmul_traffic(7, block_weight_bytes(w));
     mr->valid = L;
     mr->last_row.assign(cache_k->data + (size_t)(L - 1) * hd, cache_k->data + (size_t)L * hd);
+    return VOXCPM_SUCCESS;
+}
+
+namespace voxq {
+namespace {
+
+// Sinusoidal embedding of the reference (src/loc_dit.c:35-50): row[2i] =
+// sin(t f_i), row[2i + 1] = cos(t f_i), f_i = 1 / 10000^(2i / D), on the host
+// with the same libm calls.
+void sinusoidal(float t, int D, float* row) {
+    const int half = D / 2;
+    for (int i = 0; i < half; i++) {
+        const float inv_freq = 1.0f / powf(10000.0f, 2.0f * (float)i / (float)D);
+        const float val = t * inv_freq;
+        row[2 * i] = sinf(val);
+        row[2 * i + 1] = cosf(val);
+    }
+}
+
+int ew(int n) { return (n + 255) / 256 > 0 ? (n + 255) / 256 : 1; }
+
+}  // namespace
+}  // namespace voxq
+
+extern "C" VoxCPMError voxq_locdit_sample(const voxq_locdit_desc* dit, const Tensor* mu, const Tensor* cond,
+                                          int n_timesteps, float cfg_value, const Tensor* x_init, Tensor* out) {
+    constexpr VoxCPMError kHost = VOXCPM_ERR_CUDA_NOT_FOUND;
+    if (!dit || !mu || !cond || !x_init || !out || n_timesteps < 1 || !dit->layers || dit->n_layers < 1 ||
+        !dit->output_norm)
+        return kHost;
+    cudaStream_t st = (cudaStream_t)library_stream();
+    if (!st) return kHost;
+    const int D = dit->d_model, F = dit->feat_dim;
+    if (!is_host_f32(mu) || mu->ndim != 2 || mu->shape[0] != 1 || mu->shape[1] != D) return kHost;
+    if (!is_host_f32(out) || out->ndim != 3 || out->shape[0] != 1 || out->shape[1] != F) return kHost;
+    const int P = out->shape[2];
+    if (!is_host_f32(x_init) || x_init->ndim != 3 || x_init->shape[0] != 1 || x_init->shape[1] != F ||
+        x_init->shape[2] != P || P < 1)
+        return kHost;
+    if (cond->ndim != 3 || cond->shape[0] != 1 || cond->shape[1] != F || cond->is_cuda || cond->is_fp16) return kHost;
+    const int Tc = cond->shape[2];
+    if (Tc > 0 && !cond->data) return kHost;
+    if (cfg_value < 0.0f) cfg_value = 0.0f;
+    const int nb = (cfg_value > 1.0f && Tc > 0) ? 2 : 1;
+    const int S = 1 + P + Tc, M = nb * S;
+    // weights
+    voxq_qweight win, wc, wout, wt1, wt2, wd1, wd2;
+    if (!device_qweight(dit->in_proj_weight, &win) || !device_qweight(dit->out_proj_weight, &wout) ||
+        !device_qweight(dit->time_mlp_1_weight, &wt1) || !device_qweight(dit->time_mlp_2_weight, &wt2) ||
+        !device_qweight(dit->delta_mlp_1_weight, &wd1) || !device_qweight(dit->delta_mlp_2_weight, &wd2))
+        return kHost;
+    if (Tc > 0 && !device_qweight(dit->cond_proj_weight, &wc)) return kHost;
+    if (win.N != D || win.K != F || wout.N != F || wout.K != D || wt1.N != D || wt1.K != D || wt2.N != D ||
+        wt2.K != D || wd1.N != D || wd1.K != D || wd2.N != D || wd2.K != D || (Tc > 0 && (wc.N != D || wc.K != F)))
+        return kHost;
+    std::vector<BlockW> bw(dit->n_layers);
+    for (int l = 0; l < dit->n_layers; l++) {
+        if (!block_weights(&dit->layers[l], &bw[l]) || bw[l].D != D) return kHost;
+        if (S > kMaxCacheLen) return kHost;
+    }
+    const int dev = current_device();
+    if (dev < 0 || dev >= 16) return kHost;
+
+    std::lock_guard<std::mutex> lk(g_blk_mu);
+    BlockDev& bd = g_blk[dev];
+    VoxCPMError e = VOXCPM_SUCCESS;
+    for (int l = 0; l < dit->n_layers; l++) {
+        e = block_norms(bd, &dit->layers[l], &bw[l], st);
+        if (e) return e;
+    }
+    // biases and the output norm weight: cached device copies of host tensors
+    const float *b_in = nullptr, *b_c = nullptr, *b_out = nullptr, *b_t1 = nullptr, *b_t2 = nullptr,
+                *b_d1 = nullptr, *b_d2 = nullptr, *w_on = nullptr;
+    const Tensor* bt[8] = {dit->in_proj_bias,  dit->cond_proj_bias,  dit->out_proj_bias,  dit->time_mlp_1_bias,
+                           dit->time_mlp_2_bias, dit->delta_mlp_1_bias, dit->delta_mlp_2_bias, dit->output_norm->weight};
+    const float** bp[8] = {&b_in, &b_c, &b_out, &b_t1, &b_t2, &b_d1, &b_d2, &w_on};
+    for (int i = 0; i < 8; i++) {
+        e = norm_weight(bd, bt[i], st, bp[i]);
+        if (e) return e;
+    }
+    // arena: seq | block scratch | K | V | small buffers
+    int maxKVH = 0, maxhd = 0;
+    size_t scr = 0;
+    for (auto& w : bw) {
+        maxKVH = std::max(maxKVH, w.KVH);
+        maxhd = std::max(maxhd, w.hd);
+        scr = std::max(scr, scratch_floats(M, w));
+    }
+    const size_t nseq = (size_t)M * D, nkv = (size_t)nb * maxKVH * S * maxhd;
+    const size_t o_scr = al64(nseq), o_k = o_scr + scr, o_v = o_k + al64(nkv), o_x = o_v + al64(nkv),
+                 o_xp = o_x + al64((size_t)F * P), o_xpr = o_xp + al64((size_t)P * F),
+                 o_cp = o_xpr + al64((size_t)P * D), o_ct = o_cp + al64((size_t)Tc * F),
+                 o_cr = o_ct + al64((size_t)Tc * D), o_mu = o_cr + al64((size_t)Tc * D), o_emb = o_mu + al64((size_t)D),
+                 o_hid = o_emb + al64((size_t)D), o_tf = o_hid + al64((size_t)D), o_df = o_tf + al64((size_t)D),
+                 o_gc = o_df + al64((size_t)D), o_xs = o_gc + al64((size_t)D), o_vr = o_xs + al64((size_t)nb * P * D),
+                 total = o_vr + al64((size_t)nb * P * F);
+    if (!grow(&bd.dit_arena, &bd.dit_arena_floats, total, false, st)) return VOXCPM_ERR_OOM;
+    const size_t hs_n = (size_t)n_timesteps * 2 * D + (size_t)F * P + (size_t)F * Tc + (size_t)F * P + (size_t)D;
+    if (!grow(&bd.h_stage, &bd.h_stage_floats, hs_n, true, st)) return VOXCPM_ERR_OOM;
+    float* A = bd.dit_arena;
+    float *d_seq = A, *d_k = A + o_k, *d_v = A + o_v, *d_x = A + o_x, *d_xperm = A + o_xp, *d_xproj = A + o_xpr,
+          *d_cperm = A + o_cp, *d_cond = A + o_ct, *d_crows = A + o_cr, *d_emb = A + o_emb, *d_hid = A + o_hid,
+          *d_tf = A + o_tf, *d_df = A + o_df, *d_gc = A + o_gc, *d_xs = A + o_xs, *d_vr = A + o_vr,
+          *d_mu = A + o_mu;
+    // host side: every step's two embeddings, x_init, cond
+    float* hs = bd.h_stage;
+    const float sigma_min = 1e-6f;
+    const float dt = (1.0f - sigma_min) / (float)n_timesteps;
+    for (int i = 0; i < n_timesteps; i++) {
+        const float t_cur = 1.0f - (float)i * dt;
+        sinusoidal(t_cur, D, hs + (size_t)i * 2 * D);
+        sinusoidal(dt, D, hs + (size_t)i * 2 * D + D);
+    }
+    float* h_x = hs + (size_t)n_timesteps * 2 * D;
+    memcpy(h_x, x_init->data, (size_t)F * P * sizeof(float));
+    float* h_c = h_x + (size_t)F * P;
+    if (Tc > 0) memcpy(h_c, cond->data, (size_t)F * Tc * sizeof(float));
+    float* h_out = h_c + (size_t)F * Tc;
+    float* h_mu = h_out + (size_t)F * P;
+    memcpy(h_mu, mu->data, (size_t)D * sizeof(float));
+    // upload: x_init -> d_x, mu -> d_mu, cond -> d_cond (as [F][Tc] then transposed to [Tc][F])
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(d_x, h_x, (size_t)F * P * sizeof(float), cudaMemcpyHostToDevice, st));
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(d_mu, h_mu, (size_t)D * sizeof(float), cudaMemcpyHostToDevice, st));
+    if (Tc > 0) {
+        VOXQ_CUDA_TRY(cudaMemcpyAsync(d_cperm, h_c, (size_t)F * Tc * sizeof(float), cudaMemcpyHostToDevice, st));
+        transpose_kernel<<<ew(F * Tc), 256, 0, st>>>(d_cperm, d_cond, F, Tc);
+        // condition rows [Tc][D] = cond^T Wc^T + bc (constant over the steps)
+        voxq_epilogue epi = {b_c, nullptr, 0, nullptr};
+        e = voxq_matmul_nt_q(d_cond, Tc, F, &wc, d_crows, D, &epi, st);
+        if (e) return e;
+    }
+    // the scratch K/V of every block: a fresh cache filled whole (pos 0, length S)
+    Mirror kvm;
+    kvm.k = d_k;
+    kvm.v = d_v;
+    uint64_t traffic = 0;
+    for (int i = 0; i < n_timesteps; i++) {
+        // time / delta features: Linear-SiLU-Linear of the step's embeddings
+        VOXQ_CUDA_TRY(cudaMemcpyAsync(d_emb, hs + (size_t)i * 2 * D, (size_t)D * sizeof(float),
+                                      cudaMemcpyHostToDevice, st));
+        voxq_epilogue e1 = {b_t1, nullptr, 0, nullptr}, e2 = {b_t2, nullptr, 0, nullptr};
+        e = voxq_matmul_nt_q(d_emb, 1, D, &wt1, d_hid, D, &e1, st);
+        if (e) return e;
+        silu_inplace_kernel<<<ew(D), 256, 0, st>>>(d_hid, D);
+        e = voxq_matmul_nt_q(d_hid, 1, D, &wt2, d_tf, D, &e2, st);
+        if (e) return e;
+        VOXQ_CUDA_TRY(cudaMemcpyAsync(d_emb, hs + (size_t)i * 2 * D + D, (size_t)D * sizeof(float),
+                                      cudaMemcpyHostToDevice, st));
+        voxq_epilogue e3 = {b_d1, nullptr, 0, nullptr}, e4 = {b_d2, nullptr, 0, nullptr};
+        e = voxq_matmul_nt_q(d_emb, 1, D, &wd1, d_hid, D, &e3, st);
+        if (e) return e;
+        silu_inplace_kernel<<<ew(D), 256, 0, st>>>(d_hid, D);
+        e = voxq_matmul_nt_q(d_hid, 1, D, &wd2, d_df, D, &e4, st);
+        if (e) return e;
+        add_vec_kernel<<<ew(D), 256, 0, st>>>(d_tf, d_df, d_gc, D);
+        // input projection of x_t: [F][P] -> [P][F] -> [P][D] + b_in
+        transpose_kernel<<<ew(F * P), 256, 0, st>>>(d_x, d_xperm, F, P);
+        voxq_epilogue ei = {b_in, nullptr, 0, nullptr};
+        e = voxq_matmul_nt_q(d_xperm, P, F, &win, d_xproj, D, &ei, st);
+        if (e) return e;
+        // the branches' sequences, the blocks, the x rows, the output norm and projection
+        dit_seq_kernel<<<ew((int)std::min<size_t>(nseq, 1 << 20)), 256, 0, st>>>(d_seq, d_mu, d_xproj, d_crows,
+                                                                                   b_c, d_gc, nb, P, Tc, D);
+        VOXQ_CUDA_TRY(cudaGetLastError());
+        for (int l = 0; l < dit->n_layers; l++) {
+            const Scratch sc = scratch_at(A + o_scr, M, bw[l]);
+            e = block_core(bw[l], sc, d_seq, d_seq, nb, S, &kvm, S, 0, nullptr, 0, 0, nullptr, nullptr, nullptr, st);
+            if (e) return e;
+            traffic += block_weight_bytes(bw[l]);
+        }
+        dit_slice_kernel<<<ew(nb * P * D), 256, 0, st>>>(d_seq, d_xs, nb, P, S, D);
+        rmsnorm_kernel<<<nb * P, kBlockThreads, 0, st>>>(d_xs, w_on, dit->output_norm->eps, d_xs, D);
+        voxq_epilogue eo = {b_out, nullptr, 0, nullptr};
+        e = voxq_matmul_nt_q(d_xs, nb * P, D, &wout, d_vr, F, &eo, st);
+        if (e) return e;
+        dit_step_kernel<<<ew(F * P), 256, 0, st>>>(d_x, d_vr, nb, P, F, cfg_value, dt);
+        VOXQ_CUDA_TRY(cudaGetLastError());
+    }
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(h_out, d_x, (size_t)F * P * sizeof(float), cudaMemcpyDeviceToHost, st));
+    VOXQ_CUDA_TRY(cudaStreamSynchronize(st));
+    memcpy(out->data, h_out, (size_t)F * P * sizeof(float));
+    count_matmul_traffic((uint64_t)n_timesteps * (7 * dit->n_layers + 6) + (Tc > 0 ? 1 : 0), traffic);
     return VOXCPM_SUCCESS;
 }
 

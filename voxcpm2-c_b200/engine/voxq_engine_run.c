@@ -176,10 +176,34 @@ VoxCPMError __wrap_tensor_matmul_nt(const Tensor* a, const Tensor* b, Tensor* ou
 
 VoxCPMError __real_loc_dit_sample(const LocDiT* dit, const Tensor* mu, const Tensor* cond, int n_timesteps,
                                   float cfg_value, Tensor* out);
+/* loc_dit_sample: in the libvoxq build the whole sampler runs on the device
+ * (voxq_locdit_sample: the sequence resident, the CFG branches batched) with
+ * the starting noise drawn here exactly as loc_dit_sample draws it
+ * (src/loc_dit.c:471-474: tensor_rand_normal, seed 42); VOXQ_ENGINE_DIT=cpu
+ * keeps the engine's own sampler (its blocks still go to the device). */
+static int g_dit_gpu = 1;
+static VoxCPMError dit_sample(const LocDiT* dit, const Tensor* mu, const Tensor* cond, int n_timesteps,
+                              float cfg_value, Tensor* out) {
+#ifdef VOXQ_ENGINE_LIBVOXQ
+    if (g_dit_gpu && dit && mu && out && out->ndim == 3) {
+        Tensor* x0 = tensor_create(3, (int[]){out->shape[0], out->shape[1], out->shape[2]});
+        if (x0) {
+            uint64_t seed = 42;
+            tensor_rand_normal(x0, &seed);
+            const VoxCPMError r = voxq_locdit_sample((const voxq_locdit_desc*)dit, mu, cond, n_timesteps, cfg_value,
+                                                     x0, out);
+            tensor_free(x0);
+            if (r != VOXCPM_ERR_CUDA_NOT_FOUND) return r;
+        }
+    }
+#endif
+    return __real_loc_dit_sample(dit, mu, cond, n_timesteps, cfg_value, out);
+}
+
 VoxCPMError __wrap_loc_dit_sample(const LocDiT* dit, const Tensor* mu, const Tensor* cond, int n_timesteps,
                                   float cfg_value, Tensor* out) {
     VoxCPMError r;
-    TIMED(ST_DIT, __real_loc_dit_sample(dit, mu, cond, n_timesteps, cfg_value, out));
+    TIMED(ST_DIT, dit_sample(dit, mu, cond, n_timesteps, cfg_value, out));
     if (r == VOXCPM_SUCCESS && out && out->data && !out->is_cuda) {
         const int n = (int)out->size;
         if (g_latent_n + n > g_latent_cap) {
@@ -492,6 +516,7 @@ int main(int argc, char** argv) {
         if (v && !strcmp(v, "convs")) g_vae_whole = 0;
     }
     if (getenv("VOXQ_ENGINE_BLOCK") && !strcmp(getenv("VOXQ_ENGINE_BLOCK"), "cpu")) g_block_gpu = 0;
+    if (getenv("VOXQ_ENGINE_DIT") && !strcmp(getenv("VOXQ_ENGINE_DIT"), "cpu")) g_dit_gpu = 0;
 #endif
     g_dump_dir = getenv("VOXQ_ENGINE_DUMP_DIR");
 

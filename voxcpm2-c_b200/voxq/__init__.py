@@ -167,6 +167,7 @@ SIGNATURES = {
     "voxq_vae_decode": ([C.POINTER(VaeOp), _i, C.c_float, _TP, _TP], _i),
     "voxq_transformer_block_forward": ([C.POINTER(BlockDesc), _TP, _TP, _TP, _TP, _TP, _i, _TP], _i),
     "voxq_block_cache_clear": ([], None),
+    "voxq_locdit_sample": ([_vp, _TP, _TP, _i, C.c_float, _TP, _TP], _i),
     "voxq_vxcpm2_open": ([C.c_char_p, C.POINTER(_vp)], _i),
     "voxq_vxcpm2_close": ([_vp], None),
     "voxq_vxcpm2_info": ([_vp, C.POINTER(Vxcpm2Header), C.POINTER(_i)], _i),
