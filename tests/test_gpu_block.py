@@ -135,7 +135,7 @@ def test_block_on_device_matches_reference(qname):
         at = voxq.AttentionDesc(T["wq"], T["wk"], T["wv"], T["wo"], D, H, KVH, hd)
         ff = voxq.SwigluDesc(T["w1"], T["w2"], T["w3"], D, F)
         bd = voxq.BlockDesc(C.pointer(n1), C.pointer(at), C.pointer(n2), C.pointer(ff))
-        positions = 64
+        positions = 96
         inv = 10000.0 ** (-np.arange(hd // 2) * 2.0 / hd)
         ang = np.arange(positions)[:, None] * inv[None, :]
         freqs_np = np.stack([np.cos(ang), np.sin(ang)], -1).astype(np.float32)
@@ -192,6 +192,13 @@ def test_block_on_device_matches_reference(qname):
         rk[:] = 0.0
         rv[:] = 0.0
         run(3, 0, ck, cv, rk, rv, True, True, "restart S=3")
+        # enough query rows (seq x heads per kv head >= 64) for the tiled attention kernel: a fill, and a
+        # causal prefill with RoPE followed by a two-row continuation over more than one key tile
+        ck2, cv2, rk2, rv2 = cache(40)
+        run(40, 0, ck2, cv2, rk2, rv2, False, False, "fill S=40 (tiled attention)")
+        ck3, cv3, rk3, rv3 = cache(96)
+        run(36, 0, ck3, cv3, rk3, rv3, True, True, "prefill S=36 (tiled attention)")
+        run(32, 36, ck3, cv3, rk3, rv3, True, True, "continuation S=32 over 68 > 2 key tiles")
         assert voxq.lib().voxq_device_error(1) == 0
     finally:
         for t in keep:

@@ -192,6 +192,93 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const float* __restr
     }
 }
 
+// Attention for many query rows (prefill, the LocDiT's sequences): the same
+// function as attn_kernel, tiled so a key / value tile in shared memory serves
+// 64 query vectors -- the query rows of a CTA times the G = H / KVH query heads
+// that read one kv head -- instead of every CTA re-reading the whole cache.
+// Four threads per query vector, each holding head_dim / 4 interleaved
+// dimensions (d = part + 4 j, conflict-free shared reads); an online softmax
+// (running max m and sum l, accumulator rescaled by exp(m_old - m_new)) over
+// key tiles of kFK; out = acc / (l + 1e-10).  grid = (ceil(seq / (64 / G)),
+// KVH, B).
+constexpr int kFK = 32;
+constexpr int kFThreads = 256;
+template <int HD>
+__global__ void __launch_bounds__(kFThreads) attn_tiled_kernel(const float* __restrict__ q, const float* __restrict__ ck,
+                                                               const float* __restrict__ cv,
+                                                               const float* __restrict__ mask, int mrows, int mcols,
+                                                               float* __restrict__ out, int seq, int H, int KVH,
+                                                               int max_seq, int L, float inv_scale) {
+    constexpr int DPT = HD / 4;
+    __shared__ __align__(16) float Ks[kFK][HD];
+    __shared__ __align__(16) float Vs[kFK][HD];
+    const int G = H / KVH, QR = 64 / G;
+    const int kh = blockIdx.y, b = blockIdx.z;
+    const int r = threadIdx.x >> 2, part = threadIdx.x & 3;
+    const int h = kh * G + r % G, s = blockIdx.x * QR + r / G;
+    const bool valid = s < seq;
+    float qv[DPT], acc[DPT];
+    const float* qr = q + (((int64_t)b * H + h) * seq + (valid ? s : 0)) * HD;
+#pragma unroll
+    for (int j = 0; j < DPT; j++) {
+        qv[j] = valid ? qr[part + 4 * j] : 0.0f;
+        acc[j] = 0.0f;
+    }
+    float m = -INFINITY, l = 0.0f;
+    const float* kb = ck + ((int64_t)b * KVH + kh) * max_seq * HD;
+    const float* vb = cv + ((int64_t)b * KVH + kh) * max_seq * HD;
+    for (int t0 = 0; t0 < L; t0 += kFK) {
+        __syncthreads();  // the previous tile is consumed
+        const int nt = min(kFK, L - t0);
+        for (int i = threadIdx.x; i < kFK * HD / 4; i += kFThreads) {
+            const int row = (i * 4) / HD, col = (i * 4) % HD;
+            float4 kk = make_float4(0.f, 0.f, 0.f, 0.f), vv = kk;
+            if (row < nt) {
+                kk = *reinterpret_cast<const float4*>(kb + (int64_t)(t0 + row) * HD + col);
+                vv = *reinterpret_cast<const float4*>(vb + (int64_t)(t0 + row) * HD + col);
+            }
+            *reinterpret_cast<float4*>(&Ks[row][col]) = kk;
+            *reinterpret_cast<float4*>(&Vs[row][col]) = vv;
+        }
+        __syncthreads();
+        float sc[kFK];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < kFK; k++) {
+            float pd = 0.0f;
+#pragma unroll
+            for (int j = 0; j < DPT; j++) pd = fmaf(qv[j], Ks[k][part + 4 * j], pd);
+            pd += __shfl_xor_sync(0xffffffffu, pd, 1);
+            pd += __shfl_xor_sync(0xffffffffu, pd, 2);
+            float v = pd * inv_scale;
+            const int t = t0 + k;
+            if (mask && s < mrows && t < mcols) v += mask[(int64_t)s * mcols + t];
+            if (k >= nt) v = -INFINITY;
+            sc[k] = v;
+            mx = fmaxf(mx, v);
+        }
+        const float mn = fmaxf(m, mx);
+        if (mn == -INFINITY) continue;  // every key so far masked
+        const float f = expf(m - mn);   // 0 on the first visible tile (m = -inf)
+        l *= f;
+#pragma unroll
+        for (int j = 0; j < DPT; j++) acc[j] *= f;
+#pragma unroll
+        for (int k = 0; k < kFK; k++) {
+            const float p = expf(sc[k] - mn);
+            l += p;
+#pragma unroll
+            for (int j = 0; j < DPT; j++) acc[j] = fmaf(p, Vs[k][part + 4 * j], acc[j]);
+        }
+        m = mn;
+    }
+    if (!valid) return;
+    const float inv = 1.0f / (l + 1e-10f);
+    float* orow = out + (((int64_t)b * seq + s) * H + h) * HD;
+#pragma unroll
+    for (int j = 0; j < DPT; j++) orow[part + 4 * j] = acc[j] * inv;
+}
+
 // Gathers cache rows [r0, r1) of every (b, kv head) from a contiguous host
 // staging block [B][KVH][r1 - r0][hd] into the device cache.
 __global__ void cache_fill_kernel(const float* __restrict__ src, float* __restrict__ dst, int BK, int rows, int hd,
@@ -612,8 +699,21 @@ VoxCPMError block_core(const BlockW& w, const Scratch& sc, const float* d_x, flo
         cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (kMaxHeadDim + kMaxCacheLen) * (int)sizeof(float));
     });
-    attn_kernel<<<dim3(seq, H, B), kAttnThreads, smem, st>>>(sc.qr, mr->k, mr->v, d_mask, mrows, mcols, sc.ao, seq, H,
-                                                            KVH, hd, max_seq, L, 1.0f / sqrtf((float)hd));
+    const int G = H / KVH;
+    const float inv_scale = 1.0f / sqrtf((float)hd);
+    if (seq * G >= 64 && 64 % G == 0 && (hd == 64 || hd == 128)) {
+        // many query rows: tiled, key / value tiles shared by 64 query vectors
+        const dim3 grid((unsigned)((seq + 64 / G - 1) / (64 / G)), (unsigned)KVH, (unsigned)B);
+        if (hd == 128)
+            attn_tiled_kernel<128><<<grid, kFThreads, 0, st>>>(sc.qr, mr->k, mr->v, d_mask, mrows, mcols, sc.ao, seq,
+                                                                H, KVH, max_seq, L, inv_scale);
+        else
+            attn_tiled_kernel<64><<<grid, kFThreads, 0, st>>>(sc.qr, mr->k, mr->v, d_mask, mrows, mcols, sc.ao, seq, H,
+                                                               KVH, max_seq, L, inv_scale);
+    } else {
+        attn_kernel<<<dim3(seq, H, B), kAttnThreads, smem, st>>>(sc.qr, mr->k, mr->v, d_mask, mrows, mcols, sc.ao, seq,
+                                                                H, KVH, hd, max_seq, L, inv_scale);
+    }
     VOXQ_CUDA_TRY(cudaGetLastError());
     // h = x + a Wo^T ; n2 = RMSNorm(h) ; g = silu(n2 W1^T) * (n2 W3^T) ; o = h + g W2^T
     e = project(sc.ao, M, qk, w.wo, sc.h, d_x, nullptr, st);
