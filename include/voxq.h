@@ -499,6 +499,67 @@ VOXQ_API VoxCPMError voxq_vxcpm2_dequantize(const voxq_vxcpm2* f, int i, int q8_
 VOXQ_API VoxCPMError voxq_vxcpm2_upload_qweight(const voxq_vxcpm2* f, int i, uint8_t* d_codes, void* d_scales,
                                               void* stream);
 
+/* ======================================================================== */
+/* Pre-quantized weights in the engine's own VXCP container                 */
+/* ======================================================================== */
+/*
+ * The VXCP format (docs/WEIGHT_FORMAT.md §2, §5; read by weight_index_build /
+ * weight_load_tensor, src/model.c:1628-1877) names dtype 3 (Q4_0) and 4 (Q4_1)
+ * but its loader sizes both as 0 bytes and rejects them (src/model.c:1715-1727,
+ * 1855-1858), and it has no Q8 code.  voxq's VXCP quantized dtypes:
+ *
+ *   4  Q4_1  20-byte blocks of 32 values, fields in docs/WEIGHT_FORMAT.md §5
+ *            order: fp16 d, fp16 m, uint8 q[16] with byte i = q[2i] << 4 |
+ *            q[2i+1] (the nibble order of scripts/quantize.py:48-50);
+ *            value = q * d + m in fp32.  d, m, q are quantize_q4_block's
+ *            scale, min and codes (scripts/quantize.py:42-54).
+ *   5  Q8    40-byte blocks: fp32 d, fp32 m, uint8 q[32]; value = q * d + m
+ *            (q unsigned); quantize_q8_block's scale, min and codes
+ *            (scripts/quantize.py:69-75), header first like Q4_1.
+ *
+ * Blocks run over the flattened tensor, the last one zero-padded, as in
+ * scripts/quantize.py:239-260.  Q4_0 (3, 18-byte blocks per §5) has no
+ * producer and no defined dequantization; readers size it and reject it.
+ */
+enum { VOXQ_VXCP_FP32 = 0, VOXQ_VXCP_BF16 = 1, VOXQ_VXCP_FP16 = 2, VOXQ_VXCP_Q4_0 = 3, VOXQ_VXCP_Q4_1 = 4,
+       VOXQ_VXCP_Q8 = 5 };
+
+typedef struct {
+    uint32_t tensors;    /* tensors in the file */
+    uint32_t quantized;  /* tensors written as Q4_1 / Q8 */
+    uint64_t bytes_in, bytes_out;  /* file sizes */
+} voxq_vxcp_stats;
+
+/* Rewrites the VXCP model file src_path as dst_path with every 2-D fp32 /
+ * fp16 / bf16 tensor whose row length is a multiple of 32 quantized to
+ * qtype (VOXQ_Q4 -> dtype 4, VOXQ_Q8 -> dtype 5) on the current device,
+ * bit-exact with scripts/quantize.py's blocks; other tensors, and those whose
+ * name contains one of the n_keep strings in keep (e.g. "embed_tokens", a
+ * table the engine reads on the host, src/tslm.c:415), are copied unchanged.
+ * Header, metadata order, string table and both CRC32C checksums are written
+ * as make_model / convert_weights.py write them.  Host call; returns after the
+ * file is closed.  VOXCPM_ERR_FILE_NOT_FOUND, _INVALID_MODEL (magic, version,
+ * bounds), _UNSUPPORTED (a Q4_0 or unknown dtype, qtype not Q4 / Q8),
+ * _OOM, _INTERNAL (write failure; the partial file is removed). */
+VOXQ_API VoxCPMError voxq_vxcp_quantize(const char* src_path, const char* dst_path, int qtype,
+                                        const char* const* keep, int n_keep, voxq_vxcp_stats* stats);
+
+/* Hands tensor_to_cuda the quantize.py block stream (block fields in
+ * scripts/quantize.py order: codes, then scale and min) of a 2-D host weight
+ * loaded from a pre-quantized file.  Ownership of `blocks` (malloc'd,
+ * voxq_quant_bytes(N*K, qtype) bytes) passes to the library.  The tensor's own
+ * host data (the dequantized values, for any host-side reader) is left as it
+ * is; the next tensor_to_cuda(t) uploads the blocks to the packed device
+ * layout instead of quantizing t's values (whatever VOXCPM_QUANT says) and
+ * frees both.  Needs no device and no tensor_cuda_init.
+ * VOXCPM_ERR_SHAPE_MISMATCH (not 2-D, K % 32 != 0, wrong byte count, device
+ * tensor) or _UNSUPPORTED (qtype); on error ownership stays with the caller. */
+VOXQ_API VoxCPMError voxq_tensor_attach_blocks(const Tensor* t, int qtype, void* blocks, size_t nbytes);
+
+/* Frees the blocks attached to t, if any (call before freeing a tensor that
+ * was never uploaded).  Returns 1 if blocks were attached, else 0. */
+VOXQ_API int voxq_tensor_detach_blocks(const Tensor* t);
+
 #ifdef __cplusplus
 }
 #endif

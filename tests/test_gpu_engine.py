@@ -63,10 +63,11 @@ def _workdir():
     pytest.skip("no folder with 12 GB free for the 5 GB random-init model")
 
 
-def test_unchanged_engine_on_libvoxq_matches_cpu_engine():
+@pytest.fixture(scope="module")
+def model():
+    """The golden run's seeded random-init model, written once for this module:
+    (folder, model path prefix, golden metadata)."""
     meta = json.load(open(os.path.join(GOLDEN, "engine_c4_q8.json")))
-    gold = np.load(os.path.join(GOLDEN, "engine_c4_q8.npz"))
-    want, want_audio = gold["latents"], gold["audio"]
     for exe in ("make_model", "voxq_engine_run_gpu"):
         assert os.path.exists(os.path.join(BUILD, exe)), \
             f"{exe} missing: build it with `make -C voxcpm2-c_b200/engine REF=<reference checkout>`"
@@ -78,23 +79,39 @@ def test_unchanged_engine_on_libvoxq_matches_cpu_engine():
                                         text=True).stdout.strip().splitlines()[-1])
         for k in ("model_data_crc32c", "audiovae_data_crc32c", "model_bytes", "audiovae_bytes"):
             assert gen[k] == meta["model"][k], f"regenerated model differs from the golden run's ({k})"
-        runs = {}
-        for vae in ("gpu", "cpu"):
-            lat = os.path.join(work, f"lat_{vae}.f32")
-            aud = os.path.join(work, f"audio_{vae}.f32")
-            env = dict(os.environ, VOXCPM_QUANT="q8", VOXQ_ENGINE_VAE=vae)
-            r = subprocess.run([os.path.join(BUILD, "voxq_engine_run_gpu"), "--model", prefix + ".vxcpm", "--gpu",
-                                "--patches", str(meta["patches"]), "--tokens", str(meta["tokens"]),
-                                "--token-seed", str(meta["token_seed"]), "--latents", lat, "--audio", aud],
-                               env=env, capture_output=True, text=True, timeout=1200)
-            assert r.returncode == 0, r.stderr[-3000:]
-            assert "GPU upload complete" in r.stderr
-            runs[vae] = (json.loads(r.stdout.strip().splitlines()[-1]),
-                         np.fromfile(lat, dtype=np.float32).reshape(want.shape), np.fromfile(aud, dtype=np.float32))
-        run, got, got_audio = runs["gpu"]
-        _, got_cpu_vae, host_audio = runs["cpu"]
+        yield work, prefix, meta
     finally:
         shutil.rmtree(work, ignore_errors=True)
+
+
+def _run(exe, model_path, meta, work, tag, **env):
+    """One engine run; returns (its JSON line, latents, audio)."""
+    lat = os.path.join(work, f"lat_{tag}.f32")
+    aud = os.path.join(work, f"audio_{tag}.f32")
+    r = subprocess.run([os.path.join(BUILD, exe), "--model", model_path, "--gpu",
+                        "--patches", str(meta["patches"]), "--tokens", str(meta["tokens"]),
+                        "--token-seed", str(meta["token_seed"]), "--latents", lat, "--audio", aud],
+                       env=dict(os.environ, **env), capture_output=True, text=True, timeout=1200)
+    assert r.returncode == 0, r.stderr[-3000:]
+    assert "GPU upload complete" in r.stderr
+    out = (json.loads(r.stdout.strip().splitlines()[-1]), np.fromfile(lat, dtype=np.float32),
+           np.fromfile(aud, dtype=np.float32))
+    os.remove(lat)
+    os.remove(aud)
+    return out
+
+
+def test_unchanged_engine_on_libvoxq_matches_cpu_engine(model):
+    work, prefix, meta = model
+    gold = np.load(os.path.join(GOLDEN, "engine_c4_q8.npz"))
+    want, want_audio = gold["latents"], gold["audio"]
+    runs = {}
+    for vae in ("gpu", "cpu"):
+        run_, lat, aud = _run("voxq_engine_run_gpu", prefix + ".vxcpm", meta, work, vae, VOXCPM_QUANT="q8",
+                              VOXQ_ENGINE_VAE=vae)
+        runs[vae] = (run_, lat.reshape(want.shape), aud)
+    run, got, got_audio = runs["gpu"]
+    _, got_cpu_vae, host_audio = runs["cpu"]
     assert run["build"] == "gpu" and run["vae"] == "device"
     # every transformer block (TSLM, RALM, LocDiT, LocEnc) ran on the device
     assert run["blocks"]["device"] > 0 and run["blocks"]["host"] == 0, run["blocks"]
@@ -115,3 +132,48 @@ def test_unchanged_engine_on_libvoxq_matches_cpu_engine():
     print(f"audio, device vs host convolutions on the same latents: mean |d| {mean:.2e}, p99 {p99:.2e}, "
           f"max {float(d.max()):.2e}")
     assert mean <= AUDIO_MEAN_TOL and p99 <= AUDIO_P99_TOL, f"audio mean |d| {mean:.2e}, p99 {p99:.2e}"
+
+
+@pytest.mark.parametrize("quant", ["q8", "q4"])
+def test_prequantized_vxcp_file(model, quant):
+    """The engine starting from a pre-quantized VXCP file (voxq_vxcp_quantize:
+    every 2-D projection weight stored as Q8 / Q4_1 blocks, the host-read token
+    embedding kept as it is) through the qfile build, whose loader reads those
+    dtypes and hands the blocks to tensor_to_cuda, with VOXCPM_QUANT unset,
+    must produce the same latents bit for bit as the fp32/fp16 file quantized
+    on upload (VOXCPM_QUANT=q8 / q4): the device weights are the same
+    quantize.py blocks either way.  For Q8 that also ties it to the CPU
+    engine's golden latents (the model's weights are exact in Q8)."""
+    import sys
+    sys.path.insert(0, os.path.join(REPO, "voxcpm2-c_b200"))
+    import voxq
+    from voxq import vxcp
+    work, prefix, meta = model
+    exe = "voxq_engine_run_gpu_qfile"
+    assert os.path.exists(os.path.join(BUILD, exe)), f"{exe} missing: build the engine harness"
+    qdir = os.path.join(work, quant)
+    os.makedirs(qdir, exist_ok=True)
+    qpath = os.path.join(qdir, "rand.vxcpm")
+    st = vxcp.quantize_file(prefix + ".vxcpm", qpath, voxq.Q8 if quant == "q8" else voxq.Q4,
+                            keep=("embed_tokens",))
+    os.symlink(prefix + "_audiovae.vxcpm", os.path.join(qdir, "rand_audiovae.vxcpm"))
+    try:
+        assert st["quantized"] > 0 and st["bytes_out"] < st["bytes_in"], st
+        ref_run, ref_lat, _ = _run("voxq_engine_run_gpu", prefix + ".vxcpm", meta, work, "up_" + quant,
+                                   VOXCPM_QUANT=quant)
+        env = {k: v for k, v in os.environ.items() if k != "VOXCPM_QUANT"}
+        lat = os.path.join(work, f"lat_file_{quant}.f32")
+        r = subprocess.run([os.path.join(BUILD, exe), "--model", qpath, "--gpu", "--patches", str(meta["patches"]),
+                            "--tokens", str(meta["tokens"]), "--token-seed", str(meta["token_seed"]),
+                            "--latents", lat], env=env, capture_output=True, text=True, timeout=1200)
+        assert r.returncode == 0, r.stderr[-3000:]
+        run = json.loads(r.stdout.strip().splitlines()[-1])
+        got = np.fromfile(lat, dtype=np.float32)
+    finally:
+        shutil.rmtree(qdir, ignore_errors=True)
+    assert run["blocks"]["device"] > 0 and run["blocks"]["host"] == 0, run["blocks"]
+    print(f"{quant}: file {st['bytes_in'] / 1e9:.2f} GB -> {st['bytes_out'] / 1e9:.2f} GB, "
+          f"{st['quantized']} of {st['tensors']} tensors quantized; upload {run['upload_s']:.2f} s "
+          f"vs {ref_run['upload_s']:.2f} s quantizing on upload")
+    assert got.shape == ref_lat.shape and np.isfinite(got).all()
+    assert np.array_equal(got, ref_lat), f"max |d| {float(np.abs(got - ref_lat).max()):.3e}"

@@ -49,9 +49,22 @@ struct DevState {
     std::vector<void*> retired;  // outgrown workspace buffers, freed at shutdown
 };
 
+// Blocks of a pre-quantized weight waiting for tensor_to_cuda
+// (voxq_tensor_attach_blocks), keyed by the host tensor; `data` is the
+// tensor's host buffer at attach time, so a tensor later allocated at the
+// same address does not inherit them.
+struct Pending {
+    int qtype;
+    void* blocks;
+    size_t nbytes;
+    const void* data;
+};
+
 static DevState g_dev[kMaxDev];
-static std::mutex g_mu;  // guards g_dev growth and the side table
+static std::mutex g_mu;  // guards g_dev growth and the side tables
 static std::unordered_map<const void*, QRec> g_qtab;
+static std::unordered_map<const Tensor*, Pending> g_pending;
+static std::atomic<int> g_pending_n{0};
 static thread_local int t_dev = -1;
 
 int current_device() {
@@ -224,6 +237,45 @@ extern "C" int voxq_device_error(int clear) {
     return v ? v : na;
 }
 
+extern "C" VoxCPMError voxq_tensor_attach_blocks(const Tensor* t, int qtype, void* blocks, size_t nbytes) {
+    if (!t || !blocks) return VOXCPM_ERR_INTERNAL;
+    if (qtype != VOXQ_Q4 && qtype != VOXQ_Q8) return VOXCPM_ERR_UNSUPPORTED;
+    if (t->is_cuda || t->ndim != 2 || !t->shape || t->shape[0] <= 0 || t->shape[1] <= 0 ||
+        t->shape[1] % VOXQ_QBLK != 0)
+        return VOXCPM_ERR_SHAPE_MISMATCH;
+    if (nbytes != voxq_quant_bytes((size_t)t->shape[0] * t->shape[1], qtype)) return VOXCPM_ERR_SHAPE_MISMATCH;
+    const void* data = t->is_fp16 ? (const void*)t->data_fp16 : (const void*)t->data;
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_pending.find(t);
+    if (it != g_pending.end()) {
+        free(it->second.blocks);
+        it->second = Pending{qtype, blocks, nbytes, data};
+    } else {
+        g_pending.emplace(t, Pending{qtype, blocks, nbytes, data});
+        g_pending_n.fetch_add(1);
+    }
+    return VOXCPM_SUCCESS;
+}
+
+// Removes t's pending blocks from the table into *out (true) or reports none.
+static bool take_pending(const Tensor* t, Pending* out) {
+    if (g_pending_n.load() == 0) return false;
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_pending.find(t);
+    if (it == g_pending.end()) return false;
+    *out = it->second;
+    g_pending.erase(it);
+    g_pending_n.fetch_sub(1);
+    return true;
+}
+
+extern "C" int voxq_tensor_detach_blocks(const Tensor* t) {
+    Pending p;
+    if (!take_pending(t, &p)) return 0;
+    free(p.blocks);
+    return 1;
+}
+
 extern "C" VoxCPMError voxq_set_device(int device) {
     if (device < 0 || device >= kMaxDev) return VOXCPM_ERR_CUDA_NOT_FOUND;
     if (cudaSetDevice(device) != cudaSuccess) {
@@ -344,12 +396,77 @@ static bool lookup_q(const void* p, QRec* out) {
     return true;
 }
 
+// tensor_to_cuda for a weight with attached pre-quantized blocks: the blocks
+// go to the packed device layout as they are (voxq_pack_blocks), the host
+// buffers are freed, and the tensor becomes the same opaque device weight the
+// quantizing upload makes.
+static VoxCPMError upload_attached(DevState* s, Tensor* t, const Pending& pb) {
+    const int N = t->shape[0], K = t->shape[1], qt = pb.qtype;
+    const size_t cb = voxq_codes_bytes(N, K, qt), sb = voxq_scales_bytes(N, K, qt);
+    uint8_t* d_blocks = nullptr;
+    void* base = nullptr;
+    auto fail = [&](VoxCPMError e, cudaError_t ce, const char* what) {
+        if (ce != cudaSuccess)
+            fprintf(stderr, "[voxq] tensor_to_cuda (attached blocks): %s failed: %s\n", what, cudaGetErrorString(ce));
+        cudaStreamSynchronize(s->stream);
+        cudaGetLastError();
+        if (d_blocks) cudaFree(d_blocks);
+        if (base) cudaFree(base);
+        free(pb.blocks);
+        return e;
+    };
+    cudaError_t ce;
+    if ((ce = cudaMalloc(&d_blocks, pb.nbytes)) != cudaSuccess) {
+        d_blocks = nullptr;
+        return fail(VOXCPM_ERR_OOM, ce, "cudaMalloc");
+    }
+    if ((ce = cudaMalloc(&base, align256(cb) + sb)) != cudaSuccess) {
+        base = nullptr;
+        return fail(VOXCPM_ERR_OOM, ce, "cudaMalloc");
+    }
+    if ((ce = cudaMemcpyAsync(d_blocks, pb.blocks, pb.nbytes, cudaMemcpyHostToDevice, s->stream)) != cudaSuccess)
+        return fail(VOXCPM_ERR_INTERNAL, ce, "cudaMemcpy");
+    uint8_t* codes = (uint8_t*)base;
+    void* scales = (uint8_t*)base + align256(cb);
+    VoxCPMError e = voxq_pack_blocks(d_blocks, N, K, qt, codes, scales, s->stream);
+    if (e) return fail(e, cudaSuccess, "");
+    if ((ce = cudaStreamSynchronize(s->stream)) != cudaSuccess)
+        return fail(VOXCPM_ERR_INTERNAL, ce, "cudaStreamSynchronize");
+    cudaFree(d_blocks);
+    free(pb.blocks);
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        g_qtab[base] = QRec{base, codes, scales, N, K, qt, false};
+    }
+    if (t->is_fp16) {
+        free(t->data_fp16);
+        t->data_fp16 = nullptr;
+        t->is_fp16 = false;
+    } else {
+        free(t->data);
+    }
+    t->data = (float*)base;
+    t->is_cuda = true;
+    return VOXCPM_SUCCESS;
+}
+
 extern "C" VoxCPMError tensor_to_cuda(Tensor* t) {
     if (!t) return VOXCPM_ERR_INTERNAL;
     if (t->is_cuda) return VOXCPM_SUCCESS;
     if (t->size == 0) return VOXCPM_SUCCESS;
     DevState* s = state();
     if (!s || !s->init) return VOXCPM_ERR_CUDA_NOT_FOUND;
+    {
+        Pending pb;
+        if (take_pending(t, &pb)) {
+            const void* data = t->is_fp16 ? (const void*)t->data_fp16 : (const void*)t->data;
+            // blocks attached to an earlier tensor at this address: dropped
+            if (data == pb.data && t->ndim == 2 &&
+                pb.nbytes == voxq_quant_bytes((size_t)t->shape[0] * t->shape[1], pb.qtype))
+                return upload_attached(s, t, pb);
+            free(pb.blocks);
+        }
+    }
     const bool quantize = s->quant != VOXQ_F32 && t->ndim == 2 && t->shape[1] > 0 &&
                           t->shape[1] % VOXQ_QBLK == 0 && (t->is_fp16 ? t->data_fp16 != nullptr : t->data != nullptr);
     if (quantize) {

@@ -176,6 +176,9 @@ SIGNATURES = {
     "voxq_vxcpm2_verify": ([_vp], _i),
     "voxq_vxcpm2_dequantize": ([_vp, _i, _i, _vp], _i),
     "voxq_vxcpm2_upload_qweight": ([_vp, _i, _vp, _vp, _vp], _i),
+    "voxq_vxcp_quantize": ([C.c_char_p, C.c_char_p, _i, C.POINTER(C.c_char_p), _i, _vp], _i),
+    "voxq_tensor_attach_blocks": ([_TP, _i, _vp, _sz], _i),
+    "voxq_tensor_detach_blocks": ([_TP], _i),
 }
 
 _lib = None
