@@ -567,8 +567,17 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32) gemv_kernel(const __gri
 // only on K, not on T, so the launch may pick T (smaller tiles for small
 // launches) without changing a single bit of the result.
 // ---------------------------------------------------------------------------
-constexpr int kMmaWarps = 8;                     // consumer warps (+1 producer)
-constexpr int kMmaStages = 2;
+#ifndef VOXQ_GEMV_MMA_WARPS
+#define VOXQ_GEMV_MMA_WARPS 8
+#endif
+constexpr int kMmaWarps = VOXQ_GEMV_MMA_WARPS;   // consumer warps (+1 producer)
+#ifndef VOXQ_GEMV_MMA_STAGES
+#define VOXQ_GEMV_MMA_STAGES 2
+#endif
+#ifndef VOXQ_GEMV_MMA_MINB
+#define VOXQ_GEMV_MMA_MINB 2  // CTAs per SM the register budget is sized for
+#endif
+constexpr int kMmaStages = VOXQ_GEMV_MMA_STAGES;
 constexpr int kMmaTile = 32768;                  // code bytes per stage
 constexpr int kMmaTW = kMmaTile / 4 + 32;        // trailer window bytes per stage
 // A stage: the code region (two halves of the tile's rows, see split_tile)
@@ -706,7 +715,7 @@ __device__ __forceinline__ void produce_split(const GemvParams<MAXI>& p, int tb,
 // TRX (Q4, every item's trailer rows a multiple of 16 bytes): trailers handed
 // to the lanes through a per-warp scratch (see the unit loop).
 template <int QT, bool SIGNED, bool TRX, int MAXI>
-__global__ void __launch_bounds__((kMmaWarps + 1) * 32, 2) gemv_mma_kernel(const __grid_constant__ GemvParams<MAXI> p) {
+__global__ void __launch_bounds__((kMmaWarps + 1) * 32, VOXQ_GEMV_MMA_MINB) gemv_mma_kernel(const __grid_constant__ GemvParams<MAXI> p) {
     constexpr int G = limb_granules(QT);
     constexpr int SB = (QT == VOXQ_Q4) ? 4 : 8;  // trailer bytes per block
     constexpr int STAGE = kMmaStage;
