@@ -969,11 +969,12 @@ def measure_c4(patches=4, workdir=None, cpu_patches=0, model=None):
         # engine deviation
         out["ours_200_patches"] = _engine_run("voxq_engine_run_gpu", model, 200, {"VOXCPM_QUANT": "q8"},
                                               ["--gpu", "--ralm-max-seq", "16384"])
-        # the same build with only the tensor.h boundary in use: the engine's own blocks, sampler
-        # and AudioVAE decoder on the host, their projections through tensor_matmul_nt_cuda
+        # the same build with only the tensor.h boundary in use: the engine's own blocks, sampler,
+        # encoder and AudioVAE decoder on the host, their projections through tensor_matmul_nt_cuda
         out["ours_tensor_h_only"] = _engine_run("voxq_engine_run_gpu", model, patches,
                                                 {"VOXCPM_QUANT": "q8", "VOXQ_ENGINE_BLOCK": "cpu",
-                                                 "VOXQ_ENGINE_DIT": "cpu", "VOXQ_ENGINE_VAE": "cpu"}, ["--gpu"])
+                                                 "VOXQ_ENGINE_DIT": "cpu", "VOXQ_ENGINE_LOCENC": "cpu",
+                                                 "VOXQ_ENGINE_VAE": "cpu"}, ["--gpu"])
         if os.path.exists(os.path.join(ENGINE_BUILD, "voxq_engine_run_refgpu")):
             out["reference_gpu"] = _engine_run("voxq_engine_run_refgpu", model, patches, {}, ["--gpu"])
         if cpu_patches > 0:

@@ -451,6 +451,28 @@ typedef struct {
 VOXQ_API VoxCPMError voxq_locdit_sample(const voxq_locdit_desc* dit, const Tensor* mu, const Tensor* cond,
                                         int n_timesteps, float cfg_value, const Tensor* x_init, Tensor* out);
 
+/* loc_enc_forward (src/loc_enc.c:19-190) on the device, the hidden state
+ * resident across all layers: audio_feats [B, T, P, F] (host) -> in_proj
+ * (+ bias) -> per time step [special token; P projected patches] -> the
+ * n_layers blocks (bidirectional attention over all T (P + 1) tokens, no RoPE,
+ * scratch K/V as the reference's single-use per-call cache) -> each step's
+ * first token -> output RMSNorm -> out [B, T, D] (host).  The descriptor has
+ * the field layout of the engine's LocEnc (include/model.h:141-150).  Returns
+ * VOXCPM_ERR_CUDA_NOT_FOUND (the caller then runs its own code) for host
+ * weights, device operands, shapes the kernels do not take, or before
+ * tensor_cuda_init. */
+typedef struct {
+    const Tensor* in_proj_weight;   /* [D, F], quantized by tensor_to_cuda */
+    const Tensor* in_proj_bias;     /* [D] host, or NULL */
+    const Tensor* special_token;    /* [1, 1, 1, D] host */
+    const voxq_block_desc* layers;  /* n_layers blocks */
+    int n_layers;
+    const voxq_rmsnorm_desc* output_norm;
+    int d_model;
+    int patch_size;
+} voxq_locenc_desc;
+VOXQ_API VoxCPMError voxq_locenc_forward(const voxq_locenc_desc* enc, const Tensor* audio_feats, Tensor* out);
+
 /* ---- quantize.py weight containers (VXCPM2) ---------------------------
  * Reads the container written by the reference's quantizer
  * (scripts/quantize.py:110-312): a 256-byte header, the layer-group offset

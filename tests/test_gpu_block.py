@@ -88,11 +88,11 @@ def block_ref(x, W, ck, cv, mask, freqs, pos, H, KVH, hd, eps):
     return h + g @ W["w2"].T
 
 
-def close(got, ref, what):
+def close(got, ref, what, tol=TOL):
     ref = np.asarray(ref, dtype=np.float64)
     scale = np.sqrt((ref ** 2).mean()) + np.abs(ref)
     err = np.abs(got.astype(np.float64) - ref)
-    bad = err > TOL * scale
+    bad = err > tol * scale
     assert np.isfinite(got).all(), what
     assert not bad.any(), f"{what}: {int(bad.sum())} of {bad.size} beyond tol; worst {float((err / scale).max()):.2e}"
     return float((err / scale).max())
@@ -200,6 +200,82 @@ def test_block_on_device_matches_reference(qname):
         run(36, 0, ck3, cv3, rk3, rv3, True, True, "prefill S=36 (tiled attention)")
         run(32, 36, ck3, cv3, rk3, rv3, True, True, "continuation S=32 over 68 > 2 key tiles")
         assert voxq.lib().voxq_device_error(1) == 0
+    finally:
+        for t in keep:
+            voxq.free_tensor(t)
+        L.voxq_block_cache_clear()
+        L.tensor_cuda_shutdown()
+        os.environ.pop("VOXCPM_QUANT", None)
+
+
+@pytest.mark.parametrize("qname", ["q8", "q4"])
+def test_locenc_on_device_matches_reference(qname):
+    """voxq_locenc_forward against a float64 restatement of loc_enc_forward
+    (src/loc_enc.c:19-190): in_proj + bias, [special; P patches] per step, the
+    layers over all T (P + 1) tokens (bidirectional, no RoPE, fresh cache at
+    pos 0), each step's first token, output RMSNorm.  T = 2 takes the per-row
+    attention kernel, T = 13 the tiled one.  Rule: 5e-3 of scale (two chained
+    layers of fp16 tensor-core projections; one block alone meets 1e-3)."""
+    L = voxq.lib()
+    os.environ["VOXCPM_QUANT"] = qname
+    L.tensor_cuda_shutdown()
+    assert L.tensor_cuda_init() == 0
+    rng = np.random.default_rng(23)
+    D, H, KVH, hd, FF, eps, Fd, P, NL = 256, 4, 2, 64, 512, 1e-6, 64, 4, 2
+    layers = []
+    for _ in range(NL):
+        layers.append({"wq": exact_weight(rng, H * hd, D, qname), "wk": exact_weight(rng, KVH * hd, D, qname),
+                       "wv": exact_weight(rng, KVH * hd, D, qname), "wo": exact_weight(rng, D, H * hd, qname),
+                       "w1": exact_weight(rng, FF, D, qname), "w2": exact_weight(rng, D, FF, qname),
+                       "w3": exact_weight(rng, FF, D, qname),
+                       "n1": (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32),
+                       "n2": (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32)})
+    win = exact_weight(rng, D, Fd, qname)
+    b_in = (0.02 * rng.standard_normal(D)).astype(np.float32)
+    special = (0.02 * rng.standard_normal(D)).astype(np.float32)
+    wn = (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    keep, descs = [], []
+    try:
+        blocks = (voxq.BlockDesc * NL)()
+        for l, W in enumerate(layers):
+            T_ = {k: voxq.host_tensor(W[k]) for k in W}
+            keep += list(T_.values())
+            for k in ("wq", "wk", "wv", "wo", "w1", "w2", "w3"):
+                voxq.check(L.tensor_to_cuda(T_[k]), "tensor_to_cuda")
+            n1, n2 = voxq.RmsNormDesc(T_["n1"], eps), voxq.RmsNormDesc(T_["n2"], eps)
+            at = voxq.AttentionDesc(T_["wq"], T_["wk"], T_["wv"], T_["wo"], D, H, KVH, hd)
+            ff = voxq.SwigluDesc(T_["w1"], T_["w2"], T_["w3"], D, FF)
+            descs += [n1, n2, at, ff]
+            blocks[l] = voxq.BlockDesc(C.pointer(n1), C.pointer(at), C.pointer(n2), C.pointer(ff))
+        tw, tb = voxq.host_tensor(win), voxq.host_tensor(b_in)
+        ts = voxq.host_tensor(special.reshape(1, 1, 1, D))
+        tn = voxq.host_tensor(wn)
+        keep += [tw, tb, ts, tn]
+        voxq.check(L.tensor_to_cuda(tw), "tensor_to_cuda")
+        on = voxq.RmsNormDesc(tn, eps)
+        enc = voxq.LocEncDesc(tw, tb, ts, C.cast(blocks, C.POINTER(voxq.BlockDesc)), NL, C.pointer(on), D, P)
+        for T in (2, 13):
+            feats = rng.standard_normal((1, T, P, Fd)).astype(np.float32)
+            tf = voxq.host_tensor(feats)
+            to = voxq.host_tensor(np.zeros((1, T, D), np.float32))
+            try:
+                assert L.voxq_locenc_forward(C.byref(enc), tf, to) == 0
+                got = voxq.host_tensor_view(to)
+            finally:
+                voxq.free_tensor(tf)
+                voxq.free_tensor(to)
+            proj = feats.reshape(T * P, Fd).astype(np.float64) @ win.T.astype(np.float64) + b_in
+            x = np.concatenate([np.broadcast_to(special, (T, 1, D)), proj.reshape(T, P, D)], 1)
+            x = x.reshape(1, T * (P + 1), D)
+            S = T * (P + 1)
+            for W in layers:
+                ck, cv = np.zeros((1, KVH, S, hd)), np.zeros((1, KVH, S, hd))
+                x = block_ref(x, W, ck, cv, None, None, 0, H, KVH, hd, eps)
+            ref = rmsnorm(x.reshape(T, P + 1, D)[:, 0][None], wn, eps)
+            # two chained layers whose projections (more than 8 rows) run on fp16 tensor cores:
+            # the library's GEMM rule, 5e-3, rather than the single block's 1e-3
+            close(got, ref, f"locenc {qname} T={T}", tol=5e-3)
+        assert L.voxq_device_error(1) == 0
     finally:
         for t in keep:
             voxq.free_tensor(t)

@@ -347,6 +347,30 @@ __global__ void dit_slice_kernel(const float* __restrict__ seq, float* __restric
     }
 }
 
+// LocEnc input sequence (src/loc_enc.c:104-122): per (b, t) the special
+// token, then the step's P projected patches; x [B][T (P + 1)][D].
+__global__ void enc_seq_kernel(float* __restrict__ x, const float* __restrict__ proj,
+                               const float* __restrict__ special, int B, int T, int P, int D) {
+    const int64_t n = (int64_t)B * T * (P + 1) * D;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int d = (int)(i % D);
+        const int64_t r = i / D;  // (b, t, j) row
+        const int j = (int)(r % (P + 1));
+        const int64_t bt = r / (P + 1);
+        x[i] = j == 0 ? special[d] : proj[(bt * P + (j - 1)) * D + d];
+    }
+}
+
+// Each step's first token (src/loc_enc.c:168-177): cls [B T][D].
+__global__ void enc_cls_kernel(const float* __restrict__ x, float* __restrict__ cls, int BT, int P, int D) {
+    const int64_t n = (int64_t)BT * D;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int d = (int)(i % D);
+        const int64_t bt = i / D;
+        cls[i] = x[bt * (P + 1) * D + d];
+    }
+}
+
 // Euler step with guidance: v rows [nb * P][F] (branch 0 conditional);
 // x [F][P] -= dt * (v_u + cfg (v_c - v_u)) (or v_c alone).
 __global__ void dit_step_kernel(float* __restrict__ x, const float* __restrict__ v, int nb, int P, int F, float cfg,
@@ -1067,6 +1091,90 @@ extern "C" VoxCPMError voxq_locdit_sample(const voxq_locdit_desc* dit, const Ten
     VOXQ_CUDA_TRY(cudaStreamSynchronize(st));
     memcpy(out->data, h_out, (size_t)F * P * sizeof(float));
     count_matmul_traffic((uint64_t)n_timesteps * (7 * dit->n_layers + 6) + (Tc > 0 ? 1 : 0), traffic);
+    return VOXCPM_SUCCESS;
+}
+
+extern "C" VoxCPMError voxq_locenc_forward(const voxq_locenc_desc* enc, const Tensor* audio_feats, Tensor* out) {
+    constexpr VoxCPMError kHost = VOXCPM_ERR_CUDA_NOT_FOUND;
+    if (!enc || !audio_feats || !out || !enc->layers || enc->n_layers < 1 || !enc->output_norm ||
+        !enc->special_token)
+        return kHost;
+    cudaStream_t st = (cudaStream_t)library_stream();
+    if (!st) return kHost;
+    const int D = enc->d_model;
+    if (!is_host_f32(audio_feats) || audio_feats->ndim != 4 || !is_host_f32(out) || out->ndim != 3) return kHost;
+    const int B = audio_feats->shape[0], T = audio_feats->shape[1], P = audio_feats->shape[2],
+              F = audio_feats->shape[3];
+    if (B < 1 || T < 1 || P < 1 || F < 1 || out->shape[0] != B || out->shape[1] != T || out->shape[2] != D)
+        return kHost;
+    if (!is_host_f32(enc->special_token) || enc->special_token->size < (size_t)D) return kHost;
+    voxq_qweight win;
+    if (!device_qweight(enc->in_proj_weight, &win) || win.N != D || win.K != F) return kHost;
+    const int S = T * (P + 1), M = B * S;
+    if (S > kMaxCacheLen) return kHost;
+    std::vector<BlockW> bw(enc->n_layers);
+    for (int l = 0; l < enc->n_layers; l++)
+        if (!block_weights(&enc->layers[l], &bw[l]) || bw[l].D != D) return kHost;
+    const int dev = current_device();
+    if (dev < 0 || dev >= 16) return kHost;
+
+    std::lock_guard<std::mutex> lk(g_blk_mu);
+    BlockDev& bd = g_blk[dev];
+    VoxCPMError e = VOXCPM_SUCCESS;
+    for (int l = 0; l < enc->n_layers; l++) {
+        e = block_norms(bd, &enc->layers[l], &bw[l], st);
+        if (e) return e;
+    }
+    const float *b_in = nullptr, *d_special = nullptr, *w_on = nullptr;
+    e = norm_weight(bd, enc->in_proj_bias, st, &b_in);
+    if (!e) e = norm_weight(bd, enc->special_token, st, &d_special);
+    if (!e) e = norm_weight(bd, enc->output_norm->weight, st, &w_on);
+    if (e) return e;
+    // arena: sequence | block scratch | K | V | features | projections | cls rows
+    int maxKVH = 0, maxhd = 0;
+    size_t scr = 0;
+    for (auto& w : bw) {
+        maxKVH = std::max(maxKVH, w.KVH);
+        maxhd = std::max(maxhd, w.hd);
+        scr = std::max(scr, scratch_floats(M, w));
+    }
+    const size_t nx = (size_t)M * D, nkv = (size_t)B * maxKVH * S * maxhd, nf = (size_t)B * T * P * F,
+                 np = (size_t)B * T * P * D, nc = (size_t)B * T * D;
+    const size_t o_scr = al64(nx), o_k = o_scr + scr, o_v = o_k + al64(nkv), o_f = o_v + al64(nkv),
+                 o_p = o_f + al64(nf), o_c = o_p + al64(np), total = o_c + al64(nc);
+    if (!grow(&bd.dit_arena, &bd.dit_arena_floats, total, false, st)) return VOXCPM_ERR_OOM;
+    if (!grow(&bd.h_stage, &bd.h_stage_floats, al64(nf) + nc, true, st)) return VOXCPM_ERR_OOM;
+    float* A = bd.dit_arena;
+    float *d_x = A, *d_feats = A + o_f, *d_proj = A + o_p, *d_cls = A + o_c;
+    float* h_f = bd.h_stage;
+    float* h_out = bd.h_stage + al64(nf);
+    memcpy(h_f, audio_feats->data, nf * sizeof(float));
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(d_feats, h_f, nf * sizeof(float), cudaMemcpyHostToDevice, st));
+    // input projection + bias (src/loc_enc.c:76-101)
+    voxq_epilogue ei = {b_in, nullptr, 0, nullptr};
+    e = voxq_matmul_nt_q(d_feats, B * T * P, F, &win, d_proj, D, &ei, st);
+    if (e) return e;
+    enc_seq_kernel<<<ew((int)std::min<size_t>(nx, 1 << 20)), 256, 0, st>>>(d_x, d_proj, d_special, B, T, P, D);
+    VOXQ_CUDA_TRY(cudaGetLastError());
+    // the layers, in place, each over a fresh scratch cache (pos 0, length S)
+    Mirror kvm;
+    kvm.k = A + o_k;
+    kvm.v = A + o_v;
+    uint64_t traffic = (uint64_t)voxq_codes_bytes(win.N, win.K, win.qtype) + voxq_scales_bytes(win.N, win.K, win.qtype);
+    for (int l = 0; l < enc->n_layers; l++) {
+        const Scratch sc = scratch_at(A + o_scr, M, bw[l]);
+        e = block_core(bw[l], sc, d_x, d_x, B, S, &kvm, S, 0, nullptr, 0, 0, nullptr, nullptr, nullptr, st);
+        if (e) return e;
+        traffic += block_weight_bytes(bw[l]);
+    }
+    // first token of each step, output norm (src/loc_enc.c:168-186)
+    enc_cls_kernel<<<ew((int)nc), 256, 0, st>>>(d_x, d_cls, B * T, P, D);
+    rmsnorm_kernel<<<B * T, kBlockThreads, 0, st>>>(d_cls, w_on, enc->output_norm->eps, d_cls, D);
+    VOXQ_CUDA_TRY(cudaGetLastError());
+    VOXQ_CUDA_TRY(cudaMemcpyAsync(h_out, d_cls, nc * sizeof(float), cudaMemcpyDeviceToHost, st));
+    VOXQ_CUDA_TRY(cudaStreamSynchronize(st));
+    memcpy(out->data, h_out, nc * sizeof(float));
+    count_matmul_traffic(1 + 7 * (uint64_t)enc->n_layers, traffic);
     return VOXCPM_SUCCESS;
 }
 

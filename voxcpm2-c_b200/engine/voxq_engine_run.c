@@ -110,9 +110,24 @@ VoxCPMError __wrap_ralm_forward(RALM* ralm, const Tensor* x, const Tensor* freqs
 }
 
 VoxCPMError __real_loc_enc_forward(const LocEnc* enc, const Tensor* feats, Tensor* out);
+/* loc_enc_forward: in the libvoxq build the whole encoder runs on the device
+ * (voxq_locenc_forward: the hidden state resident across the 12 layers, one
+ * upload of the features, one download of the step embeddings) instead of a
+ * host round trip per layer; VOXQ_ENGINE_LOCENC=cpu keeps the engine's own
+ * loop (its blocks still go to the device one by one). */
+static int g_enc_gpu = 1;
+static VoxCPMError enc_forward(const LocEnc* enc, const Tensor* feats, Tensor* out) {
+#ifdef VOXQ_ENGINE_LIBVOXQ
+    if (g_enc_gpu) {
+        const VoxCPMError r = voxq_locenc_forward((const voxq_locenc_desc*)enc, feats, out);
+        if (r != VOXCPM_ERR_CUDA_NOT_FOUND) return r;
+    }
+#endif
+    return __real_loc_enc_forward(enc, feats, out);
+}
 VoxCPMError __wrap_loc_enc_forward(const LocEnc* enc, const Tensor* feats, Tensor* out) {
     VoxCPMError r;
-    TIMED(ST_LOCENC, __real_loc_enc_forward(enc, feats, out));
+    TIMED(ST_LOCENC, enc_forward(enc, feats, out));
     return r;
 }
 
@@ -517,6 +532,7 @@ int main(int argc, char** argv) {
     }
     if (getenv("VOXQ_ENGINE_BLOCK") && !strcmp(getenv("VOXQ_ENGINE_BLOCK"), "cpu")) g_block_gpu = 0;
     if (getenv("VOXQ_ENGINE_DIT") && !strcmp(getenv("VOXQ_ENGINE_DIT"), "cpu")) g_dit_gpu = 0;
+    if (getenv("VOXQ_ENGINE_LOCENC") && !strcmp(getenv("VOXQ_ENGINE_LOCENC"), "cpu")) g_enc_gpu = 0;
 #endif
     g_dump_dir = getenv("VOXQ_ENGINE_DUMP_DIR");
 

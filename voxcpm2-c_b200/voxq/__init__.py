@@ -133,6 +133,13 @@ class BlockDesc(C.Structure):
                 ("rms_ffn", C.POINTER(RmsNormDesc)), ("ffn", C.POINTER(SwigluDesc))]
 
 
+class LocEncDesc(C.Structure):
+    """voxq_locenc_desc (the engine's LocEnc)."""
+    _fields_ = [("in_proj_weight", C.POINTER(Tensor)), ("in_proj_bias", C.POINTER(Tensor)),
+                ("special_token", C.POINTER(Tensor)), ("layers", C.POINTER(BlockDesc)), ("n_layers", C.c_int),
+                ("output_norm", C.POINTER(RmsNormDesc)), ("d_model", C.c_int), ("patch_size", C.c_int)]
+
+
 _vp, _sz, _i, _i64 = C.c_void_p, C.c_size_t, C.c_int, C.c_int64
 _TP = C.POINTER(Tensor)
 SIGNATURES = {
@@ -168,6 +175,7 @@ SIGNATURES = {
     "voxq_transformer_block_forward": ([C.POINTER(BlockDesc), _TP, _TP, _TP, _TP, _TP, _i, _TP], _i),
     "voxq_block_cache_clear": ([], None),
     "voxq_locdit_sample": ([_vp, _TP, _TP, _i, C.c_float, _TP, _TP], _i),
+    "voxq_locenc_forward": ([_vp, _TP, _TP], _i),
     "voxq_vxcpm2_open": ([C.c_char_p, C.POINTER(_vp)], _i),
     "voxq_vxcpm2_close": ([_vp], None),
     "voxq_vxcpm2_info": ([_vp, C.POINTER(Vxcpm2Header), C.POINTER(_i)], _i),
