@@ -199,6 +199,17 @@ def test_block_on_device_matches_reference(qname):
         ck3, cv3, rk3, rv3 = cache(96)
         run(36, 0, ck3, cv3, rk3, rv3, True, True, "prefill S=36 (tiled attention)")
         run(32, 36, ck3, cv3, rk3, rv3, True, True, "continuation S=32 over 68 > 2 key tiles")
+        # a continuation of a long cache with few query tiles: the keys are split over several
+        # CTAs and the splits combined (the RALM's per-patch call late in an utterance); the
+        # earlier rows come from the host cache (a fresh mirror); the second call at the same
+        # position passes an equal mask (its device copy is reused), the third a new one
+        ck4, cv4, rk4, rv4 = cache(2304)
+        for arr, ref in ((as_array(ck4), rk4), (as_array(cv4), rv4)):
+            arr[:, :, :2048] = rng.standard_normal((B, KVH, 2048, hd)).astype(np.float32)
+            ref[:, :, :2048] = arr[:, :, :2048]
+        run(64, 2048, ck4, cv4, rk4, rv4, True, False, "continuation S=64 at pos 2048 (key splits)")
+        run(64, 2048, ck4, cv4, rk4, rv4, True, False, "again at pos 2048 (mask reused)")
+        run(64, 2112, ck4, cv4, rk4, rv4, True, False, "continuation S=64 at pos 2112 (key splits)")
         assert voxq.lib().voxq_device_error(1) == 0
     finally:
         for t in keep:

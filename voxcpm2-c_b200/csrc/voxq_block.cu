@@ -208,14 +208,20 @@ __global__ void __launch_bounds__(kFThreads) attn_tiled_kernel(const float* __re
                                                                const float* __restrict__ cv,
                                                                const float* __restrict__ mask, int mrows, int mcols,
                                                                float* __restrict__ out, int seq, int H, int KVH,
-                                                               int max_seq, int L, float inv_scale) {
+                                                               int max_seq, int L, float inv_scale, int nsplit,
+                                                               float* __restrict__ partial) {
     constexpr int DPT = HD / 4;
     __shared__ __align__(16) float Ks[kFK][HD];
     __shared__ __align__(16) float Vs[kFK][HD];
     const int G = H / KVH, QR = 64 / G;
     const int kh = blockIdx.y, b = blockIdx.z;
+    // blockIdx.x = query tile * nsplit + key split; split sp takes whole key
+    // tiles [sp * tps, (sp + 1) * tps)
+    const int qt = blockIdx.x / nsplit, sp = blockIdx.x % nsplit;
+    const int ntiles = (L + kFK - 1) / kFK, tps = (ntiles + nsplit - 1) / nsplit;
+    const int t_beg = sp * tps * kFK, t_end = min(L, (sp + 1) * tps * kFK);
     const int r = threadIdx.x >> 2, part = threadIdx.x & 3;
-    const int h = kh * G + r % G, s = blockIdx.x * QR + r / G;
+    const int h = kh * G + r % G, s = qt * QR + r / G;
     const bool valid = s < seq;
     float qv[DPT], acc[DPT];
     const float* qr = q + (((int64_t)b * H + h) * seq + (valid ? s : 0)) * HD;
@@ -227,9 +233,9 @@ __global__ void __launch_bounds__(kFThreads) attn_tiled_kernel(const float* __re
     float m = -INFINITY, l = 0.0f;
     const float* kb = ck + ((int64_t)b * KVH + kh) * max_seq * HD;
     const float* vb = cv + ((int64_t)b * KVH + kh) * max_seq * HD;
-    for (int t0 = 0; t0 < L; t0 += kFK) {
+    for (int t0 = t_beg; t0 < t_end; t0 += kFK) {
         __syncthreads();  // the previous tile is consumed
-        const int nt = min(kFK, L - t0);
+        const int nt = min(kFK, t_end - t0);
         for (int i = threadIdx.x; i < kFK * HD / 4; i += kFThreads) {
             const int row = (i * 4) / HD, col = (i * 4) % HD;
             float4 kk = make_float4(0.f, 0.f, 0.f, 0.f), vv = kk;
@@ -272,11 +278,65 @@ __global__ void __launch_bounds__(kFThreads) attn_tiled_kernel(const float* __re
         }
         m = mn;
     }
+    if (nsplit > 1) {
+        // this split's running max, sum and unnormalised accumulator, combined by attn_combine_kernel
+        const int nqt = gridDim.x / nsplit;
+        float* rec = partial + (((((int64_t)b * KVH + kh) * nqt + qt) * nsplit + sp) * 64 + r) * (HD + 2);
+        if (part == 0) {
+            rec[0] = m;
+            rec[1] = l;
+        }
+#pragma unroll
+        for (int j = 0; j < DPT; j++) rec[2 + part + 4 * j] = acc[j];
+        return;
+    }
     if (!valid) return;
     const float inv = 1.0f / (l + 1e-10f);
     float* orow = out + (((int64_t)b * seq + s) * H + h) * HD;
 #pragma unroll
     for (int j = 0; j < DPT; j++) orow[part + 4 * j] = acc[j] * inv;
+}
+
+// Combines the key splits of attn_tiled_kernel: one warp per query vector,
+// M = max m_sp, l = sum l_sp e^(m_sp - M), acc = sum acc_sp e^(m_sp - M),
+// out = acc / (l + 1e-10) -- the single pass's result up to fp32 rounding;
+// a vector whose keys were all masked gets zeros, as in the single pass.
+template <int HD>
+__global__ void attn_combine_kernel(const float* __restrict__ partial, float* __restrict__ out, int seq, int H,
+                                    int KVH, int B, int nqt, int nsplit) {
+    const int G = H / KVH, QR = 64 / G;
+    const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw >= (int64_t)B * KVH * nqt * 64) return;
+    const int r = (int)(gw % 64);
+    const int64_t tile = gw / 64;  // ((b * KVH + kh) * nqt + qt)
+    const int qt = (int)(tile % nqt), kh = (int)((tile / nqt) % KVH), b = (int)(tile / ((int64_t)nqt * KVH));
+    const int h = kh * G + r % G, s = qt * QR + r / G;
+    if (s >= seq) return;
+    const float* rec0 = partial + (tile * nsplit * 64 + r) * (HD + 2);
+    const int64_t step = (int64_t)64 * (HD + 2);
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; sp++) M = fmaxf(M, rec0[sp * step]);
+    constexpr int DPL = HD / 32;
+    float acc[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; j++) acc[j] = 0.0f;
+    float l = 0.0f;
+    if (M != -INFINITY) {
+        for (int sp = 0; sp < nsplit; sp++) {
+            const float* rec = rec0 + sp * step;
+            const float ms = rec[0];
+            if (ms == -INFINITY) continue;
+            const float f = expf(ms - M);
+            l = fmaf(rec[1], f, l);
+#pragma unroll
+            for (int j = 0; j < DPL; j++) acc[j] = fmaf(rec[2 + lane + 32 * j], f, acc[j]);
+        }
+    }
+    const float inv = 1.0f / (l + 1e-10f);
+    float* orow = out + (((int64_t)b * seq + s) * H + h) * HD;
+#pragma unroll
+    for (int j = 0; j < DPL; j++) orow[lane + 32 * j] = acc[j] * inv;
 }
 
 // Gathers cache rows [r0, r1) of every (b, kv head) from a contiguous host
@@ -417,6 +477,15 @@ struct BlockDev {
     size_t dit_arena_floats = 0;
     float* h_stage = nullptr;  // pinned
     size_t h_stage_floats = 0;
+    float* attn_part = nullptr;  // key-split partials of the tiled attention
+    size_t attn_part_floats = 0;
+    // the last mask uploaded by a non-graph call, kept on the device while the
+    // host rows stay equal (the engine builds one mask per forward and passes it
+    // to every layer)
+    float* mask_dev = nullptr;
+    size_t mask_dev_floats = 0;
+    std::vector<float> mask_host;
+    int mask_rows = 0, mask_cols = 0;
     uint64_t clock = 0;
     // CUDA graphs of repeated fill calls (pos 0, seq = cache length: the LocDiT's
     // per-forward blocks), keyed by every pointer and size the launches bake in;
@@ -686,7 +755,8 @@ Scratch scratch_at(float* p, int M, const BlockW& w) {
 // are given, into them ([B][KVH][seq][hd], for the host write-back).
 VoxCPMError block_core(const BlockW& w, const Scratch& sc, const float* d_x, float* d_o, int B, int seq,
                        const Mirror* mr, int max_seq, int pos, const float* d_mask, int mrows, int mcols,
-                       const float* d_freqs, float* d_kn, float* d_vn, cudaStream_t st) {
+                       const float* d_freqs, float* d_kn, float* d_vn, cudaStream_t st, float* part_buf = nullptr,
+                       size_t part_floats = 0) {
     const int M = B * seq, D = w.D, H = w.H, KVH = w.KVH, hd = w.hd, F = w.F, qk = H * hd, L = pos + seq;
     VoxCPMError e = VOXCPM_SUCCESS;
     // n = RMSNorm(x)
@@ -726,14 +796,32 @@ VoxCPMError block_core(const BlockW& w, const Scratch& sc, const float* d_x, flo
     const int G = H / KVH;
     const float inv_scale = 1.0f / sqrtf((float)hd);
     if (seq * G >= 64 && 64 % G == 0 && (hd == 64 || hd == 128)) {
-        // many query rows: tiled, key / value tiles shared by 64 query vectors
-        const dim3 grid((unsigned)((seq + 64 / G - 1) / (64 / G)), (unsigned)KVH, (unsigned)B);
+        // many query rows: tiled, key / value tiles shared by 64 query vectors; a call that
+        // continues a long cache (pos > 0) with too few query tiles to fill the GPU also splits
+        // the keys (at least 8 tiles each) and combines the splits in a second kernel
+        const int nqt = (seq + 64 / G - 1) / (64 / G), ctas = nqt * KVH * B;
+        int nsplit = 1;
+        if (pos > 0 && part_buf) {
+            const int want = (2 * device_sm_count() + ctas - 1) / ctas, most = (L + 8 * kFK - 1) / (8 * kFK);
+            nsplit = std::max(1, std::min(std::min(want, most), 64));
+            if ((size_t)ctas * nsplit * 64 * (hd + 2) > part_floats) nsplit = 1;
+        }
+        const dim3 grid((unsigned)(nqt * nsplit), (unsigned)KVH, (unsigned)B);
         if (hd == 128)
             attn_tiled_kernel<128><<<grid, kFThreads, 0, st>>>(sc.qr, mr->k, mr->v, d_mask, mrows, mcols, sc.ao, seq,
-                                                                H, KVH, max_seq, L, inv_scale);
+                                                                H, KVH, max_seq, L, inv_scale, nsplit, part_buf);
         else
             attn_tiled_kernel<64><<<grid, kFThreads, 0, st>>>(sc.qr, mr->k, mr->v, d_mask, mrows, mcols, sc.ao, seq, H,
-                                                               KVH, max_seq, L, inv_scale);
+                                                               KVH, max_seq, L, inv_scale, nsplit, part_buf);
+        if (nsplit > 1) {
+            VOXQ_CUDA_TRY(cudaGetLastError());
+            const int64_t threads = (int64_t)ctas * 64 * 32;
+            const int blocks = (int)((threads + 255) / 256);
+            if (hd == 128)
+                attn_combine_kernel<128><<<blocks, 256, 0, st>>>(part_buf, sc.ao, seq, H, KVH, B, nqt, nsplit);
+            else
+                attn_combine_kernel<64><<<blocks, 256, 0, st>>>(part_buf, sc.ao, seq, H, KVH, B, nqt, nsplit);
+        }
     } else {
         attn_kernel<<<dim3(seq, H, B), kAttnThreads, smem, st>>>(sc.qr, mr->k, mr->v, d_mask, mrows, mcols, sc.ao, seq,
                                                                 H, KVH, hd, max_seq, L, inv_scale);
@@ -766,6 +854,8 @@ void block_cache_clear() {
         if (bd.arena) cudaFree(bd.arena);
         if (bd.dit_arena) cudaFree(bd.dit_arena);
         if (bd.h_stage) cudaFreeHost(bd.h_stage);
+        if (bd.attn_part) cudaFree(bd.attn_part);
+        if (bd.mask_dev) cudaFree(bd.mask_dev);
         bd = BlockDev();
     }
 }
@@ -825,26 +915,60 @@ extern "C" VoxCPMError voxq_transformer_block_forward(const voxq_block_desc* blk
     Mirror* mr = nullptr;
     e = mirror_for(bd, cache_k, cache_v, B * KVH, max_seq, hd, pos, seq == max_seq, st, &mr);
     if (e) return e;
+    // key-split partials for a continuation of a long cache through the tiled attention
+    const bool graph_call = pos == 0 && seq == max_seq;
+    if (pos > 0) {
+        const int G = w.H / KVH;
+        if (seq * G >= 64 && 64 % G == 0 && (hd == 64 || hd == 128)) {
+            const size_t ctas = (size_t)((seq + 64 / G - 1) / (64 / G)) * KVH * B;
+            if (!grow(&bd.attn_part, &bd.attn_part_floats, (ctas + 2 * (size_t)device_sm_count()) * 64 * (hd + 2),
+                      false, st))
+                return VOXCPM_ERR_OOM;
+        }
+    }
+    // mask rows: outside graph calls, re-uploaded only when they differ from the last upload
+    const bool mask_cached = nm && !graph_call;
+    bool mask_upload = false;
+    if (mask_cached) {
+        bool same = bd.mask_dev && bd.mask_rows == mrows && bd.mask_cols == mcols;
+        for (int r = 0; same && r < mrows; r++)
+            same = memcmp(bd.mask_host.data() + (size_t)r * mcols, mask->data + (size_t)r * mask->shape[1],
+                          (size_t)mcols * sizeof(float)) == 0;
+        if (!same) {
+            if (!grow(&bd.mask_dev, &bd.mask_dev_floats, nm, false, st)) return VOXCPM_ERR_OOM;
+            bd.mask_host.resize(nm);
+            for (int r = 0; r < mrows; r++)
+                memcpy(bd.mask_host.data() + (size_t)r * mcols, mask->data + (size_t)r * mask->shape[1],
+                       (size_t)mcols * sizeof(float));
+            bd.mask_rows = mrows;
+            bd.mask_cols = mcols;
+            mask_upload = true;
+        }
+    }
 
     float* A = bd.arena;
     float *d_x = A, *d_o = A + off_o, *d_kn = A + off_kn, *d_vn = A + off_vn, *d_f = A + off_f, *d_m = A + off_m;
+    const float* d_mask = nm ? (mask_cached ? bd.mask_dev : d_m) : nullptr;
     const Scratch sc = scratch_at(A + off_s, M, w);
     float* hs = bd.h_stage;
     memcpy(hs, x->data, nx * sizeof(float));
     if (nf) memcpy(hs + al64(nx), freqs_cis->data + (size_t)pos * half * 2, nf * sizeof(float));
-    for (int r = 0; r < mrows; r++)
-        memcpy(hs + al64(nx) + al64(nf) + (size_t)r * mcols, mask->data + (size_t)r * mask->shape[1],
-               (size_t)mcols * sizeof(float));
+    if (mask_upload)
+        memcpy(hs + al64(nx) + al64(nf), bd.mask_host.data(), nm * sizeof(float));
+    else if (nm && !mask_cached)
+        for (int r = 0; r < mrows; r++)
+            memcpy(hs + al64(nx) + al64(nf) + (size_t)r * mcols, mask->data + (size_t)r * mask->shape[1],
+                   (size_t)mcols * sizeof(float));
     float* hd_out = hs + up_n;
     // everything from the upload to the downloads, on `st`
     auto enqueue = [&]() -> VoxCPMError {
         VOXQ_CUDA_TRY(cudaMemcpyAsync(d_x, hs, nx * sizeof(float), cudaMemcpyHostToDevice, st));
         if (nf) VOXQ_CUDA_TRY(cudaMemcpyAsync(d_f, hs + al64(nx), nf * sizeof(float), cudaMemcpyHostToDevice, st));
-        if (nm)
-            VOXQ_CUDA_TRY(cudaMemcpyAsync(d_m, hs + al64(nx) + al64(nf), nm * sizeof(float), cudaMemcpyHostToDevice,
-                                          st));
-        const VoxCPMError ce = block_core(w, sc, d_x, d_o, B, seq, mr, max_seq, pos, nm ? d_m : nullptr, mrows,
-                                          mcols, nf ? d_f : nullptr, d_kn, d_vn, st);
+        if (nm && (!mask_cached || mask_upload))
+            VOXQ_CUDA_TRY(cudaMemcpyAsync(mask_cached ? bd.mask_dev : d_m, hs + al64(nx) + al64(nf),
+                                          nm * sizeof(float), cudaMemcpyHostToDevice, st));
+        const VoxCPMError ce = block_core(w, sc, d_x, d_o, B, seq, mr, max_seq, pos, d_mask, mrows, mcols,
+                                          nf ? d_f : nullptr, d_kn, d_vn, st, bd.attn_part, bd.attn_part_floats);
         if (ce) return ce;
         // downloads: out, new cache rows (the caller waits once)
         VOXQ_CUDA_TRY(cudaMemcpyAsync(hd_out, d_o, nx * sizeof(float), cudaMemcpyDeviceToHost, st));
