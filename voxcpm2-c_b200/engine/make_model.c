@@ -366,7 +366,9 @@ static int write_file(const char* path, const SpecList* L, uint64_t seed, int th
         off += len + 1;
     }
     /* tensor data, generated in parallel per tensor */
+    if (L->n <= 0) { fprintf(stderr, "make_model: empty tensor list\n"); return -1; }
     uint8_t** bufs = (uint8_t**)calloc((size_t)L->n, sizeof(uint8_t*));
+    if (!bufs) { fprintf(stderr, "make_model: out of memory\n"); return -1; }
     for (int i = 0; i < L->n; i++) {
         bufs[i] = (uint8_t*)malloc(nbytes(&L->t[i]));
         if (!bufs[i]) { fprintf(stderr, "make_model: out of memory\n"); return -1; }
