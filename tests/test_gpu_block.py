@@ -21,6 +21,8 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -217,6 +219,115 @@ def test_block_on_device_matches_reference(qname):
         L.voxq_block_cache_clear()
         L.tensor_cuda_shutdown()
         os.environ.pop("VOXCPM_QUANT", None)
+
+
+def test_attention_at_the_engine_head_shape():
+    """The engine's attention shape (head_dim 128, 16 query heads over 2 kv
+    heads, so a CTA's 64 query vectors are 8 rows x 8 heads), through the
+    tensor-core attention (the default) or, in the child-process test below,
+    the CUDA-core kernel.  Calls of at most 8 rows project on the fp32 GEMV,
+    so they are held to the block's 1e-3 rule: an 8-row fill (exactly the 64
+    query vectors of one CTA) and an 8-row continuation of a 1024-row cache
+    (keys split over CTAs) whose mask hides the first 40 keys of every row (a
+    whole key tile with no visible key, then a partly visible one).  Larger
+    calls project on the fp16 tensor-core GEMM and take the library's GEMM
+    rule, 5e-3: a LocDiT-style fill of both CFG branches (B = 2, 201 rows, no
+    mask; repeated, so the second call is captured into a CUDA graph and the
+    third replays it), a causal prefill with RoPE, and a 64-row continuation
+    with the same hidden keys."""
+    L = voxq.lib()
+    os.environ["VOXCPM_QUANT"] = "q8"
+    L.tensor_cuda_shutdown()
+    assert L.tensor_cuda_init() == 0
+    rng = np.random.default_rng(29)
+    D, H, KVH, hd, F, eps = 256, 16, 2, 128, 256, 1e-6
+    W = {"wq": exact_weight(rng, H * hd, D, "q8"), "wk": exact_weight(rng, KVH * hd, D, "q8"),
+         "wv": exact_weight(rng, KVH * hd, D, "q8"), "wo": exact_weight(rng, D, H * hd, "q8"),
+         "w1": exact_weight(rng, F, D, "q8"), "w2": exact_weight(rng, D, F, "q8"),
+         "w3": exact_weight(rng, F, D, "q8"),
+         "n1": (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32),
+         "n2": (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32)}
+    keep = []
+    try:
+        T = {k: voxq.host_tensor(W[k]) for k in W}
+        keep += list(T.values())
+        for k in ("wq", "wk", "wv", "wo", "w1", "w2", "w3"):
+            voxq.check(L.tensor_to_cuda(T[k]), "tensor_to_cuda")
+        n1 = voxq.RmsNormDesc(T["n1"], eps)
+        n2 = voxq.RmsNormDesc(T["n2"], eps)
+        at = voxq.AttentionDesc(T["wq"], T["wk"], T["wv"], T["wo"], D, H, KVH, hd)
+        ff = voxq.SwigluDesc(T["w1"], T["w2"], T["w3"], D, F)
+        bd = voxq.BlockDesc(C.pointer(n1), C.pointer(at), C.pointer(n2), C.pointer(ff))
+        positions = 64
+        inv = 10000.0 ** (-np.arange(hd // 2) * 2.0 / hd)
+        ang = np.arange(positions)[:, None] * inv[None, :]
+        freqs_np = np.stack([np.cos(ang), np.sin(ang)], -1).astype(np.float32)
+        freqs = voxq.host_tensor(freqs_np)
+        keep.append(freqs)
+
+        def cache(B, max_seq):
+            ck = voxq.host_tensor(np.zeros((B, KVH, max_seq, hd), np.float32))
+            cv = voxq.host_tensor(np.zeros((B, KVH, max_seq, hd), np.float32))
+            keep.extend([ck, cv])
+            return ck, cv, np.zeros((B, KVH, max_seq, hd)), np.zeros((B, KVH, max_seq, hd))
+
+        def run(B, S, pos, c, mask_np, use_freqs, what, tol=TOL):
+            ck, cv, ref_ck, ref_cv = c
+            x_np = rng.standard_normal((B, S, D)).astype(np.float32)
+            x, out = voxq.host_tensor(x_np), voxq.host_tensor(np.zeros((B, S, D), np.float32))
+            mask = voxq.host_tensor(mask_np) if mask_np is not None else None
+            try:
+                r = L.voxq_transformer_block_forward(C.byref(bd), x, ck, cv, mask, freqs if use_freqs else None,
+                                                     pos, out)
+                assert r == 0, f"{what}: error {r}"
+                got = voxq.host_tensor_view(out)
+            finally:
+                for t_ in (x, out) + ((mask,) if mask is not None else ()):
+                    voxq.free_tensor(t_)
+            ref = block_ref(x_np, W, ref_ck, ref_cv, mask_np, freqs_np if use_freqs else None, pos, H, KVH, hd,
+                            eps)
+            close(got, ref, what, tol)
+            close(as_array(ck)[:, :, pos:pos + S], ref_ck[:, :, pos:pos + S], what + " (cache K rows)", tol)
+
+        gemm_tol = 5e-3  # more than 8 rows: projections on fp16 tensor cores
+        c = cache(1, 8)
+        run(1, 8, 0, c, None, False, "fill S=8 (64 query vectors)")
+        c = cache(2, 201)
+        for rep in range(3):
+            run(2, 201, 0, c, None, False, f"fill B=2 S=201 (call {rep + 1})", gemm_tol)
+        c = cache(1, 64)
+        run(1, 40, 0, c, causal(40, 40), True, "prefill S=40", gemm_tol)
+        c = cache(1, 1152)
+        for arr, ref in ((as_array(c[0]), c[2]), (as_array(c[1]), c[3])):
+            arr[:, :, :1024] = rng.standard_normal((1, KVH, 1024, hd)).astype(np.float32)
+            ref[:, :, :1024] = arr[:, :, :1024]
+        m = causal(8, 1032)
+        m[:, :40] = -np.inf
+        run(1, 8, 1024, c, m, False, "continuation S=8 at pos 1024, first 40 keys hidden (key splits)")
+        m = causal(64, 1096)
+        m[:, :40] = -np.inf
+        run(1, 64, 1032, c, m, False, "continuation S=64 at pos 1032, first 40 keys hidden (key splits)",
+            gemm_tol)
+        assert voxq.lib().voxq_device_error(1) == 0
+    finally:
+        for t_ in keep:
+            voxq.free_tensor(t_)
+        L.voxq_block_cache_clear()
+        L.tensor_cuda_shutdown()
+        os.environ.pop("VOXCPM_QUANT", None)
+
+
+def test_cuda_core_attention_in_child_process():
+    """VOXQ_ATTN_MMA=0 (read once per process) selects the CUDA-core tiled
+    attention kernel in place of the tensor-core one: the attention cases of
+    this file run again in a child process with it set."""
+    env = dict(os.environ, VOXQ_ATTN_MMA="0")
+    here = os.path.dirname(os.path.abspath(__file__))
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider",
+                        os.path.join(here, "test_gpu_block.py"), "-k", "matches_reference or engine_head_shape"],
+                       env=env, cwd=os.path.dirname(here), capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+    assert "5 passed" in r.stdout, r.stdout[-2000:]
 
 
 @pytest.mark.parametrize("qname", ["q8", "q4"])

@@ -297,6 +297,249 @@ __global__ void __launch_bounds__(kFThreads) attn_tiled_kernel(const float* __re
     for (int j = 0; j < DPT; j++) orow[part + 4 * j] = acc[j] * inv;
 }
 
+// ---------------------------------------------------------------------------
+// attn_tiled_kernel's function with both products on the tensor cores.
+//
+// Same grid, same 64 query vectors per CTA (the query rows of a CTA times the
+// G heads that read one kv head), same key tiles of kFK, same key splits and
+// partial records (so attn_combine_kernel merges them).  Four warps, each
+// owning 16 of the vectors as the M = 16 side of mma.sync m16n8k8 TF32 tiles:
+//
+//   S = Q K^T   (16 x 32 per warp per key tile: 4 n-blocks of 8 keys,
+//               HD / 8 k-steps over the head dims)
+//   online softmax on S in registers (the tiled kernel's m / l recurrence)
+//   O += P V    (16 x HD per warp: HD / 8 n-blocks, 4 k-steps of 8 keys)
+//
+// Every operand is split into a TF32 high part and a TF32 low part (the
+// rounding remainder), and each product is a_lo b_hi + a_hi b_lo + a_hi b_hi
+// accumulated in fp32: the dropped a_lo b_lo term is ~2^-22 relative, so the
+// result matches the fp32 CUDA-core kernel to within fp32 rounding.
+//
+// The P operand comes straight from the S accumulators: a lane holds keys
+// 2t and 2t + 1 of each 8-key block (C layout), while the A operand wants
+// columns t and t + 4; reading the block's keys in the order
+// (0, 2, 4, 6, 1, 3, 5, 7) -- A column t is key 2t, column t + 4 is key
+// 2t + 1 -- makes the two layouts coincide, and the V operand is read in the
+// same key order.  Shared-memory rows have a pitch of HD + 4 floats, which
+// puts the 32 lanes of every fragment load in 32 different banks.
+constexpr int kMThreads = 128;
+constexpr int kMPitchPad = 4;
+
+__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hi) : "f"(x));
+    const float r = x - __uint_as_float(hi);
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lo) : "f"(r));
+}
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// d += a b with both operands split (three TF32 products, small ones first).
+__device__ __forceinline__ void mma_tf32x3(float (&d)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
+                                           uint32_t bh0, uint32_t bh1, uint32_t bl0, uint32_t bl1) {
+    mma_tf32(d, al, bh0, bh1);
+    mma_tf32(d, ah, bl0, bl1);
+    mma_tf32(d, ah, bh0, bh1);
+}
+
+template <int HD>
+constexpr int attn_mma_smem_bytes() {
+    return (64 + 2 * kFK) * (HD + kMPitchPad) * (int)sizeof(float);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kMThreads) attn_mma_kernel(const float* __restrict__ q, const float* __restrict__ ck,
+                                                             const float* __restrict__ cv,
+                                                             const float* __restrict__ mask, int mrows, int mcols,
+                                                             float* __restrict__ out, int seq, int H, int KVH,
+                                                             int max_seq, int L, float inv_scale, int nsplit,
+                                                             float* __restrict__ partial) {
+    constexpr int P = HD + kMPitchPad;  // shared row pitch (floats)
+    constexpr int NB = HD / 8;          // 8-wide blocks of the head dims
+    extern __shared__ __align__(16) float asm_sh[];
+    float* Qs = asm_sh;          // [64][P]   the CTA's query vectors
+    float* Ks = Qs + 64 * P;     // [kFK][P]  key tile
+    float* Vs = Ks + kFK * P;    // [kFK][P]  value tile
+    const int G = H / KVH, QR = 64 / G;
+    const int kh = blockIdx.y, b = blockIdx.z;
+    const int qt = blockIdx.x / nsplit, sp = blockIdx.x % nsplit;
+    const int ntiles = (L + kFK - 1) / kFK, tps = (ntiles + nsplit - 1) / nsplit;
+    const int t_beg = sp * tps * kFK, t_end = min(L, (sp + 1) * tps * kFK);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+
+    // the 64 query vectors (zeros past the sequence)
+    for (int i = threadIdx.x; i < 64 * HD / 4; i += kMThreads) {
+        const int r = (i * 4) / HD, col = (i * 4) % HD;
+        const int h = kh * G + r % G, s = qt * QR + r / G;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (s < seq) v = *reinterpret_cast<const float4*>(q + (((int64_t)b * H + h) * seq + s) * HD + col);
+        *reinterpret_cast<float4*>(Qs + r * P + col) = v;
+    }
+
+    // this lane's two query vectors (MMA rows g and g + 8 of the warp's 16)
+    const int r0 = warp * 16 + g, r1 = r0 + 8;
+    const int s0 = qt * QR + r0 / G, s1 = qt * QR + r1 / G;
+    float o[NB][4];
+#pragma unroll
+    for (int j = 0; j < NB; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // l: this lane's share of the row sums
+    const float* kb = ck + ((int64_t)b * KVH + kh) * max_seq * HD;
+    const float* vb = cv + ((int64_t)b * KVH + kh) * max_seq * HD;
+    const float* qa = Qs + r0 * P + t;
+    const float* qb = Qs + r1 * P + t;
+
+    for (int t0 = t_beg; t0 < t_end; t0 += kFK) {
+        __syncthreads();  // the previous tile is consumed (and, at first, Qs is written)
+        const int nt = min(kFK, t_end - t0);
+        for (int i = threadIdx.x; i < kFK * HD / 4; i += kMThreads) {
+            const int row = (i * 4) / HD, col = (i * 4) % HD;
+            float4 kk = make_float4(0.f, 0.f, 0.f, 0.f), vv = kk;
+            if (row < nt) {
+                kk = *reinterpret_cast<const float4*>(kb + (int64_t)(t0 + row) * HD + col);
+                vv = *reinterpret_cast<const float4*>(vb + (int64_t)(t0 + row) * HD + col);
+            }
+            *reinterpret_cast<float4*>(Ks + row * P + col) = kk;
+            *reinterpret_cast<float4*>(Vs + row * P + col) = vv;
+        }
+        __syncthreads();
+
+        // S = Q K^T for the tile's 4 blocks of 8 keys
+        float sc[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+#pragma unroll 4
+        for (int kk = 0; kk < NB; kk++) {
+            uint32_t ah[4], al[4];
+            tf32_split(qa[kk * 8], ah[0], al[0]);
+            tf32_split(qb[kk * 8], ah[1], al[1]);
+            tf32_split(qa[kk * 8 + 4], ah[2], al[2]);
+            tf32_split(qb[kk * 8 + 4], ah[3], al[3]);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float* kr = Ks + (j * 8 + g) * P + kk * 8 + t;
+                uint32_t bh0, bl0, bh1, bl1;
+                tf32_split(kr[0], bh0, bl0);
+                tf32_split(kr[4], bh1, bl1);
+                mma_tf32x3(sc[j], ah, al, bh0, bh1, bl0, bl1);
+            }
+        }
+
+        // scale, mask, keys past the tile's end; row maxima over the quad
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const int key = j * 8 + 2 * t + (c & 1), tk = t0 + key;
+                const int srow = c < 2 ? s0 : s1;
+                float v = sc[j][c] * inv_scale;
+                if (mask && srow < mrows && tk < mcols) v += mask[(int64_t)srow * mcols + tk];
+                if (key >= nt) v = -INFINITY;
+                sc[j][c] = v;
+                if (c < 2)
+                    mx0 = fmaxf(mx0, v);
+                else
+                    mx1 = fmaxf(mx1, v);
+            }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        // a row whose keys so far are all masked keeps zero weights (and m = -inf)
+        const bool live0 = mn0 != -INFINITY, live1 = mn1 != -INFINITY;
+        const float f0 = live0 ? expf(m0 - mn0) : 1.0f, f1 = live1 ? expf(m1 - mn1) : 1.0f;
+        float ps0 = 0.0f, ps1 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const bool r1c = c >= 2;
+                const float p = (r1c ? live1 : live0) ? expf(sc[j][c] - (r1c ? mn1 : mn0)) : 0.0f;
+                sc[j][c] = p;
+                if (r1c)
+                    ps1 += p;
+                else
+                    ps0 += p;
+            }
+        l0 = fmaf(l0, f0, ps0);
+        l1 = fmaf(l1, f1, ps1);
+        m0 = live0 ? mn0 : m0;
+        m1 = live1 ? mn1 : m1;
+#pragma unroll
+        for (int j = 0; j < NB; j++) {
+            o[j][0] *= f0;
+            o[j][1] *= f0;
+            o[j][2] *= f1;
+            o[j][3] *= f1;
+        }
+
+        // O += P V, keys of block j read in the order (0, 2, 4, 6, 1, 3, 5, 7)
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            uint32_t ah[4], al[4];
+            tf32_split(sc[j][0], ah[0], al[0]);  // row g,     key 2t
+            tf32_split(sc[j][2], ah[1], al[1]);  // row g + 8, key 2t
+            tf32_split(sc[j][1], ah[2], al[2]);  // row g,     key 2t + 1
+            tf32_split(sc[j][3], ah[3], al[3]);  // row g + 8, key 2t + 1
+            const float* v0 = Vs + (j * 8 + 2 * t) * P + g;
+            const float* v1 = v0 + P;
+#pragma unroll
+            for (int n = 0; n < NB; n++) {
+                uint32_t bh0, bl0, bh1, bl1;
+                tf32_split(v0[n * 8], bh0, bl0);
+                tf32_split(v1[n * 8], bh1, bl1);
+                mma_tf32x3(o[n], ah, al, bh0, bh1, bl0, bl1);
+            }
+        }
+    }
+
+    // the row sums over the quad
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    if (nsplit > 1) {
+        // this split's running max, sum and unnormalised accumulator, combined by attn_combine_kernel
+        const int nqt = gridDim.x / nsplit;
+        float* rec = partial + ((((int64_t)b * KVH + kh) * nqt + qt) * nsplit + sp) * 64 * (HD + 2);
+        float* ra = rec + (int64_t)r0 * (HD + 2);
+        float* rb = rec + (int64_t)r1 * (HD + 2);
+        if (t == 0) {
+            ra[0] = m0;
+            ra[1] = l0;
+            rb[0] = m1;
+            rb[1] = l1;
+        }
+#pragma unroll
+        for (int n = 0; n < NB; n++) {
+            ra[2 + n * 8 + 2 * t] = o[n][0];
+            ra[3 + n * 8 + 2 * t] = o[n][1];
+            rb[2 + n * 8 + 2 * t] = o[n][2];
+            rb[3 + n * 8 + 2 * t] = o[n][3];
+        }
+        return;
+    }
+    const float inv0 = 1.0f / (l0 + 1e-10f), inv1 = 1.0f / (l1 + 1e-10f);
+    if (s0 < seq) {
+        float* orow = out + (((int64_t)b * seq + s0) * H + kh * G + r0 % G) * HD + 2 * t;
+#pragma unroll
+        for (int n = 0; n < NB; n++)
+            *reinterpret_cast<float2*>(orow + n * 8) = make_float2(o[n][0] * inv0, o[n][1] * inv0);
+    }
+    if (s1 < seq) {
+        float* orow = out + (((int64_t)b * seq + s1) * H + kh * G + r1 % G) * HD + 2 * t;
+#pragma unroll
+        for (int n = 0; n < NB; n++)
+            *reinterpret_cast<float2*>(orow + n * 8) = make_float2(o[n][2] * inv1, o[n][3] * inv1);
+    }
+}
+
 // Combines the key splits of attn_tiled_kernel: one warp per query vector,
 // M = max m_sp, l = sum l_sp e^(m_sp - M), acc = sum acc_sp e^(m_sp - M),
 // out = acc / (l + 1e-10) -- the single pass's result up to fp32 rounding;
@@ -669,6 +912,35 @@ VoxCPMError mirror_for(BlockDev& bd, Tensor* ck, Tensor* cv, int BK, int max_seq
 
 bool is_host_f32(const Tensor* t) { return t && t->data && !t->is_cuda && !t->is_fp16; }
 
+// Tensor-core attention for many query rows (attn_mma_kernel) unless
+// VOXQ_ATTN_MMA=0 selects the CUDA-core kernel (attn_tiled_kernel).
+bool attn_mma_enabled() {
+    static const bool v = [] {
+        const char* e = getenv("VOXQ_ATTN_MMA");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
+// attn_mma_kernel needs more than the default 48 KB of dynamic shared memory
+// (68 KB at head_dim 128); the opt-in is a per-device function attribute.
+cudaError_t attn_mma_prepare() {
+    static std::mutex mu;
+    static bool done[16] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev >= 0 && dev < 16 && done[dev]) return cudaSuccess;
+    e = cudaFuncSetAttribute(attn_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             attn_mma_smem_bytes<128>());
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 attn_mma_smem_bytes<64>());
+    if (e == cudaSuccess && dev >= 0 && dev < 16) done[dev] = true;
+    return e;
+}
+
 VoxCPMError project(const float* a, int M, int K, const voxq_qweight& w, float* out, const float* residual,
                     const voxq_qweight* up, cudaStream_t st) {
     voxq_epilogue epi = {nullptr, residual, w.N, up};
@@ -807,12 +1079,24 @@ VoxCPMError block_core(const BlockW& w, const Scratch& sc, const float* d_x, flo
             if ((size_t)ctas * nsplit * 64 * (hd + 2) > part_floats) nsplit = 1;
         }
         const dim3 grid((unsigned)(nqt * nsplit), (unsigned)KVH, (unsigned)B);
-        if (hd == 128)
+        if (attn_mma_enabled()) {
+            // both products on the tensor cores (split TF32), same grid and partial records
+            VOXQ_CUDA_TRY(attn_mma_prepare());
+            if (hd == 128)
+                attn_mma_kernel<128><<<grid, kMThreads, attn_mma_smem_bytes<128>(), st>>>(
+                    sc.qr, mr->k, mr->v, d_mask, mrows, mcols, sc.ao, seq, H, KVH, max_seq, L, inv_scale, nsplit,
+                    part_buf);
+            else
+                attn_mma_kernel<64><<<grid, kMThreads, attn_mma_smem_bytes<64>(), st>>>(
+                    sc.qr, mr->k, mr->v, d_mask, mrows, mcols, sc.ao, seq, H, KVH, max_seq, L, inv_scale, nsplit,
+                    part_buf);
+        } else if (hd == 128) {
             attn_tiled_kernel<128><<<grid, kFThreads, 0, st>>>(sc.qr, mr->k, mr->v, d_mask, mrows, mcols, sc.ao, seq,
                                                                 H, KVH, max_seq, L, inv_scale, nsplit, part_buf);
-        else
+        } else {
             attn_tiled_kernel<64><<<grid, kFThreads, 0, st>>>(sc.qr, mr->k, mr->v, d_mask, mrows, mcols, sc.ao, seq, H,
                                                                KVH, max_seq, L, inv_scale, nsplit, part_buf);
+        }
         if (nsplit > 1) {
             VOXQ_CUDA_TRY(cudaGetLastError());
             const int64_t threads = (int64_t)ctas * 64 * 32;
