@@ -1081,6 +1081,63 @@ def run_c4(args):
     print(json.dumps(line), flush=True)
 
 
+def run_attn(args):
+    """One transformer-block call (voxq_transformer_block_forward) at the LocDiT's shape at the
+    last patch of the full C4 run: both CFG branches, 801 rows (5 + 4 x 199), hidden 1024, 16
+    query heads over 2 kv heads of 128, FFN 4096, Q8 weights, a fresh cache filled whole.  The
+    median wall time per call (upload, block, download) with the attention kernel that
+    VOXQ_ATTN_MMA selects (unset or 1: tensor cores, 0: CUDA cores); everything else in the call
+    is the same, so two runs, one per setting, differ by the attention alone."""
+    import ctypes as C
+    import numpy as np
+    sys.path.insert(0, os.path.join(REPO, "voxcpm2-c_b200"))
+    import voxq
+    os.environ["VOXCPM_QUANT"] = "q8"
+    L = voxq.lib()
+    voxq.check(L.tensor_cuda_init(), "tensor_cuda_init")
+    B, S, D, H, KVH, hd, F = 2, 801, 1024, 16, 2, 128, 4096
+    rng = np.random.default_rng(5)
+
+    def w(n, k):
+        return (0.02 * rng.standard_normal((n, k))).astype(np.float32)
+
+    W = {"wq": w(H * hd, D), "wk": w(KVH * hd, D), "wv": w(KVH * hd, D), "wo": w(D, H * hd), "w1": w(F, D),
+         "w2": w(D, F), "w3": w(F, D), "n1": np.ones(D, np.float32), "n2": np.ones(D, np.float32)}
+    T = {k: voxq.host_tensor(v) for k, v in W.items()}
+    for k in ("wq", "wk", "wv", "wo", "w1", "w2", "w3"):
+        voxq.check(L.tensor_to_cuda(T[k]), "tensor_to_cuda")
+    n1, n2 = voxq.RmsNormDesc(T["n1"], 1e-6), voxq.RmsNormDesc(T["n2"], 1e-6)
+    at = voxq.AttentionDesc(T["wq"], T["wk"], T["wv"], T["wo"], D, H, KVH, hd)
+    ff = voxq.SwigluDesc(T["w1"], T["w2"], T["w3"], D, F)
+    bd = voxq.BlockDesc(C.pointer(n1), C.pointer(at), C.pointer(n2), C.pointer(ff))
+    x = voxq.host_tensor(rng.standard_normal((B, S, D)).astype(np.float32))
+    out = voxq.host_tensor(np.zeros((B, S, D), np.float32))
+    ck = voxq.host_tensor(np.zeros((B, KVH, S, hd), np.float32))
+    cv = voxq.host_tensor(np.zeros((B, KVH, S, hd), np.float32))
+
+    def call():
+        voxq.check(L.voxq_transformer_block_forward(C.byref(bd), x, ck, cv, None, None, 0, out), "block")
+
+    for _ in range(args.warmup):
+        call()
+    times = []
+    for _ in range(max(1, min(args.steps, 200))):
+        t0 = time.perf_counter()
+        call()
+        times.append(time.perf_counter() - t0)
+    mma = os.environ.get("VOXQ_ATTN_MMA", "1")[:1] != "0"
+    line = {"metric": "block_call_ms", "value": round(float(np.median(times)) * 1e3, 4), "unit": "ms",
+            "higher_is_better": False, "steps": len(times), "warmup": args.warmup,
+            "attention": "tensor cores (split TF32 mma.sync)" if mma else "CUDA cores (fp32 FMA)",
+            "config": {"workload": "one transformer block, LocDiT shape at the last of 200 patches: B=2 (CFG), "
+                                   "S=801, hidden 1024, heads 16/2 x 128, FFN 4096, Q8, fresh cache filled whole",
+                       "attention_flops": 2 * 2 * B * H * S * S * hd},
+            "min_ms": round(min(times) * 1e3, 4)}
+    print(json.dumps(line), flush=True)
+    L.voxq_block_cache_clear()
+    L.tensor_cuda_shutdown()
+
+
 def measure_sharded_c3(torch, voxq, dist, dev, st, rank, world, steps, warmup):
     """Config-3 GEMM column shards (no collective): rank r owns weight rows
     [r*N/G, (r+1)*N/G), quantized on its own GPU, and writes its column slice of
@@ -1150,9 +1207,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-tensor-abi", dest="tensor_abi", action="store_false")
     ap.add_argument("--shape", default="", help="c3 only: one shape 'M,N,q8|q4'")
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4"],
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "attn"],
                     help="c2: the headline decode step (default); c1: one Q8 GEMV; c3: GEMM sweep, one line per "
-                         "shape; c4: the unchanged engine's RTF")
+                         "shape; c4: the unchanged engine's RTF; attn: one transformer-block call at the LocDiT's "
+                         "200-patch shape (VOXQ_ATTN_MMA picks the attention kernel)")
     ap.add_argument("--c4-patches", type=int, default=4)
     ap.add_argument("--c4-cpu-patches", type=int, default=0, help="c4: also time the CPU engine on this many patches")
     ap.add_argument("--no-configs", dest="configs", action="store_false",
@@ -1169,6 +1227,9 @@ def main():
         return
     if args.config == "c4":
         run_c4(args)
+        return
+    if args.config == "attn":
+        run_attn(args)
         return
 
     rank = int(os.environ.get("RANK", "0"))

@@ -9,7 +9,8 @@
 //   n   = RMSNorm(x)                      rmsnorm_kernel
 //   q, k, v = n Wq^T, n Wk^T, n Wv^T      one grouped GEMV launch (M <= 8) or three GEMMs
 //   RoPE(q, k); k, v -> cache[pos ..]     rope_cache_kernel
-//   a   = softmax(q k^T / sqrt(d) + mask) v   attn_kernel (one CTA per query row and head)
+//   a   = softmax(q k^T / sqrt(d) + mask) v   attn_kernel (one CTA per query row and head), or
+//                                         for many query rows attn_mma_kernel (tensor cores)
 //   h   = x + a Wo^T                      projection with the residual epilogue
 //   n2  = RMSNorm(h)
 //   g   = silu(n2 W1^T) * (n2 W3^T)       projection with the SwiGLU epilogue
