@@ -325,6 +325,7 @@ __global__ void __launch_bounds__(kFThreads) attn_tiled_kernel(const float* __re
 // puts the 32 lanes of every fragment load in 32 different banks.
 constexpr int kMThreads = 128;
 constexpr int kMPitchPad = 4;
+constexpr int kMPvGroup = 8;  // head-dim blocks whose P V products are interleaved
 
 __device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hi) : "f"(x));
@@ -339,12 +340,20 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// d += a b with both operands split (three TF32 products, small ones first).
-__device__ __forceinline__ void mma_tf32x3(float (&d)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
-                                           uint32_t bh0, uint32_t bh1, uint32_t bl0, uint32_t bl1) {
-    mma_tf32(d, al, bh0, bh1);
-    mma_tf32(d, ah, bl0, bl1);
-    mma_tf32(d, ah, bh0, bh1);
+// d[i] += a b[i] for NG accumulators with both operands split: three TF32
+// products per accumulator, small ones first (a_lo b_hi, a_hi b_lo, a_hi b_hi).
+// Each product is issued for all NG accumulators before the next one, so
+// consecutive MMAs are independent and overlap in the pipe; every accumulator
+// still receives its three products in the same order.
+template <int NG>
+__device__ __forceinline__ void mma_tf32x3_group(float (*d)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
+                                                 const uint32_t (&bh)[NG][2], const uint32_t (&bl)[NG][2]) {
+#pragma unroll
+    for (int i = 0; i < NG; i++) mma_tf32(d[i], al, bh[i][0], bh[i][1]);
+#pragma unroll
+    for (int i = 0; i < NG; i++) mma_tf32(d[i], ah, bl[i][0], bl[i][1]);
+#pragma unroll
+    for (int i = 0; i < NG; i++) mma_tf32(d[i], ah, bh[i][0], bh[i][1]);
 }
 
 template <int HD>
@@ -420,14 +429,14 @@ __global__ void __launch_bounds__(kMThreads) attn_mma_kernel(const float* __rest
             tf32_split(qb[kk * 8], ah[1], al[1]);
             tf32_split(qa[kk * 8 + 4], ah[2], al[2]);
             tf32_split(qb[kk * 8 + 4], ah[3], al[3]);
+            uint32_t bh[4][2], bl[4][2];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 const float* kr = Ks + (j * 8 + g) * P + kk * 8 + t;
-                uint32_t bh0, bl0, bh1, bl1;
-                tf32_split(kr[0], bh0, bl0);
-                tf32_split(kr[4], bh1, bl1);
-                mma_tf32x3(sc[j], ah, al, bh0, bh1, bl0, bl1);
+                tf32_split(kr[0], bh[j][0], bl[j][0]);
+                tf32_split(kr[4], bh[j][1], bl[j][1]);
             }
+            mma_tf32x3_group<4>(sc, ah, al, bh, bl);
         }
 
         // scale, mask, keys past the tile's end; row maxima over the quad
@@ -490,12 +499,16 @@ __global__ void __launch_bounds__(kMThreads) attn_mma_kernel(const float* __rest
             tf32_split(sc[j][3], ah[3], al[3]);  // row g + 8, key 2t + 1
             const float* v0 = Vs + (j * 8 + 2 * t) * P + g;
             const float* v1 = v0 + P;
+            constexpr int NG = kMPvGroup < NB ? kMPvGroup : NB;
 #pragma unroll
-            for (int n = 0; n < NB; n++) {
-                uint32_t bh0, bl0, bh1, bl1;
-                tf32_split(v0[n * 8], bh0, bl0);
-                tf32_split(v1[n * 8], bh1, bl1);
-                mma_tf32x3(o[n], ah, al, bh0, bh1, bl0, bl1);
+            for (int n0 = 0; n0 < NB; n0 += NG) {
+                uint32_t bh[NG][2], bl[NG][2];
+#pragma unroll
+                for (int i = 0; i < NG; i++) {
+                    tf32_split(v0[(n0 + i) * 8], bh[i][0], bl[i][0]);
+                    tf32_split(v1[(n0 + i) * 8], bh[i][1], bl[i][1]);
+                }
+                mma_tf32x3_group<NG>(o + n0, ah, al, bh, bl);
             }
         }
     }
