@@ -85,3 +85,24 @@ def test_no_worker_up_raises(tmp_path):
     with pytest.raises(RuntimeError, match="no serving worker"):
         S.serve(FAKE, S.workload(2, patches=1), gpus=[0], workers_per_gpu=1,
                 env=dict(os.environ, FAKE_NO_READY="1"), deadline_s=2, ready_timeout_s=10)
+
+
+def test_workers_follow_the_callers_visible_devices(tmp_path):
+    """A caller that itself sees only some GPUs (CUDA_VISIBLE_DEVICES=6,3) numbers them 0 and 1;
+    its worker for GPU 1 must be pinned to physical GPU 3, not 1: here the worker on "3" never
+    loads, so worker 1 is the dead one and GPU 0 ("6") answers everything."""
+    assert S.visible_device(1, {"CUDA_VISIBLE_DEVICES": "6,3"}) == "3"
+    assert S.visible_device(0, {"CUDA_VISIBLE_DEVICES": "GPU-aa, GPU-bb"}) == "GPU-aa"
+    assert S.visible_device(2, {"CUDA_VISIBLE_DEVICES": "6,3"}) == "2"
+    assert S.visible_device(1, {}) == "1"
+    wrapper = tmp_path / "w.py"
+    wrapper.write_text(
+        "import os, runpy, sys\n"
+        "if os.environ.get('CUDA_VISIBLE_DEVICES') == '3': os.environ['FAKE_NO_READY'] = '1'\n"
+        f"sys.argv = [{FAKE[1]!r}]\n"
+        f"runpy.run_path({FAKE[1]!r}, run_name='__main__')\n")
+    utts = S.workload(4, patches=1, seed=4)
+    r = S.serve([sys.executable, str(wrapper)], utts, gpus=[0, 1], workers_per_gpu=1,
+                env=dict(os.environ, CUDA_VISIBLE_DEVICES="6,3"), deadline_s=5, ready_timeout_s=30)
+    assert r["dead_workers"] == [1]
+    assert r["answered"] == 4 and all(x["gpu"] == 0 for x in r["results"])

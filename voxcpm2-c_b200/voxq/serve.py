@@ -108,11 +108,20 @@ class _Worker:
             pass
 
 
+def visible_device(g: int, env: dict) -> str:
+    """The ``CUDA_VISIBLE_DEVICES`` value that pins a worker to GPU ``g`` as the calling process
+    numbers its GPUs: the g-th entry of the caller's own ``CUDA_VISIBLE_DEVICES`` when that is set
+    (an index or a UUID), else ``g`` itself (also for an index past the caller's list)."""
+    ids = [x.strip() for x in env.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip()]
+    return ids[g] if 0 <= g < len(ids) else str(g)
+
+
 def serve(cmd: Sequence[str], utterances: Sequence[dict], gpus: Sequence[int], workers_per_gpu: int = 1,
           env: Optional[dict] = None, deadline_s: float = 120.0, ready_timeout_s: float = 900.0) -> dict:
     """Runs ``utterances`` (dicts from ``workload``) on ``len(gpus) * workers_per_gpu`` workers of
     ``cmd`` and returns the per-utterance answers and the throughput.  Throughput is measured from
-    the moment the requests are written (every worker loaded) to the last answer."""
+    the moment the requests are written (every worker loaded) to the last answer.  ``gpus`` are
+    indices as this process sees its GPUs (``visible_device``)."""
     if not gpus or workers_per_gpu < 1:
         raise ValueError("need at least one GPU and one worker per GPU")
     by_index = {u["index"]: u for u in utterances}
@@ -122,7 +131,7 @@ def serve(cmd: Sequence[str], utterances: Sequence[dict], gpus: Sequence[int], w
     workers: List[_Worker] = []
     for g in gpus:
         for _ in range(workers_per_gpu):
-            e = dict(base_env, CUDA_VISIBLE_DEVICES=str(g))
+            e = dict(base_env, CUDA_VISIBLE_DEVICES=visible_device(g, base_env))
             workers.append(_Worker(len(workers), g, cmd, e, events))
     results: Dict[int, dict] = {}
     errors: List[dict] = []
@@ -254,4 +263,4 @@ def serve(cmd: Sequence[str], utterances: Sequence[dict], gpus: Sequence[int], w
     }
 
 
-__all__ = ["workload", "cost", "serve", "VOCAB"]
+__all__ = ["workload", "cost", "serve", "visible_device", "VOCAB"]
