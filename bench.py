@@ -512,6 +512,16 @@ def run_c1(args, torch):
     print(json.dumps(measure_c1(torch, voxq, dev, torch.cuda.Stream(dev), args.steps, args.warmup)), flush=True)
 
 
+def run_chain(args, torch):
+    """The dependent C2 decode step alone (configs.c2_chain of the default line)."""
+    import voxq
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    r = measure_c2_chain(torch, voxq, dev, torch.cuda.Stream(dev), voxq.Q4, max(20, args.steps // 20),
+                         args.warmup)
+    print(json.dumps(r), flush=True)
+
+
 C3_M = (16, 64, 256, 2048)
 C3_N = (1024, 4096)
 
@@ -1207,10 +1217,11 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-tensor-abi", dest="tensor_abi", action="store_false")
     ap.add_argument("--shape", default="", help="c3 only: one shape 'M,N,q8|q4'")
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "attn"],
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "attn", "chain"],
                     help="c2: the headline decode step (default); c1: one Q8 GEMV; c3: GEMM sweep, one line per "
                          "shape; c4: the unchanged engine's RTF; attn: one transformer-block call at the LocDiT's "
-                         "200-patch shape (VOXQ_ATTN_MMA picks the attention kernel)")
+                         "200-patch shape (VOXQ_ATTN_MMA picks the attention kernel); chain: the dependent C2 "
+                         "decode step alone")
     ap.add_argument("--c4-patches", type=int, default=4)
     ap.add_argument("--c4-cpu-patches", type=int, default=0, help="c4: also time the CPU engine on this many patches")
     ap.add_argument("--no-configs", dest="configs", action="store_false",
@@ -1221,9 +1232,9 @@ def main():
     if args.ref_gpu_worker:
         ref_gpu_worker(args)
         return
-    if args.config in ("c1", "c3"):
+    if args.config in ("c1", "c3", "chain"):
         import torch
-        (run_c1 if args.config == "c1" else run_c3)(args, torch)
+        {"c1": run_c1, "c3": run_c3, "chain": run_chain}[args.config](args, torch)
         return
     if args.config == "c4":
         run_c4(args)
