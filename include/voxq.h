@@ -124,7 +124,11 @@ VOXQ_API const char* voxq_version(void);
 
 /* Selects the CUDA device for the calling thread's later calls (multi-GPU
  * runners use one host thread or process per GPU).  No counterpart in the
- * reference, which hard-codes device 0 (src/tensor_cuda.cu:50). */
+ * reference, which hard-codes device 0 (src/tensor_cuda.cu:50).  Limitation:
+ * the kernels that need more than 48 KB of shared memory get their opt-in on
+ * the first device that launches them in a process, so one process drives one
+ * GPU (a launch on a second device returns VOXCPM_ERR_INTERNAL); run one
+ * process per GPU, as bench.py and the serving workers do. */
 VOXQ_API VoxCPMError voxq_set_device(int device);
 
 /* Device-side status of the current device's kernels: 0, or the code of the
