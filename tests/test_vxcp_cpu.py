@@ -112,6 +112,34 @@ def test_loader_sizes_and_rejects_q4_0(tmp_path):
     assert got["b.f32"]["offset"] == got["a.q40"]["offset"] + 36
 
 
+@pytest.mark.skipif(not os.path.exists(CHECK), reason="engine harness not built (needs the reference checkout)")
+def test_loader_rejects_corrupt_shapes(tmp_path):
+    """Malformed index entries end in VOXCPM_ERR_INVALID_MODEL (-2), never in a read outside
+    the file or the entry: a shape whose value count would wrap 64 bits (the index is refused),
+    and an ndim of 0 (sized by the index as one value, src/model.c:1715-1719) whose shape[0]
+    names 1000 values (the load of that tensor is refused; the engine's loader would read them)."""
+    import struct
+    a = np.arange(1000, dtype=np.float32)
+    base = str(tmp_path / "ok.vxcpm")
+    vxcp.write(base, [("a.f32", vxcp.FP32, (1000,), a.tobytes()), ("b.f32", vxcp.FP32, (8,), a[:8].tobytes())])
+    raw = bytearray(open(base, "rb").read())
+    wrap = bytearray(raw)
+    struct.pack_into("<5I", wrap, 64 + 12, 4, 0xFFFFFFFF, 0xFFFFFFFF, 0xFFFFFFFF, 0xFFFFFFFF)
+    p = tmp_path / "wrap.vxcpm"
+    p.write_bytes(bytes(wrap))
+    r = subprocess.run([CHECK, str(p)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and json.loads(r.stdout.strip().splitlines()[-1]) == {"tensors": 0, "status": -2}
+    assert "impossible shape" in r.stderr
+    flat = bytearray(raw)
+    struct.pack_into("<I", flat, 64 + 12, 0)  # a.f32: ndim 0, shape[0] still 1000
+    p = tmp_path / "ndim0.vxcpm"
+    p.write_bytes(bytes(flat))
+    r = subprocess.run([CHECK, str(p)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
+    got = {x["name"]: x for x in map(json.loads, r.stdout.strip().splitlines()[:-1])}
+    assert got["a.f32"]["bytes"] == 4 and got["a.f32"]["load"] == -2
+
+
 def test_writer_checksums_and_block_order(tmp_path):
     """The writer's header / data CRC32C and the VXCP <-> quantize.py block order round trip."""
     rng = np.random.default_rng(3)

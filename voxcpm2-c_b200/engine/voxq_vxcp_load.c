@@ -15,7 +15,8 @@
  *     from the byte after the string table's last NUL, entries sorted by name
  *     for weight_index_find's binary search (src/model.c:1733, 1773-1786);
  *     header CRC32C checked and a mismatch only reported, as the engine does;
- *     bounds checked against the mapping (the engine does not);
+ *     bounds checked against the mapping and shapes against the file size
+ *     (the engine does neither), and a load never reads past its entry;
  *   - fp32 / fp16 / bf16 tensors load exactly as the engine loads them
  *     (src/model.c:1811-1858: fp16 kept as fp16 except 1-D, bf16 widened,
  *     NaN set to 0 in fp32 data);
@@ -160,10 +161,21 @@ WeightIndex* weight_index_build(const uint8_t* data, size_t data_size) {
         idx->count++;
         e->dtype = ql_rd32(m + 8);
         e->ndim = ql_rd32(m + 12);
+        /* no tensor inside the file holds more values than twice its bytes (the
+         * smallest encoding, Q4_0, takes 18 bytes per 32 values): a shape past
+         * that is corrupt, and checking before each product keeps n from wrapping */
+        const uint64_t cap = 2 * (uint64_t)data_size;
         uint64_t n = 1;
         for (int d = 0; d < 4; d++) {
             e->shape[d] = ql_rd32(m + 16 + 4 * d);
-            if (d < (int)e->ndim) n *= e->shape[d];
+            if (d < (int)e->ndim) {
+                const uint64_t s = e->shape[d];
+                if (s && n > cap / s) {
+                    fprintf(stderr, "[voxq loader] tensor '%s' has an impossible shape\n", e->name);
+                    goto fail;
+                }
+                n *= s;
+            }
         }
         int ok;
         /* an unknown dtype is sized as fp32, as the engine does */
@@ -219,10 +231,16 @@ VoxCPMError weight_load_tensor(const uint8_t* data, const WeightEntry* entry, Te
     int64_t n = 1;
     for (int i = 0; i < ndim; i++) {
         shape[i] = (int)entry->shape[i];
+        if (shape[i] < 0) return VOXCPM_ERR_INVALID_MODEL;
         n *= shape[i];
     }
     const size_t map = ql_map_size(data);
     if (map && entry->data_offset + entry->data_size > map) return VOXCPM_ERR_INVALID_MODEL;
+    /* the values this load reads must lie inside the entry (an ndim outside
+     * 1..4 is read as one dimension, as the engine reads it, while the index
+     * sized it from the stored ndim) */
+    int ok_dtype;
+    if (n < 0 || ql_bytes(entry->dtype, (uint64_t)n, &ok_dtype) > entry->data_size) return VOXCPM_ERR_INVALID_MODEL;
     const uint8_t* src = data + entry->data_offset;
     if (entry->dtype != QL_FP32 && entry->dtype != QL_BF16 && entry->dtype != QL_FP16 &&
         entry->dtype != QL_Q4_1 && entry->dtype != QL_Q8)
