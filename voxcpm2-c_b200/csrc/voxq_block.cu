@@ -42,6 +42,9 @@ constexpr int kMaxHeadDim = 256;
 
 // RMSNorm of one row per CTA: sum of squares in double (NaN counted as 0),
 // rms = sqrt(sum / D + eps) in double, out = (float)(x * (1 / rms)) * w.
+// The LocDiT and LocEnc paths normalise in place (out == x): every read of the
+// sum pass is done before the barriers that end the reduction, and in the
+// output pass each thread writes only the elements it reads itself.
 __global__ void __launch_bounds__(kBlockThreads) rmsnorm_kernel(const float* __restrict__ x,
                                                                 const float* __restrict__ w, float eps,
                                                                 float* __restrict__ out, int D) {
